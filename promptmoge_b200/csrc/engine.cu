@@ -1,0 +1,588 @@
+// The fused refiner plan: every buffer sized once, the whole K-step refinement enqueued as device work with no host
+// round trip, and captured into one CUDA graph.
+//
+// One refine step (the loop body of MoGeModel.forward, moge/model/v3.py:547-576, with the soft-gated LiDAR residual):
+//   fit      z = exp(logz), target = nearest LiDAR, trimmed LS (prompt_stem.py:211-240)       fit.cu
+//   prompt   residual/gate features (v3.py:376-383, 552-555), input_proj + prompt_proj        fit.cu, rowops.cu
+//   levels   voxelise + level-0 neighbour map, then per transition pool/dedup + neighbour map  structure.cu
+//   U-Net    Sparse3DUNet.forward (sparse_unet.py:176-258) with int8 layers                   spconv.cu, rowops.cu
+//   apply    logz += out_proj(x) (v3.py:358-359)                                              rowops.cu
+// Level sizes are only known on the device: every kernel reads its level's count from device memory and is launched
+// for the level's capacity.  A level that outgrows its capacity sets PMG_ERR_OVERFLOW in the plan's status word; the
+// host grows the capacities (pmg_refiner_set_capacity) and re-captures.
+#include <cuda_fp16.h>
+
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "rowops.cuh"
+
+namespace pmg {
+size_t fit_workspace_bytes(int B, int64_t N);
+int fit_solve(const float* z, const float* y, const uint8_t* flags, int B, int64_t N, int iters, float trim,
+              int min_points, pmg_fit_state* st, void* ws, cudaStream_t s);
+void* fit_clear_region(void* ws, int B, int64_t N, size_t* bytes);
+int fit_prep_prompt(const float* logz, int64_t stride, const float* lidar, const float* conf, int B, int H, int W,
+                    int h, int w, float* z, float* y, uint8_t* flags, cudaStream_t s);
+int prompt_feats(const float* logz, int64_t stride, const float* lidar, const float* conf, const pmg_fit_state* st,
+                 int B, int H, int W, int h, int w, int soft, float* out, cudaStream_t s);
+}  // namespace pmg
+
+using namespace pmg;
+
+namespace {
+
+struct QL {
+    const int8_t* w = nullptr;
+    const float* ws = nullptr;
+    const float* b = nullptr;
+    float sa = 0.f;
+    bool set = false;
+};
+struct NL {
+    const float* g = nullptr;
+    const float* b = nullptr;
+    bool set = false;
+};
+struct RB {
+    NL norm;
+    QL c1, c2;
+};
+struct PL {
+    const float* w = nullptr;
+    const float* b = nullptr;
+    bool set = false;
+};
+
+struct LevelBuf {
+    int H = 0, W = 0, C = 0;
+    int64_t cap = 0;
+    int32_t* z = nullptr;          // level >= 1 (level 0 uses zq)
+    int32_t* col = nullptr;        // level >= 1
+    int32_t* col_start = nullptr;  // level >= 1: [ncol + 1]
+    int32_t* nmap = nullptr;       // [27][cap]
+    uint32_t* mask = nullptr;      // [cap / 32 + 1]
+    float* X = nullptr;            // [cap][C] residual input / up-path sum
+    float* S = nullptr;            // [cap][C] skip / block output
+    int8_t* q1 = nullptr;          // [cap][C]
+    int8_t* q2 = nullptr;          // [cap][C]
+    // transition to the next level
+    int32_t* parent = nullptr;     // [cap]
+    int32_t* seg_idx = nullptr;    // [cap]
+    int32_t* seg_off = nullptr;    // [cap_next + 1]
+    int8_t* pq = nullptr;          // pooled + quantised [cap_next][C]
+    int8_t* uq = nullptr;          // this level's output quantised for the up projection [cap][C]
+    float* uc = nullptr;           // up projection at this level's rows, next-finer width [cap][C_finer]
+    void* pool_ws = nullptr;
+    size_t pool_ws_bytes = 0;
+};
+
+}  // namespace
+
+struct pmg_refiner {
+    pmg_refiner_config cfg{};
+    int L = 0;
+    int64_t N = 0;                 // B*H*W
+    std::vector<LevelBuf> lv;
+    RB down[8], bott, up[8];
+    QL pool[8], upl[8], enc, fuse0, fuse2;
+    PL in_proj, pr_proj, out_proj;
+    // state
+    float* pc = nullptr;           // [N][3] current point map
+    float* prompt = nullptr;       // [N][2]
+    float* fz = nullptr;           // fit z
+    float* fy = nullptr;           // fit target
+    uint8_t* fflags = nullptr;
+    pmg_fit_state* fst = nullptr;  // [B]
+    void* fit_ws = nullptr;
+    size_t fit_ws_bytes = 0;
+    int32_t* zq = nullptr;         // [N]
+    int32_t* zext = nullptr;       // [2B]: zmin[B], zmax[B]
+    int32_t* counts = nullptr;     // [L][2]
+    int32_t* status = nullptr;
+    float* delta = nullptr;        // [N]
+    // conditioning
+    int T = 0;                     // tokens per frame
+    int8_t* tok_q = nullptr;       // [B*T][enc]
+    float* uv_rows = nullptr;      // [B*T][C_last]
+    float* enc_tok = nullptr;      // [B*T][C_last]
+    int8_t* aq = nullptr;          // [cap_L][2 C_last]
+    int8_t* g8 = nullptr;          // [cap_L][C_last]
+    // inputs
+    const float* in_pc = nullptr;
+    const float* lidar = nullptr;
+    const float* conf = nullptr;
+    // graph
+    cudaStream_t cap_stream = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    std::vector<void*> allocs;
+    int launches = 0;
+};
+
+namespace {
+
+template <typename T>
+int alloc(pmg_refiner* r, T** p, size_t count) {
+    void* q = nullptr;
+    if (count == 0) count = 1;
+    PMG_CUDA_TRY(cudaMalloc(&q, count * sizeof(T)));
+    r->allocs.push_back(q);
+    *p = reinterpret_cast<T*>(q);
+    return PMG_OK;
+}
+
+#define PMG_TRY(expr)                 \
+    do {                              \
+        int rc_ = (expr);             \
+        if (rc_ != PMG_OK) return rc_; \
+    } while (0)
+
+void free_all(pmg_refiner* r) {
+    for (void* p : r->allocs) cudaFree(p);
+    r->allocs.clear();
+    if (r->exec) {
+        cudaGraphExecDestroy(r->exec);
+        r->exec = nullptr;
+    }
+}
+
+int allocate(pmg_refiner* r) {
+    const auto& c = r->cfg;
+    const int B = c.batch;
+    r->N = (int64_t)B * c.height * c.width;
+    r->L = c.levels;
+    r->lv.assign(r->L, LevelBuf());
+    for (int k = 0; k < r->L; ++k) {
+        LevelBuf& l = r->lv[k];
+        l.H = c.height >> k;
+        l.W = c.width >> k;
+        l.C = c.channels[k];
+        int64_t cap = c.capacity[k] > 0 ? c.capacity[k] : r->N;
+        if (k == 0) cap = r->N;
+        cap = ((cap + 127) / 128) * 128;
+        l.cap = cap;
+    }
+    for (int k = 0; k < r->L; ++k) {
+        LevelBuf& l = r->lv[k];
+        const int64_t cap = l.cap;
+        const int64_t ncol = (int64_t)B * l.H * l.W;
+        if (k > 0) {
+            PMG_TRY(alloc(r, &l.z, cap));
+            PMG_TRY(alloc(r, &l.col, cap));
+            PMG_TRY(alloc(r, &l.col_start, ncol + 1));
+        }
+        PMG_TRY(alloc(r, &l.nmap, 27 * cap));
+        PMG_TRY(alloc(r, &l.mask, cap / 32 + 2));
+        PMG_TRY(alloc(r, &l.X, cap * l.C));
+        PMG_TRY(alloc(r, &l.S, cap * l.C));
+        PMG_TRY(alloc(r, &l.q1, cap * l.C));
+        PMG_TRY(alloc(r, &l.q2, cap * l.C));
+        PMG_TRY(alloc(r, &l.uq, cap * l.C));
+        if (k > 0) PMG_TRY(alloc(r, &l.uc, cap * r->lv[k - 1].C));
+        if (k + 1 < r->L) {
+            const LevelBuf& n = r->lv[k + 1];
+            PMG_TRY(alloc(r, &l.parent, cap));
+            PMG_TRY(alloc(r, &l.seg_idx, cap));
+            PMG_TRY(alloc(r, &l.seg_off, n.cap + 1));
+            PMG_TRY(alloc(r, &l.pq, n.cap * l.C));
+            l.pool_ws_bytes = pmg_pool_frames_workspace_bytes(B, (l.H + 1) / 2, (l.W + 1) / 2);
+            PMG_TRY(alloc(r, reinterpret_cast<char**>(&l.pool_ws), l.pool_ws_bytes));
+        }
+    }
+    const LevelBuf& last = r->lv[r->L - 1];
+    PMG_TRY(alloc(r, &r->pc, r->N * 3));
+    PMG_TRY(alloc(r, &r->prompt, r->N * 2));
+    PMG_TRY(alloc(r, &r->fz, r->N));
+    PMG_TRY(alloc(r, &r->fy, r->N));
+    PMG_TRY(alloc(r, &r->fflags, r->N));
+    PMG_TRY(alloc(r, &r->fst, B));
+    r->fit_ws_bytes = fit_workspace_bytes(B, (int64_t)c.height * c.width);
+    PMG_TRY(alloc(r, reinterpret_cast<char**>(&r->fit_ws), r->fit_ws_bytes));
+    PMG_CUDA_TRY(cudaMemset(r->fit_ws, 0, r->fit_ws_bytes));
+    PMG_TRY(alloc(r, &r->zq, r->N));
+    PMG_TRY(alloc(r, &r->zext, 2 * B));
+    PMG_TRY(alloc(r, &r->counts, 2 * r->L));
+    PMG_TRY(alloc(r, &r->status, 1));
+    PMG_TRY(alloc(r, &r->delta, r->N));
+    r->T = last.H * last.W;
+    PMG_TRY(alloc(r, &r->tok_q, (size_t)B * r->T * c.enc_channels));
+    PMG_TRY(alloc(r, &r->uv_rows, (size_t)B * r->T * last.C));
+    PMG_TRY(alloc(r, &r->enc_tok, (size_t)B * r->T * last.C));
+    PMG_TRY(alloc(r, &r->aq, last.cap * 2 * last.C));
+    PMG_TRY(alloc(r, &r->g8, last.cap * last.C));
+    PMG_CUDA_TRY(cudaMemset(r->status, 0, sizeof(int32_t)));
+    std::vector<int32_t> cnt(2 * r->L, 0);
+    cnt[0] = (int32_t)r->N;
+    cnt[1] = (int32_t)r->N;
+    PMG_CUDA_TRY(cudaMemcpy(r->counts, cnt.data(), cnt.size() * sizeof(int32_t), cudaMemcpyHostToDevice));
+    return PMG_OK;
+}
+
+int parse_index(const std::string& s, size_t pos) {
+    int v = 0;
+    bool any = false;
+    while (pos < s.size() && s[pos] >= '0' && s[pos] <= '9') {
+        v = v * 10 + (s[pos] - '0');
+        ++pos;
+        any = true;
+    }
+    return any ? v : -1;
+}
+
+// "down_stages.3.0.conv1" -> block pointer and member; returns nullptr when unknown.
+RB* block_of(pmg_refiner* r, const std::string& n, std::string* member) {
+    auto take = [&](const char* prefix, RB* arr, int limit) -> RB* {
+        const size_t pl = std::strlen(prefix);
+        if (n.compare(0, pl, prefix) != 0) return nullptr;
+        const int idx = parse_index(n, pl);
+        if (idx < 0 || idx >= limit) return nullptr;
+        const std::string rest = n.substr(pl + std::to_string(idx).size());
+        if (rest.compare(0, 3, ".0.") != 0) return nullptr;
+        *member = rest.substr(3);
+        return &arr[idx];
+    };
+    if (RB* b = take("down_stages.", r->down, r->L)) return b;
+    if (RB* b = take("up_stages.", r->up, r->L - 1)) return b;
+    if (n.compare(0, 19, "bottleneck_stage.0.") == 0) {
+        *member = n.substr(19);
+        return &r->bott;
+    }
+    return nullptr;
+}
+
+QL* qlayer_of(pmg_refiner* r, const std::string& n) {
+    std::string member;
+    if (RB* b = block_of(r, n, &member)) {
+        if (member == "conv1") return &b->c1;
+        if (member == "conv2") return &b->c2;
+        return nullptr;
+    }
+    auto lin = [&](const char* prefix, QL* arr, int limit) -> QL* {
+        const size_t pl = std::strlen(prefix);
+        if (n.compare(0, pl, prefix) != 0) return nullptr;
+        const int idx = parse_index(n, pl);
+        if (idx < 0 || idx >= limit) return nullptr;
+        if (n.substr(pl + std::to_string(idx).size()) != ".linear") return nullptr;
+        return &arr[idx];
+    };
+    if (QL* q = lin("downsample_blocks.", r->pool, r->L - 1)) return q;
+    if (QL* q = lin("upsample_blocks.", r->upl, r->L - 1)) return q;
+    if (n == "encoder_fuse") return &r->enc;
+    if (n == "fuse_proj.0") return &r->fuse0;
+    if (n == "fuse_proj.2") return &r->fuse2;
+    return nullptr;
+}
+
+int check_weights(pmg_refiner* r) {
+    auto rb_ok = [](const RB& b) { return b.norm.set && b.c1.set && b.c2.set; };
+    for (int k = 0; k < r->L; ++k)
+        if (!rb_ok(r->down[k])) return PMG_ERR_BAD_ARG;
+    for (int i = 0; i + 1 < r->L; ++i)
+        if (!rb_ok(r->up[i]) || !r->pool[i].set || !r->upl[i].set) return PMG_ERR_BAD_ARG;
+    if (!rb_ok(r->bott) || !r->enc.set || !r->fuse0.set || !r->fuse2.set) return PMG_ERR_BAD_ARG;
+    if (!r->in_proj.set || !r->out_proj.set || (r->cfg.use_prompt && !r->pr_proj.set)) return PMG_ERR_BAD_ARG;
+    return PMG_OK;
+}
+
+#define LAUNCH(expr)        \
+    do {                    \
+        PMG_TRY(expr);      \
+        ++nl;               \
+    } while (0)
+
+int conv(const LevelBuf& l, const int8_t* in, const QL& q, int mode, float out_scale, const float* resid, void* out,
+         const int32_t* count, cudaStream_t s) {
+    Epi e{mode, q.sa, out_scale, q.ws, q.b, resid, out};
+    return gemm_i8(in, l.nmap, l.cap, l.mask, count, l.cap, l.C, l.C, 27, q.w, e, s);
+}
+
+int dense(const int8_t* a, const int32_t* count, int64_t rows, int K, int N, const QL& q, int mode, float out_scale,
+          const float* resid, void* out, cudaStream_t s) {
+    Epi e{mode, q.sa, out_scale, q.ws, q.b, resid, out};
+    return gemm_i8(a, nullptr, 0, nullptr, count, rows, K, N, 1, q.w, e, s);
+}
+
+// Residual block at level k: X -> S  (S = conv2(silu(conv1(silu(LN(X))))) + X).  When `up` is given, X is first
+// formed as up.uc[parent] + S (the skip) -- NearestUp + skip add -- and written to X.
+int resblock(pmg_refiner* r, int k, const RB& b, const float* up_src, const int32_t* parent, cudaStream_t s, int& nl) {
+    LevelBuf& l = r->lv[k];
+    const int32_t* cnt = r->counts + 2 * k;
+    LAUNCH(ln_silu_q8(l.X, up_src, parent, l.S, l.X, cnt, l.cap, l.C, b.norm.g, b.norm.b, 1e-6, b.c1.sa, l.q1, s));
+    LAUNCH(conv(l, l.q1, b.c1, PMG_EPI_SILU_Q8, b.c2.sa, nullptr, l.q2, cnt, s));
+    LAUNCH(conv(l, l.q2, b.c2, PMG_EPI_F32_RESID, 0.f, l.X, l.S, cnt, s));
+    return PMG_OK;
+}
+
+int enqueue_step(pmg_refiner* r, cudaStream_t s) {
+    const auto& c = r->cfg;
+    const int B = c.batch, H = c.height, W = c.width, L = r->L;
+    int nl = 0;
+    // --- per-step LiDAR fit + prompt features (v3.py:552-555) --------------------------------------------------- //
+    if (c.use_prompt) {
+        LAUNCH(fit_prep_prompt(r->pc + 2, 3, r->lidar, r->conf, B, H, W, c.lidar_h, c.lidar_w, r->fz, r->fy,
+                               r->fflags, s));
+        size_t nclr = 0;
+        void* clr = fit_clear_region(r->fit_ws, B, (int64_t)H * W, &nclr);
+        PMG_CUDA_TRY(cudaMemsetAsync(clr, 0, nclr, s));
+        PMG_TRY(fit_solve(r->fz, r->fy, r->fflags, B, (int64_t)H * W, c.fit_iters, c.fit_trim, c.fit_min_points,
+                          r->fst, r->fit_ws, s));
+        nl += 4 * c.fit_iters + 1;
+        LAUNCH(prompt_feats(r->pc + 2, 3, r->lidar, r->conf, r->fst, B, H, W, c.lidar_h, c.lidar_w, c.soft_gate,
+                            r->prompt, s));
+    }
+    // --- structure ------------------------------------------------------------------------------------------------ //
+    PMG_CUDA_TRY(cudaMemsetAsync(r->zext, 0x7f, B * sizeof(int32_t), s));
+    PMG_CUDA_TRY(cudaMemsetAsync(r->zext + B, 0x80, B * sizeof(int32_t), s));
+    LevelBuf& l0 = r->lv[0];
+    LAUNCH(pmg_voxelize_l0(r->pc, B, H, W, c.depth_resolution, r->zq, r->zext, r->zext + B, l0.nmap, l0.cap, l0.mask,
+                           s));
+    for (int k = 0; k + 1 < L; ++k) {
+        LevelBuf& f = r->lv[k];
+        LevelBuf& n = r->lv[k + 1];
+        PMG_TRY(pmg_pool_frames(B, f.H, f.W, r->counts + 2 * k, k == 0 ? nullptr : f.col_start, k == 0 ? r->zq : f.z,
+                                k == 0 ? r->zext : nullptr, r->counts + 2 * (k + 1), n.z, n.col, n.col_start, nullptr,
+                                n.cap, f.parent, f.seg_idx, f.seg_off, f.pool_ws, f.pool_ws_bytes, r->status, s));
+        nl += 3;
+        LAUNCH(pmg_nmap_frames(B, n.H, n.W, r->counts + 2 * (k + 1), n.z, n.col, n.col_start, n.nmap, n.cap, n.mask,
+                               s));
+    }
+    // --- U-Net ---------------------------------------------------------------------------------------------------- //
+    LAUNCH(input_proj(r->pc, c.use_prompt ? r->prompt : nullptr, r->N, l0.C, r->in_proj.w, r->in_proj.b,
+                      r->pr_proj.w, r->pr_proj.b, l0.X, s));
+    for (int k = 0; k < L; ++k) {
+        PMG_TRY(resblock(r, k, r->down[k], nullptr, nullptr, s, nl));
+        if (k + 1 < L) {
+            LevelBuf& f = r->lv[k];
+            LevelBuf& n = r->lv[k + 1];
+            const int32_t* ncnt = r->counts + 2 * (k + 1);
+            LAUNCH(pool_mean(f.S, f.seg_idx, f.seg_off, ncnt, n.cap, f.C, r->pool[k].sa, f.pq, nullptr, s));
+            LAUNCH(dense(f.pq, ncnt, n.cap, f.C, n.C, r->pool[k], PMG_EPI_F32, 0.f, nullptr, n.X, s));
+        }
+    }
+    {
+        LevelBuf& l = r->lv[L - 1];
+        const int32_t* cnt = r->counts + 2 * (L - 1);
+        LAUNCH(concat_q8(l.S, r->enc_tok, l.col ? l.col : nullptr, cnt, l.cap, l.C, r->fuse0.sa, r->aq, s));
+        LAUNCH(dense(r->aq, cnt, l.cap, 2 * l.C, l.C, r->fuse0, PMG_EPI_SILU_Q8, r->fuse2.sa, nullptr, r->g8, s));
+        LAUNCH(dense(r->g8, cnt, l.cap, l.C, l.C, r->fuse2, PMG_EPI_F32, 0.f, nullptr, l.X, s));
+        PMG_TRY(resblock(r, L - 1, r->bott, nullptr, nullptr, s, nl));
+    }
+    for (int i = 0; i + 1 < L; ++i) {
+        const int src = L - 1 - i, t = src - 1;
+        LevelBuf& ls = r->lv[src];
+        LevelBuf& lt = r->lv[t];
+        const int32_t* scnt = r->counts + 2 * src;
+        LAUNCH(quantize(ls.S, ls.cap * ls.C, r->upl[i].sa, ls.uq, s));
+        LAUNCH(dense(ls.uq, scnt, ls.cap, ls.C, lt.C, r->upl[i], PMG_EPI_F32, 0.f, nullptr, ls.uc, s));
+        PMG_TRY(resblock(r, t, r->up[i], ls.uc, lt.parent, s, nl));
+    }
+    LAUNCH(out_apply(l0.S, r->N, l0.C, r->out_proj.w, r->out_proj.b, r->pc, r->pc, r->delta, s));
+    r->launches = nl;
+    return PMG_OK;
+}
+
+int enqueue_run(pmg_refiner* r, int K, float* pc_out, pmg_fit_state* fit_out, cudaStream_t s) {
+    if (!r->in_pc || (r->cfg.use_prompt && (!r->lidar || !r->conf))) return PMG_ERR_BAD_ARG;
+    PMG_TRY(check_weights(r));
+    PMG_CUDA_TRY(cudaMemcpyAsync(r->pc, r->in_pc, r->N * 3 * sizeof(float), cudaMemcpyDeviceToDevice, s));
+    for (int k = 0; k < K; ++k) PMG_TRY(enqueue_step(r, s));
+    if (pc_out) PMG_CUDA_TRY(cudaMemcpyAsync(pc_out, r->pc, r->N * 3 * sizeof(float), cudaMemcpyDeviceToDevice, s));
+    if (fit_out && r->cfg.use_prompt)
+        PMG_CUDA_TRY(cudaMemcpyAsync(fit_out, r->fst, r->cfg.batch * sizeof(pmg_fit_state), cudaMemcpyDeviceToDevice, s));
+    return PMG_OK;
+}
+
+}  // namespace
+
+extern "C" int pmg_refiner_create(const pmg_refiner_config* cfg, pmg_refiner** out) {
+    if (!cfg || !out) return PMG_ERR_BAD_ARG;
+    const int L = cfg->levels;
+    if (cfg->batch <= 0 || L < 2 || L > 8 || cfg->height <= 0 || cfg->width <= 0) return PMG_ERR_BAD_ARG;
+    if ((cfg->height % (1 << (L - 1))) || (cfg->width % (1 << (L - 1)))) return PMG_ERR_BAD_ARG;
+    for (int k = 0; k < L; ++k)
+        if (cfg->channels[k] <= 0 || cfg->channels[k] % 16 || cfg->channels[k] > 256) return PMG_ERR_UNSUPPORTED;
+    if (cfg->enc_channels % 64) return PMG_ERR_UNSUPPORTED;
+    auto* r = new pmg_refiner();
+    r->cfg = *cfg;
+    int rc = allocate(r);
+    if (rc == PMG_OK) {
+        cudaError_t e = cudaStreamCreateWithFlags(&r->cap_stream, cudaStreamNonBlocking);
+        if (e != cudaSuccess) {
+            set_cuda_error(e);
+            rc = PMG_ERR_CUDA;
+        }
+    }
+    if (rc != PMG_OK) {
+        free_all(r);
+        delete r;
+        return rc;
+    }
+    *out = r;
+    return PMG_OK;
+}
+
+extern "C" void pmg_refiner_destroy(pmg_refiner* r) {
+    if (!r) return;
+    cudaDeviceSynchronize();
+    free_all(r);
+    if (r->cap_stream) cudaStreamDestroy(r->cap_stream);
+    delete r;
+}
+
+extern "C" int pmg_refiner_set_qlayer(pmg_refiner* r, const char* name, const int8_t* weight, const float* w_scale,
+                                      const float* bias, float act_scale) {
+    if (!r || !name || !weight || !w_scale || !bias || !(act_scale > 0.f)) return PMG_ERR_BAD_ARG;
+    QL* q = qlayer_of(r, name);
+    if (!q) return PMG_ERR_BAD_ARG;
+    q->w = weight;
+    q->ws = w_scale;
+    q->b = bias;
+    q->sa = act_scale;
+    q->set = true;
+    return PMG_OK;
+}
+
+extern "C" int pmg_refiner_set_norm(pmg_refiner* r, const char* name, const float* gamma, const float* beta) {
+    if (!r || !name || !gamma || !beta) return PMG_ERR_BAD_ARG;
+    std::string member;
+    RB* b = block_of(r, name, &member);
+    if (!b || member != "norm1") return PMG_ERR_BAD_ARG;
+    b->norm.g = gamma;
+    b->norm.b = beta;
+    b->norm.set = true;
+    return PMG_OK;
+}
+
+extern "C" int pmg_refiner_set_proj(pmg_refiner* r, const char* name, const float* weight, const float* bias) {
+    if (!r || !name || !weight || !bias) return PMG_ERR_BAD_ARG;
+    const std::string n(name);
+    PL* p = n == "input_proj" ? &r->in_proj : n == "prompt_proj" ? &r->pr_proj : n == "out_proj" ? &r->out_proj : nullptr;
+    if (!p) return PMG_ERR_BAD_ARG;
+    p->w = weight;
+    p->b = bias;
+    p->set = true;
+    return PMG_OK;
+}
+
+extern "C" int pmg_refiner_set_frame(pmg_refiner* r, const uint16_t* enc_f16, const float* uv_bias, void* stream) {
+    if (!r || !enc_f16 || !r->enc.set) return PMG_ERR_BAD_ARG;
+    cudaStream_t s = as_stream(stream);
+    const int B = r->cfg.batch, K = r->cfg.enc_channels, C = r->lv[r->L - 1].C;
+    PMG_TRY(tokens_q8(enc_f16, B, K, r->T, r->enc.sa, r->tok_q, s));
+    if (uv_bias) PMG_TRY(planar_to_rows(uv_bias, B, C, r->T, r->uv_rows, s));
+    Epi e{uv_bias ? PMG_EPI_F32_RESID : PMG_EPI_F32, r->enc.sa, 0.f, r->enc.ws, r->enc.b, uv_bias ? r->uv_rows : nullptr,
+          r->enc_tok};
+    return gemm_i8(r->tok_q, nullptr, 0, nullptr, nullptr, (int64_t)B * r->T, K, C, 1, r->enc.w, e, s);
+}
+
+extern "C" int pmg_refiner_set_inputs(pmg_refiner* r, const float* point_coord, const float* lidar_depth,
+                                      const float* lidar_conf) {
+    if (!r || !point_coord) return PMG_ERR_BAD_ARG;
+    r->in_pc = point_coord;
+    r->lidar = lidar_depth;
+    r->conf = lidar_conf;
+    return PMG_OK;
+}
+
+extern "C" int pmg_refiner_enqueue(pmg_refiner* r, int32_t K, float* point_coord_out, pmg_fit_state* fit_out,
+                                   void* stream) {
+    if (!r || K < 0) return PMG_ERR_BAD_ARG;
+    return enqueue_run(r, K, point_coord_out, fit_out, as_stream(stream));
+}
+
+extern "C" int pmg_refiner_capture(pmg_refiner* r, int32_t K, float* point_coord_out, pmg_fit_state* fit_out,
+                                   void* stream) {
+    (void)stream;
+    if (!r || K < 0) return PMG_ERR_BAD_ARG;
+    if (r->exec) {
+        cudaGraphExecDestroy(r->exec);
+        r->exec = nullptr;
+    }
+    cudaStream_t s = r->cap_stream;
+    PMG_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    const int rc = enqueue_run(r, K, point_coord_out, fit_out, s);
+    cudaGraph_t g = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(s, &g);
+    if (rc != PMG_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    PMG_CUDA_TRY(e);
+    const cudaError_t ie = cudaGraphInstantiate(&r->exec, g, 0);
+    cudaGraphDestroy(g);
+    PMG_CUDA_TRY(ie);
+    return PMG_OK;
+}
+
+extern "C" int pmg_refiner_launch(pmg_refiner* r, void* stream) {
+    if (!r || !r->exec) return PMG_ERR_BAD_ARG;
+    PMG_CUDA_TRY(cudaGraphLaunch(r->exec, as_stream(stream)));
+    return PMG_OK;
+}
+
+extern "C" int pmg_refiner_status(pmg_refiner* r, int32_t* counts_host, int32_t clear, void* stream) {
+    if (!r) return PMG_ERR_BAD_ARG;
+    cudaStream_t s = as_stream(stream);
+    PMG_CUDA_TRY(cudaStreamSynchronize(s));
+    int32_t st = 0;
+    PMG_CUDA_TRY(cudaMemcpy(&st, r->status, sizeof(int32_t), cudaMemcpyDeviceToHost));
+    if (counts_host) {
+        std::vector<int32_t> c(2 * r->L);
+        PMG_CUDA_TRY(cudaMemcpy(c.data(), r->counts, c.size() * sizeof(int32_t), cudaMemcpyDeviceToHost));
+        for (int k = 0; k < r->L; ++k) counts_host[k] = c[2 * k + 1];
+    }
+    if (clear) PMG_CUDA_TRY(cudaMemset(r->status, 0, sizeof(int32_t)));
+    return st;
+}
+
+extern "C" int pmg_refiner_set_capacity(pmg_refiner* r, const int64_t* capacity) {
+    if (!r || !capacity) return PMG_ERR_BAD_ARG;
+    PMG_CUDA_TRY(cudaDeviceSynchronize());
+    free_all(r);
+    for (int k = 0; k < r->L; ++k) r->cfg.capacity[k] = capacity[k];
+    return allocate(r);
+}
+
+extern "C" int pmg_refiner_launches_per_step(const pmg_refiner* r) { return r ? r->launches : 0; }
+
+extern "C" int pmg_refiner_level_info(pmg_refiner* r, int32_t level, int64_t* cap, int32_t* H, int32_t* W,
+                                      int32_t* C) {
+    if (!r || level < 0 || level >= r->L) return PMG_ERR_BAD_ARG;
+    const LevelBuf& l = r->lv[level];
+    if (cap) *cap = l.cap;
+    if (H) *H = l.H;
+    if (W) *W = l.W;
+    if (C) *C = l.C;
+    return PMG_OK;
+}
+
+extern "C" void* pmg_refiner_debug_ptr(pmg_refiner* r, const char* what, int32_t level) {
+    if (!r || !what) return nullptr;
+    const std::string w(what);
+    if (w == "zq") return r->zq;
+    if (w == "zext") return r->zext;
+    if (w == "counts") return r->counts;
+    if (w == "pc") return r->pc;
+    if (w == "delta") return r->delta;
+    if (w == "prompt") return r->prompt;
+    if (w == "fit") return r->fst;
+    if (w == "enc_tok") return r->enc_tok;
+    if (level < 0 || level >= r->L) return nullptr;
+    LevelBuf& l = r->lv[level];
+    if (w == "z") return l.z;
+    if (w == "col") return l.col;
+    if (w == "col_start") return l.col_start;
+    if (w == "nmap") return l.nmap;
+    if (w == "tile_mask") return l.mask;
+    if (w == "parent") return l.parent;
+    if (w == "seg_indices") return l.seg_idx;
+    if (w == "seg_offsets") return l.seg_off;
+    if (w == "X") return l.X;
+    if (w == "S") return l.S;
+    if (w == "q1") return l.q1;
+    if (w == "q2") return l.q2;
+    return nullptr;
+}

@@ -1,0 +1,391 @@
+// Robust metric fit: batched trimmed least squares  target ~= s * z + t  (prompt_stem.py:211-240), the LiDAR prompt
+// features that consume it (v3.py:362-383) and the final 'lidar_ls' fit's preparation (v3.py:768-777).
+//
+// Every step runs on the device with its state in a small per-frame struct, so neither the per-step fit inside the
+// refine loop nor the final fit needs a host round trip:
+//   * sums:  each CTA reduces n, Sx, Sy, Sxx, Sxy over its slice in fp64 (warp shuffles, then shared memory); the last
+//            CTA to finish (threadfence + arrival counter) adds the per-CTA partials in a fixed order, rounds them to
+//            fp32 and solves the 2x2 system with the reference's fp32 formula;
+//   * trim:  the k-th smallest relative residual r = |s z + t - y| / max(y, 1e-3), the exact value torch.kthvalue
+//            returns, by a three-pass radix select on the fp32 bit pattern (r >= 0, so bit order = value order):
+//            11 + 11 + 10 bits, each pass a shared-memory histogram of the elements that still match the prefix,
+//            the last CTA picking the digit.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+
+namespace pmg {
+
+constexpr int kFitThreads = 256;
+constexpr int kBins = 2048;
+
+__device__ __forceinline__ int nearest_src(int dst, int out, int in, float scale) {
+    // aten nearest_idx (UpSample.h): identity, >> 1 for exact 2x, else min(floor(dst * (float)in/out), in - 1)
+    if (out == in) return dst;
+    if (out == 2 * in) return dst >> 1;
+    return min((int)floorf(__fmul_rn((float)dst, scale)), in - 1);
+}
+
+__global__ void k_fit_prep_prompt(const float* __restrict__ logz, int64_t stride, const float* __restrict__ lidar,
+                                  const float* __restrict__ conf, int B, int H, int W, int h, int w, float sy, float sx,
+                                  float* __restrict__ z, float* __restrict__ target, uint8_t* __restrict__ flags) {
+    const int64_t N = (int64_t)B * H * W;
+    for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < N; m += (int64_t)gridDim.x * blockDim.x) {
+        const int b = (int)(m / ((int64_t)H * W));
+        const int rem = (int)(m - (int64_t)b * H * W);
+        const int i = rem / W, j = rem - (rem / W) * W;
+        const int li = nearest_src(i, H, h, sy), lj = nearest_src(j, W, w, sx);
+        const int64_t l = ((int64_t)b * h + li) * w + lj;
+        const float d = lidar[l];
+        const float c = fminf(fmaxf(__fdiv_rn(conf[l], 2.0f), 0.0f), 1.0f);
+        const bool valid = isfinite(d) && d > 0.0f;
+        const bool msk = valid && c >= 0.999f;
+        z[m] = expf(logz[m * stride]);
+        target[m] = d;
+        flags[m] = (uint8_t)((valid ? 1 : 0) | (msk ? 2 : 0));
+    }
+}
+
+// Area resize (adaptive average pool) of depth and of the optional model mask to the LiDAR grid, sum in input
+// order, divided by the window height then width (aten cpu_adaptive_avg_pool); then the final fit's mask.
+__global__ void k_fit_prep_final(const float* __restrict__ depth, const float* __restrict__ mask01,
+                                 const float* __restrict__ lidar, const float* __restrict__ conf, int B, int H, int W,
+                                 int h, int w, float* __restrict__ z, float* __restrict__ target,
+                                 uint8_t* __restrict__ flags) {
+    const int64_t N = (int64_t)B * h * w;
+    for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < N; p += (int64_t)gridDim.x * blockDim.x) {
+        const int b = (int)(p / ((int64_t)h * w));
+        const int rem = (int)(p - (int64_t)b * h * w);
+        const int oh = rem / w, ow = rem - (rem / w) * w;
+        const int h0 = (int)(((int64_t)oh * H) / h), h1 = (int)(((int64_t)(oh + 1) * H + h - 1) / h);
+        const int w0 = (int)(((int64_t)ow * W) / w), w1 = (int)(((int64_t)(ow + 1) * W + w - 1) / w);
+        const float* src = depth + (int64_t)b * H * W;
+        float acc = 0.f, macc = 0.f;
+        for (int ih = h0; ih < h1; ++ih)
+            for (int iw = w0; iw < w1; ++iw) {
+                acc = __fadd_rn(acc, src[(int64_t)ih * W + iw]);
+                if (mask01) macc = __fadd_rn(macc, mask01[(int64_t)b * H * W + (int64_t)ih * W + iw]);
+            }
+        const float kh = (float)(h1 - h0), kw = (float)(w1 - w0);
+        const float zl = __fdiv_rn(__fdiv_rn(acc, kh), kw);
+        const float d = lidar[p];
+        bool ok = conf[p] >= 2.0f && d > 0.0f && zl > 0.0f;
+        if (mask01) ok = ok && __fdiv_rn(__fdiv_rn(macc, kh), kw) > 0.99f;
+        z[p] = zl;
+        target[p] = d;
+        flags[p] = (uint8_t)((isfinite(d) && d > 0.0f ? 1 : 0) | (ok ? 2 : 0));
+    }
+}
+
+__device__ __forceinline__ float rel_resid(float s, float t, float z, float y) {
+    // |(s * z + t) - y| / max(y, 1e-3), each operation rounded (prompt_stem.py:235)
+    return __fdiv_rn(fabsf(__fsub_rn(__fadd_rn(__fmul_rn(s, z), t), y)), fmaxf(y, 1e-3f));
+}
+
+struct FitArgs {
+    const float* z;
+    const float* y;
+    const uint8_t* flags;
+    int64_t N;
+    int nblk;
+    float keep;        // fp32(1 - trim)
+    int min_points;
+    pmg_fit_state* st;
+    double* partials;  // [B][nblk][5]
+    uint32_t* hist;    // [B][kBins]
+    uint32_t* arrive;  // [B]
+};
+
+// Sums over the current weights (iteration 0: the mask; later: mask & r <= thr with the state's s, t), then the
+// last CTA of the frame solves.  gridDim = (nblk, B).
+__global__ void __launch_bounds__(kFitThreads) k_fit_sums(FitArgs a, int iter) {
+    const int b = blockIdx.y;
+    pmg_fit_state* st = a.st + b;
+    const float* z = a.z + (int64_t)b * a.N;
+    const float* y = a.y + (int64_t)b * a.N;
+    const uint8_t* fl = a.flags + (int64_t)b * a.N;
+    const float s0 = st->s, t0 = st->t, thr = st->thr;
+    double acc[5] = {0, 0, 0, 0, 0};
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.N; i += (int64_t)a.nblk * blockDim.x) {
+        if (!(fl[i] & 2)) continue;
+        const float zi = z[i], yi = y[i];
+        if (iter > 0 && !(rel_resid(s0, t0, zi, yi) <= thr)) continue;
+        acc[0] += 1.0;
+        acc[1] += (double)zi;
+        acc[2] += (double)yi;
+        acc[3] += (double)__fmul_rn(zi, zi);
+        acc[4] += (double)__fmul_rn(zi, yi);
+    }
+    __shared__ double red[kFitThreads / 32][5];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+    for (int q = 0; q < 5; ++q) acc[q] = warp_sum(acc[q]);
+    if (lane == 0)
+#pragma unroll
+        for (int q = 0; q < 5; ++q) red[wid][q] = acc[q];
+    __syncthreads();
+    __shared__ bool last;
+    if (threadIdx.x == 0) {
+        double* part = a.partials + ((int64_t)b * a.nblk + blockIdx.x) * 5;
+        for (int q = 0; q < 5; ++q) {
+            double v = 0;
+            for (int w8 = 0; w8 < kFitThreads / 32; ++w8) v += red[w8][q];
+            part[q] = v;
+        }
+        __threadfence();
+        last = atomicAdd(&a.arrive[b], 1u) == (unsigned)a.nblk - 1;
+    }
+    __syncthreads();
+    if (!last || threadIdx.x != 0) return;
+    __threadfence();
+    double tot[5] = {0, 0, 0, 0, 0};
+    const volatile double* part = a.partials + (int64_t)b * a.nblk * 5;
+    for (int k = 0; k < a.nblk; ++k)
+        for (int q = 0; q < 5; ++q) tot[q] += part[k * 5 + q];
+    a.arrive[b] = 0;
+    if (iter == 0) {
+        const int count = (int)tot[0];
+        st->count = count;
+        st->ok = count >= a.min_points ? 1 : 0;
+        int k = (int)__fmul_rn(a.keep, (float)count);
+        k = max(k, a.min_points);
+        st->k = (int)min((int64_t)k, a.N);
+        st->s = 1.0f;
+        st->t = 0.0f;
+    }
+    for (int q = 0; q < 5; ++q) st->sums[q] = tot[q];
+    const float n = fmaxf((float)tot[0], 1.0f);
+    const float sx = (float)tot[1], sy = (float)tot[2], sxx = (float)tot[3], sxy = (float)tot[4];
+    const float den = __fsub_rn(__fmul_rn(n, sxx), __fmul_rn(sx, sx));
+    const float s_new = den > 1e-12f ? __fdiv_rn(__fsub_rn(__fmul_rn(n, sxy), __fmul_rn(sx, sy)), fmaxf(den, 1e-12f)) : 1.0f;
+    const float t_new = __fdiv_rn(__fsub_rn(sy, __fmul_rn(s_new, sx)), n);
+    if (st->ok) {
+        st->s = s_new;
+        st->t = t_new;
+    }
+    st->prefix = 0;
+    st->remaining = st->k;
+}
+
+// One radix pass of the k-th smallest r over the masked points.  pass 0: bits 31..21, 1: 20..10, 2: 9..0.
+__global__ void __launch_bounds__(kFitThreads) k_fit_select(FitArgs a, int pass) {
+    const int b = blockIdx.y;
+    pmg_fit_state* st = a.st + b;
+    if (st->k > st->count) {          // the k-th value is one of the +inf fill values: thr = inf (w = mask)
+        if (pass == 2 && blockIdx.x == 0 && threadIdx.x == 0) st->thr = __int_as_float(0x7f800000);
+        return;
+    }
+    const int shift = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
+    const int nbits = pass == 2 ? 10 : 11;
+    const uint32_t prefix = st->prefix;
+    const float s0 = st->s, t0 = st->t;
+    __shared__ uint32_t h[kBins];
+    for (int i = threadIdx.x; i < kBins; i += blockDim.x) h[i] = 0;
+    __syncthreads();
+    const float* z = a.z + (int64_t)b * a.N;
+    const float* y = a.y + (int64_t)b * a.N;
+    const uint8_t* fl = a.flags + (int64_t)b * a.N;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.N; i += (int64_t)a.nblk * blockDim.x) {
+        if (!(fl[i] & 2)) continue;
+        const uint32_t bits = __float_as_uint(rel_resid(s0, t0, z[i], y[i]));
+        const uint32_t hi = (pass == 0) ? 0u : (bits >> (shift + nbits));
+        if (hi != prefix) continue;
+        atomicAdd(&h[(bits >> shift) & ((1u << nbits) - 1)], 1u);
+    }
+    __syncthreads();
+    uint32_t* gh = a.hist + (int64_t)b * kBins;
+    for (int i = threadIdx.x; i < (1 << nbits); i += blockDim.x)
+        if (h[i]) atomicAdd(&gh[i], h[i]);
+    __shared__ bool last;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(&a.arrive[b], 1u) == (unsigned)a.nblk - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    // Last CTA: find the digit holding the `remaining`-th value (block-wide scan over the bins).
+    __shared__ int sm[33];
+    __shared__ uint32_t found_digit, found_before;
+    const int nb = 1 << nbits;
+    const int per = nb / kFitThreads;   // 8 or 4 bins per thread
+    uint32_t local[8];
+    uint32_t sum = 0;
+    volatile uint32_t* vgh = gh;
+    for (int q = 0; q < per; ++q) {
+        local[q] = vgh[threadIdx.x * per + q];
+        sum += local[q];
+    }
+    int total;
+    const uint32_t before = (uint32_t)block_exclusive_scan((int)sum, sm, &total);
+    const uint32_t rem = (uint32_t)st->remaining;
+    if (before < rem && before + sum >= rem) {
+        uint32_t run = before;
+        for (int q = 0; q < per; ++q) {
+            if (run + local[q] >= rem) {
+                found_digit = threadIdx.x * per + q;
+                found_before = run;
+                break;
+            }
+            run += local[q];
+        }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < nb; i += blockDim.x) gh[i] = 0;
+    if (threadIdx.x == 0) {
+        a.arrive[b] = 0;
+        const uint32_t np = (prefix << nbits) | found_digit;
+        st->prefix = np;
+        st->remaining = (int)(rem - found_before);
+        if (pass == 2) st->thr = __uint_as_float(np);
+    }
+}
+
+__global__ void k_prompt_feats(const float* __restrict__ logz, int64_t stride, const float* __restrict__ lidar,
+                               const float* __restrict__ conf, const pmg_fit_state* __restrict__ st, int B, int H,
+                               int W, int h, int w, float sy, float sx, int soft, float* __restrict__ out) {
+    const int64_t N = (int64_t)B * H * W;
+    for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < N; m += (int64_t)gridDim.x * blockDim.x) {
+        const int b = (int)(m / ((int64_t)H * W));
+        const int rem = (int)(m - (int64_t)b * H * W);
+        const int i = rem / W, j = rem - (rem / W) * W;
+        const int li = nearest_src(i, H, h, sy), lj = nearest_src(j, W, w, sx);
+        const int64_t l = ((int64_t)b * h + li) * w + lj;
+        const float d = lidar[l];
+        const float c = fminf(fmaxf(__fdiv_rn(conf[l], 2.0f), 0.0f), 1.0f);
+        const bool valid = isfinite(d) && d > 0.0f;
+        const float s = st[b].s, t = st[b].t;
+        const float d_aff = __fdiv_rn(__fsub_rn(d, t), fmaxf(s, 1e-6f));
+        const bool ok = valid && d_aff > 1e-4f;
+        const float lz = logz[m * stride];
+        const float log_d_aff = ok ? logf(fmaxf(d_aff, 1e-4f)) : lz;
+        const float okf = ok ? 1.0f : 0.0f;
+        const float gate = soft ? __fmul_rn(__fadd_rn(0.15f, __fmul_rn(0.85f, c)), okf) : __fmul_rn(c, okf);
+        out[m * 2] = __fmul_rn(__fsub_rn(log_d_aff, lz), gate);
+        out[m * 2 + 1] = gate;
+    }
+}
+
+__global__ void k_apply_affine(float* __restrict__ depth, const pmg_fit_state* __restrict__ st, int B, int64_t N) {
+    const int64_t total = (int64_t)B * N;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+        const int b = (int)(e / N);
+        depth[e] = __fadd_rn(__fmul_rn(st[b].s, depth[e]), st[b].t);
+    }
+}
+
+static int grid_for(int64_t work) {
+    return (int)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, (int64_t)kNumSMs * 16));
+}
+
+static int fit_nblk(int64_t N) { return (int)std::max<int64_t>(1, std::min<int64_t>((N + 4095) / 4096, kNumSMs)); }
+
+size_t fit_workspace_bytes(int B, int64_t N) {
+    const int nblk = fit_nblk(N);
+    return (size_t)B * nblk * 5 * sizeof(double) + (size_t)B * kBins * sizeof(uint32_t) + (size_t)B * sizeof(uint32_t) + 256;
+}
+
+// Prompt-fit inputs are prepared by k_fit_prep_prompt; the workspace must be zeroed once before first use (the
+// kernels leave their counters and histograms zeroed for the next call).
+int fit_solve(const float* z, const float* y, const uint8_t* flags, int B, int64_t N, int iters, float trim,
+              int min_points, pmg_fit_state* st, void* ws, cudaStream_t s) {
+    FitArgs a;
+    a.z = z;
+    a.y = y;
+    a.flags = flags;
+    a.N = N;
+    a.nblk = fit_nblk(N);
+    a.keep = (float)(1.0 - (double)trim);
+    a.min_points = min_points;
+    a.st = st;
+    a.partials = reinterpret_cast<double*>(ws);
+    a.hist = reinterpret_cast<uint32_t*>(a.partials + (size_t)B * a.nblk * 5);
+    a.arrive = a.hist + (size_t)B * kBins;
+    const dim3 grid(a.nblk, B);
+    for (int it = 0; it <= iters; ++it) {
+        k_fit_sums<<<grid, kFitThreads, 0, s>>>(a, it);
+        PMG_LAUNCH_CHECK();
+        if (it == iters) break;
+        for (int pass = 0; pass < 3; ++pass) {
+            k_fit_select<<<grid, kFitThreads, 0, s>>>(a, pass);
+            PMG_LAUNCH_CHECK();
+        }
+    }
+    return PMG_OK;
+}
+
+void* fit_clear_region(void* ws, int B, int64_t N, size_t* bytes) {
+    const int nblk = fit_nblk(N);
+    char* p = reinterpret_cast<char*>(ws) + (size_t)B * nblk * 5 * sizeof(double);
+    *bytes = (size_t)B * kBins * sizeof(uint32_t) + (size_t)B * sizeof(uint32_t);
+    return p;
+}
+
+int fit_prep_prompt(const float* logz, int64_t stride, const float* lidar, const float* conf, int B, int H, int W,
+                    int h, int w, float* z, float* y, uint8_t* flags, cudaStream_t s) {
+    const float sy = (float)h / (float)H, sx = (float)w / (float)W;
+    k_fit_prep_prompt<<<grid_for((int64_t)B * H * W), 256, 0, s>>>(logz, stride, lidar, conf, B, H, W, h, w, sy, sx, z,
+                                                                   y, flags);
+    PMG_LAUNCH_CHECK();
+    return PMG_OK;
+}
+
+int prompt_feats(const float* logz, int64_t stride, const float* lidar, const float* conf, const pmg_fit_state* st,
+                 int B, int H, int W, int h, int w, int soft, float* out, cudaStream_t s) {
+    const float sy = (float)h / (float)H, sx = (float)w / (float)W;
+    k_prompt_feats<<<grid_for((int64_t)B * H * W), 256, 0, s>>>(logz, stride, lidar, conf, st, B, H, W, h, w, sy, sx,
+                                                                soft, out);
+    PMG_LAUNCH_CHECK();
+    return PMG_OK;
+}
+
+}  // namespace pmg
+
+using namespace pmg;
+
+extern "C" size_t pmg_fit_workspace_bytes(int32_t B, int64_t N) { return fit_workspace_bytes(B, N); }
+
+extern "C" int pmg_fit_prep_prompt(const float* logz, int64_t logz_stride, const float* lidar, const float* conf,
+                                   int32_t B, int32_t H, int32_t W, int32_t h, int32_t w, float* z, float* target,
+                                   uint8_t* flags, void* stream) {
+    if (!logz || !lidar || !conf || !z || !target || !flags || B <= 0 || H <= 0 || W <= 0 || h <= 0 || w <= 0)
+        return PMG_ERR_BAD_ARG;
+    return fit_prep_prompt(logz, logz_stride, lidar, conf, B, H, W, h, w, z, target, flags, as_stream(stream));
+}
+
+extern "C" int pmg_fit_prep_final(const float* depth, const float* mask01, const float* lidar, const float* conf,
+                                  int32_t B, int32_t H, int32_t W, int32_t h, int32_t w, float* z, float* target,
+                                  uint8_t* flags, void* stream) {
+    if (!depth || !lidar || !conf || !z || !target || !flags || B <= 0 || H <= 0 || W <= 0 || h <= 0 || w <= 0)
+        return PMG_ERR_BAD_ARG;
+    k_fit_prep_final<<<grid_for((int64_t)B * h * w), 256, 0, as_stream(stream)>>>(depth, mask01, lidar, conf, B, H, W,
+                                                                                   h, w, z, target, flags);
+    PMG_LAUNCH_CHECK();
+    return PMG_OK;
+}
+
+extern "C" int pmg_fit_solve(const float* z, const float* target, const uint8_t* flags, int32_t B, int64_t N,
+                             int32_t iters, float trim, int32_t min_points, pmg_fit_state* state, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+    if (!z || !target || !flags || !state || !workspace || B <= 0 || N <= 0 || iters < 0) return PMG_ERR_BAD_ARG;
+    if (workspace_bytes < fit_workspace_bytes(B, N)) return PMG_ERR_BAD_ARG;
+    size_t nclr = 0;
+    void* clr = fit_clear_region(workspace, B, N, &nclr);
+    PMG_CUDA_TRY(cudaMemsetAsync(clr, 0, nclr, as_stream(stream)));
+    return fit_solve(z, target, flags, B, N, iters, trim, min_points, state, workspace, as_stream(stream));
+}
+
+extern "C" int pmg_prompt_feats(const float* logz, int64_t logz_stride, const float* lidar, const float* conf,
+                                const pmg_fit_state* state, int32_t B, int32_t H, int32_t W, int32_t h, int32_t w,
+                                int32_t soft_gate, float* out, void* stream) {
+    if (!logz || !lidar || !conf || !state || !out || B <= 0) return PMG_ERR_BAD_ARG;
+    return prompt_feats(logz, logz_stride, lidar, conf, state, B, H, W, h, w, soft_gate, out, as_stream(stream));
+}
+
+extern "C" int pmg_apply_affine(float* depth, const pmg_fit_state* state, int32_t B, int64_t N, void* stream) {
+    if (!depth || !state || B <= 0 || N < 0) return PMG_ERR_BAD_ARG;
+    k_apply_affine<<<grid_for((int64_t)B * N), 256, 0, as_stream(stream)>>>(depth, state, B, N);
+    PMG_LAUNCH_CHECK();
+    return PMG_OK;
+}

@@ -1,0 +1,44 @@
+// Internal launchers shared by the C-ABI entry points and the refiner plan.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace pmg {
+
+struct Epi {
+    int mode;
+    float sa, out_scale;
+    const float* ws;
+    const float* bias;
+    const float* resid;
+    void* out;
+};
+
+int gemm_i8_simt(const int8_t* in, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask, const int32_t* count,
+                 int64_t max_rows, int Ci, int Co, int taps, const int8_t* w, const Epi& e, cudaStream_t s);
+// tcgen05 implicit-GEMM path; returns PMG_ERR_UNSUPPORTED for shapes it does not cover.
+int gemm_i8_tc(const int8_t* in, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask, const int32_t* count,
+               int64_t max_rows, int Ci, int Co, int taps, const int8_t* w, const Epi& e, cudaStream_t s);
+// Dispatch: tcgen05 where it applies, SIMT otherwise.
+int gemm_i8(const int8_t* in, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask, const int32_t* count,
+            int64_t max_rows, int Ci, int Co, int taps, const int8_t* w, const Epi& e, cudaStream_t s);
+
+int quantize(const float* x, int64_t n, float s, int8_t* q, cudaStream_t st);
+int ln_silu_q8(const float* x, const float* up_src, const int32_t* parent, const float* skip, float* x_out,
+               const int32_t* count, int64_t max_rows, int C, const float* gamma, const float* beta, double eps,
+               float scale, int8_t* q, cudaStream_t st);
+int pool_mean(const float* x, const int32_t* seg_idx, const int32_t* seg_off, const int32_t* count, int64_t max_rows,
+              int C, float scale, int8_t* q, float* out, cudaStream_t st);
+int gather_rows(const float* x, const int32_t* parent, const int32_t* count, int64_t max_rows, int C, float* out,
+                cudaStream_t st);
+int concat_q8(const float* x, const float* enc_tok, const int32_t* col, const int32_t* count, int64_t max_rows, int C,
+              float scale, int8_t* q, cudaStream_t st);
+int tokens_q8(const void* f16, int B, int K, int T, float scale, int8_t* q, cudaStream_t st);
+int planar_to_rows(const float* f, int B, int C, int T, float* out, cudaStream_t st);
+int input_proj(const float* pc, const float* prompt, int64_t N, int C, const float* wi, const float* bi,
+               const float* wp, const float* bp, float* x0, cudaStream_t st);
+int out_apply(const float* x, int64_t N, int C, const float* wo, const float* bo, const float* pc_in, float* pc_out,
+              float* delta, cudaStream_t st);
+
+}  // namespace pmg

@@ -1,0 +1,269 @@
+"""Op-level PyTorch wrappers over the C ABI (device tensors in, device tensors out, current CUDA stream).
+
+PyTorch only provides the device memory and the stream here; every computation is a kernel of libpmg_b200.so.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _lib
+from ._lib import EPI_ACC32, EPI_F32, EPI_F32_RESID, EPI_SILU_Q8, FitState, call  # noqa: F401
+
+
+def _stream():
+    return C.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _p(t):
+    return C.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _dev(t: torch.Tensor, dtype=None, name="tensor"):
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (no CPU path)")
+    if dtype is not None and t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return t
+
+
+# ----------------------------------------------------------------------------------------------------------------- #
+# Structure
+# ----------------------------------------------------------------------------------------------------------------- #
+def voxelize_l0(point_coord: torch.Tensor, depth_resolution: float = 256.0, ld: int | None = None):
+    """Level 0 of a point map [B,H,W,3]: (zq [N], zmin [B], zmax [B], nmap [27, ld], tile_mask)."""
+    _dev(point_coord, torch.float32, "point_coord")
+    B, H, W, _ = point_coord.shape
+    N = B * H * W
+    ld = ld or N
+    dev = point_coord.device
+    zq = torch.empty(N, dtype=torch.int32, device=dev)
+    zmin = torch.full((B,), 0x7F7F7F7F, dtype=torch.int32, device=dev)
+    zmax = torch.full((B,), -0x7F7F7F80, dtype=torch.int32, device=dev)
+    nmap = torch.empty((27, ld), dtype=torch.int32, device=dev)
+    mask = torch.zeros((ld + 31) // 32 + 1, dtype=torch.int32, device=dev)
+    call("pmg_voxelize_l0", _p(point_coord), B, H, W, float(depth_resolution), _p(zq), _p(zmin), _p(zmax), _p(nmap),
+         ld, _p(mask), _stream())
+    return zq, zmin, zmax, nmap, mask
+
+
+def l0_coords(zq, zmin, B, H, W):
+    coords = torch.empty((B * H * W, 4), dtype=torch.int32, device=zq.device)
+    call("pmg_l0_coords", _p(zq), _p(zmin), B, H, W, _p(coords), _stream())
+    return coords
+
+
+def pool_frames(B, Hf, Wf, fine_col_start, fine_z, zmin, cap, fine_count=None, with_coords=True, status=None):
+    """One 2x2x2 pool transition of a frame grid.  Returns a dict with count (int32[2]: stored, required),
+    z, col, col_start, coords, parent, seg_indices, seg_offsets (device tensors, capacity-sized)."""
+    dev = fine_z.device
+    Hc, Wc = (Hf + 1) // 2, (Wf + 1) // 2
+    M_f = fine_z.shape[0]
+    out = dict(
+        count=torch.zeros(2, dtype=torch.int32, device=dev),
+        z=torch.empty(cap, dtype=torch.int32, device=dev),
+        col=torch.empty(cap, dtype=torch.int32, device=dev),
+        col_start=torch.empty(B * Hc * Wc + 1, dtype=torch.int32, device=dev),
+        coords=torch.empty((cap, 4), dtype=torch.int32, device=dev) if with_coords else None,
+        parent=torch.empty(M_f, dtype=torch.int32, device=dev),
+        seg_indices=torch.empty(M_f, dtype=torch.int32, device=dev),
+        seg_offsets=torch.empty(cap + 1, dtype=torch.int32, device=dev),
+    )
+    nbytes = _lib.load().pmg_pool_frames_workspace_bytes(B, Hc, Wc)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    st = status if status is not None else torch.zeros(1, dtype=torch.int32, device=dev)
+    call("pmg_pool_frames", B, Hf, Wf, _p(fine_count), _p(fine_col_start), _p(fine_z), _p(zmin), _p(out["count"]),
+         _p(out["z"]), _p(out["col"]), _p(out["col_start"]), _p(out["coords"]), cap, _p(out["parent"]),
+         _p(out["seg_indices"]), _p(out["seg_offsets"]), _p(ws), nbytes, _p(st), _stream())
+    out["status"] = st
+    return out
+
+
+def nmap_frames(B, H, W, count, z, col, col_start, ld):
+    dev = z.device
+    nmap = torch.empty((27, ld), dtype=torch.int32, device=dev)
+    mask = torch.zeros((ld + 31) // 32 + 1, dtype=torch.int32, device=dev)
+    call("pmg_nmap_frames", B, H, W, _p(count), _p(z), _p(col), _p(col_start), _p(nmap), ld, _p(mask), _stream())
+    return nmap, mask
+
+
+def nmap_hash(coords: torch.Tensor, extents, row_major: bool = False, ld: int | None = None, status=None):
+    """Generic neighbour map of coords [M,4] int32 within the sparse shape `extents` (4 ints)."""
+    _dev(coords, torch.int32, "coords")
+    M = coords.shape[0]
+    dev = coords.device
+    ld = ld or M
+    nmap = torch.empty((M, 27) if row_major else (27, ld), dtype=torch.int32, device=dev)
+    mask = torch.zeros((max(M, ld) + 31) // 32 + 1, dtype=torch.int32, device=dev)
+    nbytes = _lib.load().pmg_nmap_hash_workspace_bytes(max(M, 1))
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    st = status if status is not None else torch.zeros(1, dtype=torch.int32, device=dev)
+    ext = (C.c_int64 * 4)(*[int(e) for e in extents])
+    call("pmg_nmap_hash", _p(coords), M, ext, _p(nmap), ld, int(row_major), _p(mask), _p(ws), nbytes, _p(st),
+         _stream())
+    return nmap, mask, st
+
+
+# ----------------------------------------------------------------------------------------------------------------- #
+# int8 layers
+# ----------------------------------------------------------------------------------------------------------------- #
+def _epi_out(mode, rows, n, dev):
+    if mode == EPI_ACC32:
+        return torch.empty((rows, n), dtype=torch.int32, device=dev)
+    if mode == EPI_SILU_Q8:
+        return torch.empty((rows, n), dtype=torch.int8, device=dev)
+    return torch.empty((rows, n), dtype=torch.float32, device=dev)
+
+
+def spconv_i8(q_in, nmap, tile_mask, weight_tap_major, w_scale=None, bias=None, act_scale=1.0, mode=EPI_ACC32,
+              out_scale=1.0, resid=None, count=None, rows=None):
+    """Submanifold conv: q_in [M_in, Ci] int8, nmap [27, ld] int32, weight [27, Co, Ci] int8."""
+    _dev(q_in, torch.int8, "q_in")
+    _dev(weight_tap_major, torch.int8, "weight")
+    ld = nmap.shape[1]
+    rows = ld if rows is None else rows
+    Co, Ci = weight_tap_major.shape[1], weight_tap_major.shape[2]
+    out = _epi_out(mode, rows, Co, q_in.device)
+    call("pmg_spconv_i8", _p(q_in), _p(nmap), ld, _p(tile_mask), _p(count), rows, Ci, Co, _p(weight_tap_major),
+         _p(w_scale), _p(bias), float(act_scale), mode, float(out_scale), _p(resid), _p(out), _stream())
+    return out
+
+
+def dense_i8(a, weight, w_scale=None, bias=None, act_scale=1.0, mode=EPI_ACC32, out_scale=1.0, resid=None,
+             count=None, rows=None):
+    """Dense int8 layer: a [M, K] int8, weight [N, K] int8."""
+    _dev(a, torch.int8, "a")
+    _dev(weight, torch.int8, "weight")
+    rows = a.shape[0] if rows is None else rows
+    N, K = weight.shape
+    out = _epi_out(mode, rows, N, a.device)
+    call("pmg_dense_i8", _p(a), _p(count), rows, K, N, _p(weight), _p(w_scale), _p(bias), float(act_scale), mode,
+         float(out_scale), _p(resid), _p(out), _stream())
+    return out
+
+
+def quantize(x, scale):
+    _dev(x, torch.float32, "x")
+    q = torch.empty(x.shape, dtype=torch.int8, device=x.device)
+    call("pmg_quantize", _p(x), x.numel(), float(scale), _p(q), _stream())
+    return q
+
+
+def ln_silu_q8(x, gamma, beta, scale, eps=1e-6, up_src=None, parent=None, skip=None, count=None, rows=None):
+    C_ = gamma.shape[0]
+    ref = x if x is not None else skip
+    rows = ref.shape[0] if rows is None else rows
+    q = torch.empty((rows, C_), dtype=torch.int8, device=ref.device)
+    x_out = torch.empty((rows, C_), dtype=torch.float32, device=ref.device) if up_src is not None else None
+    call("pmg_ln_silu_q8", _p(x), _p(up_src), _p(parent), _p(skip), _p(x_out), _p(count), rows, C_, _p(gamma),
+         _p(beta), float(eps), float(scale), _p(q), _stream())
+    return (q, x_out) if up_src is not None else q
+
+
+def pool_mean(x, seg_indices, seg_offsets, rows, scale=None, count=None):
+    C_ = x.shape[1]
+    if scale is None:
+        out = torch.empty((rows, C_), dtype=torch.float32, device=x.device)
+        call("pmg_pool_mean_f32", _p(x), _p(seg_indices), _p(seg_offsets), _p(count), rows, C_, _p(out), _stream())
+    else:
+        out = torch.empty((rows, C_), dtype=torch.int8, device=x.device)
+        call("pmg_pool_mean_q8", _p(x), _p(seg_indices), _p(seg_offsets), _p(count), rows, C_, float(scale), _p(out),
+             _stream())
+    return out
+
+
+def gather_rows(x, parent, rows=None, count=None):
+    _dev(x, torch.float32, "x")
+    rows = parent.shape[0] if rows is None else rows
+    out = torch.empty((rows, x.shape[1]), dtype=torch.float32, device=x.device)
+    call("pmg_gather_rows_f32", _p(x), _p(parent), _p(count), rows, x.shape[1], _p(out), _stream())
+    return out
+
+
+def spconv_f32(x, nmap, tile_mask, weight_tap_major, bias=None, rows=None, count=None):
+    _dev(x, torch.float32, "x")
+    _dev(weight_tap_major, torch.float32, "weight")
+    ld = nmap.shape[1]
+    rows = ld if rows is None else rows
+    Co, Ci = weight_tap_major.shape[1], weight_tap_major.shape[2]
+    out = torch.empty((rows, Co), dtype=torch.float32, device=x.device)
+    call("pmg_spconv_f32", _p(x), _p(nmap), ld, _p(tile_mask), _p(count), rows, Ci, Co, _p(weight_tap_major),
+         _p(bias), _p(out), _stream())
+    return out
+
+
+# ----------------------------------------------------------------------------------------------------------------- #
+# Fit
+# ----------------------------------------------------------------------------------------------------------------- #
+def _fit_state(B, dev):
+    return torch.zeros((B, 18), dtype=torch.int32, device=dev)   # 72 bytes per frame (pmg_fit_state)
+
+
+def fit_state_view(state: torch.Tensor):
+    """Host copy of device fit states -> list of dicts."""
+    raw = state.cpu().numpy().tobytes()
+    n = len(raw) // C.sizeof(FitState)
+    arr = (FitState * n).from_buffer_copy(raw)
+    return [dict(s=a.s, t=a.t, thr=a.thr, count=a.count, k=a.k, ok=a.ok, sums=list(a.sums)) for a in arr]
+
+
+def fit_solve(z, target, flags, iters=4, trim=0.2, min_points=32):
+    B, N = z.shape
+    dev = z.device
+    st = _fit_state(B, dev)
+    nbytes = _lib.load().pmg_fit_workspace_bytes(B, N)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+    call("pmg_fit_solve", _p(z), _p(target), _p(flags), B, N, iters, float(trim), min_points, _p(st), _p(ws), nbytes,
+         _stream())
+    return st
+
+
+def fit_prep_prompt(logz, lidar, conf):
+    """logz [B,H,W] (contiguous) or a point map [B,H,W,3] (logz read with stride 3)."""
+    if logz.dim() == 4:
+        base, stride = logz[..., 2], 3
+        ptr = C.c_void_p(logz.data_ptr() + 8)
+        B, H, W = logz.shape[:3]
+    else:
+        base, stride = logz, 1
+        ptr = _p(logz)
+        B, H, W = logz.shape
+    h, w = lidar.shape[-2:]
+    dev = logz.device
+    N = B * H * W
+    z = torch.empty((B, H * W), dtype=torch.float32, device=dev)
+    y = torch.empty((B, H * W), dtype=torch.float32, device=dev)
+    fl = torch.empty((B, H * W), dtype=torch.uint8, device=dev)
+    del base
+    call("pmg_fit_prep_prompt", ptr, stride, _p(lidar), _p(conf), B, H, W, h, w, _p(z), _p(y), _p(fl), _stream())
+    return z, y, fl
+
+
+def fit_prep_final(depth, lidar, conf, mask01=None):
+    B, H, W = depth.shape
+    h, w = lidar.shape[-2:]
+    dev = depth.device
+    z = torch.empty((B, h * w), dtype=torch.float32, device=dev)
+    y = torch.empty((B, h * w), dtype=torch.float32, device=dev)
+    fl = torch.empty((B, h * w), dtype=torch.uint8, device=dev)
+    call("pmg_fit_prep_final", _p(depth), _p(mask01), _p(lidar), _p(conf), B, H, W, h, w, _p(z), _p(y), _p(fl),
+         _stream())
+    return z, y, fl
+
+
+def prompt_feats(logz, lidar, conf, state, soft_gate=True):
+    B, H, W = logz.shape
+    h, w = lidar.shape[-2:]
+    out = torch.empty((B * H * W, 2), dtype=torch.float32, device=logz.device)
+    call("pmg_prompt_feats", _p(logz), 1, _p(lidar), _p(conf), _p(state), B, H, W, h, w, int(soft_gate), _p(out),
+         _stream())
+    return out
+
+
+def apply_affine(depth, state):
+    B = depth.shape[0]
+    call("pmg_apply_affine", _p(depth), _p(state), B, depth[0].numel(), _stream())
+    return depth

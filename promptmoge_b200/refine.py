@@ -1,0 +1,93 @@
+"""User-facing refinement API: host (numpy / CPU tensor) frames in, refined point maps out.
+
+``Refiner`` wraps one RefinerEngine plan (a model geometry and a frame batch), keeps pinned staging buffers, and runs
+``refine(...)`` as: host->device copies of the frame's inputs, the per-frame encoder conditioning, the K-step CUDA
+graph, device->host copy of the refined point map and the per-frame (s, t) of the last LiDAR fit -- the refine loop
+of MoGeModel.forward (moge/model/v3.py:537-576) for ``infer(model, image, lidar, conf, refine_steps=K)``.
+"""
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+import numpy as np
+import torch
+
+from . import synth
+from .engine import Geometry, RefinerEngine
+from .ops import fit_state_view
+
+_CLIPS = Path(__file__).resolve().parent / "synth_clips.json"
+
+
+def synthetic_model(model: str = "A", seed: int = 0):
+    """Random-init weights of a model's refiner and the activation clips the reference's observer pass produced for
+    them on the seed-0 synthetic frame (tests/golden/make_golden.py)."""
+    weights = synth.make_refiner_weights(model, seed)
+    m = synth.MODELS[model]
+    clips = json.loads(_CLIPS.read_text())[f"{model}_{m['H']}x{m['W']}_seed{seed}"]
+    return weights, clips
+
+
+class Refiner:
+    def __init__(self, weights: dict, clips: dict, model: str = "A", height: int | None = None,
+                 width: int | None = None, batch: int = 1, device="cuda", capacity=None):
+        m = synth.MODELS[model]
+        self.geo = Geometry(channels=m["model_channels"], height=height or m["H"], width=width or m["W"],
+                            batch=batch)
+        self.device = torch.device(device)
+        self.engine = RefinerEngine(weights, clips, self.geo, device=self.device, capacity=capacity)
+        B, H, W = batch, self.geo.height, self.geo.width
+        ed = 2 ** (self.geo.levels - 1)
+        lh, lw = self.geo.lidar_hw
+        dev = self.device
+        # device-resident inputs the graph reads, and pinned host staging
+        self.d_pc = torch.empty((B, H, W, 3), dtype=torch.float32, device=dev)
+        self.d_ld = torch.empty((B, 1, lh, lw), dtype=torch.float32, device=dev)
+        self.d_lc = torch.empty((B, 1, lh, lw), dtype=torch.float32, device=dev)
+        self.d_enc = torch.empty((B, synth.ENC_CHANNELS, H // ed, W // ed), dtype=torch.float16, device=dev)
+        self.d_uv = torch.empty((B, self.geo.channels[-1], H // ed, W // ed), dtype=torch.float32, device=dev)
+        self.h_out = torch.empty((B, H, W, 3), dtype=torch.float32).pin_memory()
+        self.h_fit = torch.empty((B, 18), dtype=torch.int32).pin_memory()
+        self.engine.set_inputs(self.d_pc, self.d_ld, self.d_lc)
+        self._K = None
+
+    def input_bytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.d_pc, self.d_ld, self.d_lc, self.d_enc, self.d_uv))
+
+    def output_bytes(self) -> int:
+        return self.h_out.numel() * 4 + self.h_fit.numel() * 4
+
+    def _ensure_graph(self, K: int):
+        if self._K != K:
+            self.engine.set_inputs(self.d_pc, self.d_ld, self.d_lc)
+            self.engine.capture(K)
+            self._K = K
+
+    def refine(self, point_coord, lidar_depth, lidar_conf, encoder_feature, uv_bias=None, K: int = 1,
+               sync: bool = True):
+        """Refine a batch of frames.  Host arrays/tensors (pinned CPU tensors copy asynchronously):
+        point_coord [B,H,W,3] fp32, lidar_depth/lidar_conf [B,1,192,256] fp32, encoder_feature [B,1024,h,w] fp16,
+        uv_bias [B,C,h,w] fp32 or None.  Returns (refined point map [B,H,W,3] host tensor, fit list)."""
+        self._ensure_graph(K)
+        s = torch.cuda.current_stream(self.device)
+        for dst, src in ((self.d_pc, point_coord), (self.d_ld, lidar_depth), (self.d_lc, lidar_conf),
+                         (self.d_enc, encoder_feature)):
+            dst.copy_(torch.as_tensor(src), non_blocking=True)
+        if uv_bias is not None:
+            self.d_uv.copy_(torch.as_tensor(uv_bias), non_blocking=True)
+        self.engine.set_frame(self.d_enc, self.d_uv if uv_bias is not None else None)
+        out, fit = self.engine.replay()
+        self.h_out.copy_(out, non_blocking=True)
+        self.h_fit.copy_(fit, non_blocking=True)
+        if sync:
+            s.synchronize()
+            return self.h_out, fit_state_view(self.h_fit)
+        return self.h_out, None
+
+    def close(self):
+        self.engine.close()
+
+
+def pinned(a: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a)).pin_memory()

@@ -1,0 +1,180 @@
+"""int8 submanifold conv and dense int8 layers on the GPU: int32 accumulators bit-exact against the reference's own
+exact accumulators (fixture digests) and the oracle, epilogues bit-exact against the oracle's fp32 formulas."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import sha
+from oracle import refiner as oref
+
+pytestmark = pytest.mark.gpu
+
+SMALL = ["B_small", "A_small"]
+
+
+def _widths(g):
+    from promptmoge_b200 import synth
+    return synth.MODELS[g.config["model"]]["model_channels"]
+
+
+def _level_for_conv(name, L):
+    if name.startswith("down_stages."):
+        return int(name.split(".")[1])
+    if name.startswith("bottleneck_stage"):
+        return L - 1
+    return L - 2 - int(name.split(".")[1])
+
+
+def _tap_major(nmap_rm: np.ndarray):
+    return torch.from_numpy(np.ascontiguousarray(nmap_rm.T)).cuda()
+
+
+def _mask(nmap_rm: np.ndarray):
+    occ = (nmap_rm >= 0).astype(np.int64) << np.arange(27)
+    M = nmap_rm.shape[0]
+    out = np.zeros((M + 31) // 32 + 1, np.int64)
+    for t in range((M + 31) // 32):
+        out[t] = np.bitwise_or.reduce(occ[t * 32:(t + 1) * 32].ravel())
+    return torch.from_numpy(out.astype(np.uint32).view(np.int32)).cuda()
+
+
+@pytest.mark.parametrize("name", SMALL)
+def test_every_layer_accumulator_bit_exact(golden, name):
+    """Given the reference's int8 input of each of the 25/31 quantised layers, the GPU's int32 accumulators hash to
+    the reference's exact accumulators, and each epilogue equals the oracle's fp32 arithmetic bit for bit."""
+    from promptmoge_b200 import ops
+    from promptmoge_b200.engine import act_scale, quantise_weight
+    g = golden(name)
+    widths = _widths(g)
+    L = len(widths)
+    w = g.weights()
+    for n in g.layer_names(0):
+        key = f"s0_Q_{n}"
+        q = torch.from_numpy(g[key + "_q"]).cuda()
+        qw, sw = quantise_weight(w[n + ".weight"])
+        bias = w[n + ".bias"]
+        sa = act_scale(g.clips[n])
+        if ".conv" in n:
+            nm = g[f"s0_L{_level_for_conv(n, L)}_nmap"]
+            tm, mask = _tap_major(nm), _mask(nm)
+            wt = torch.from_numpy(np.ascontiguousarray(qw.reshape(qw.shape[0], 27, -1).transpose(1, 0, 2))).cuda()
+            acc = ops.spconv_i8(q, tm, mask, wt)
+            f32 = ops.spconv_i8(q, tm, mask, wt, torch.from_numpy(sw).cuda(), torch.from_numpy(bias).cuda(), sa,
+                                ops.EPI_F32)
+        else:
+            wt = torch.from_numpy(qw).cuda()
+            acc = ops.dense_i8(q, wt)
+            f32 = ops.dense_i8(q, wt, torch.from_numpy(sw).cuda(), torch.from_numpy(bias).cuda(), sa, ops.EPI_F32)
+        torch.cuda.synchronize()
+        acc_np = acc.cpu().numpy()
+        assert sha(acc_np) == g.digests[key + "_acc"], n
+        y = oref.dequant(acc_np.astype(np.int64), sa, sw, bias)
+        np.testing.assert_array_equal(f32.cpu().numpy(), y, err_msg=n)
+        rows = g[key + "_rows"]
+        yr = g[key + "_y_rows"]
+        assert np.abs(f32.cpu().numpy()[rows] - yr).max() <= 1e-3 * np.abs(yr).max(), n
+
+
+def test_fused_epilogues_match_oracle(golden):
+    from promptmoge_b200 import ops
+    from promptmoge_b200.engine import act_scale, quantise_weight
+    g = golden("A_small")
+    w = g.weights()
+    n1, n2 = "down_stages.1.0.conv1", "down_stages.1.0.conv2"
+    q = torch.from_numpy(g[f"s0_Q_{n1}_q"]).cuda()
+    nm = g["s0_L1_nmap"]
+    tm, mask = _tap_major(nm), _mask(nm)
+    qw, sw = quantise_weight(w[n1 + ".weight"])
+    wt = torch.from_numpy(np.ascontiguousarray(qw.reshape(qw.shape[0], 27, -1).transpose(1, 0, 2))).cuda()
+    sa, s_next = act_scale(g.clips[n1]), act_scale(g.clips[n2])
+    args = (torch.from_numpy(sw).cuda(), torch.from_numpy(w[n1 + ".bias"]).cuda(), sa)
+    acc = ops.spconv_i8(q, tm, mask, wt).cpu().numpy().astype(np.int64)
+    y = oref.dequant(acc, sa, sw, w[n1 + ".bias"])
+    q8 = ops.spconv_i8(q, tm, mask, wt, *args, ops.EPI_SILU_Q8, s_next).cpu().numpy()
+    want = np.clip(np.rint(oref.silu(y) / np.float32(s_next)), -127, 127).astype(np.int8)
+    # SiLU's exp may differ by an ulp between CUDA and numpy: allow rare one-step flips, nothing larger.
+    d = np.abs(q8.astype(np.int32) - want.astype(np.int32))
+    assert d.max() <= 1 and (d > 0).mean() < 1e-3
+    resid = torch.randn(acc.shape, generator=torch.Generator().manual_seed(0)).cuda()
+    r = ops.spconv_i8(q, tm, mask, wt, *args, ops.EPI_F32_RESID, 1.0, resid).cpu().numpy()
+    np.testing.assert_array_equal(r, (y + resid.cpu().numpy()).astype(np.float32))
+
+
+@pytest.mark.parametrize("name", ["conv_20k_c32", "conv_100k_c16"])
+def test_conv_sweep_accumulators(golden, name):
+    from promptmoge_b200 import ops, synth
+    g = golden(name)
+    c = g.config
+    coords = torch.from_numpy(synth.make_surface_voxels(c["N"], c["seed"])).cuda()
+    nm_tm, mask, _ = ops.nmap_hash(coords, [1, 1 << 21, 1 << 21, 1 << 21])
+    rng = np.random.default_rng(c["seed"] + 100)
+    q = rng.integers(-127, 128, (coords.shape[0], c["C"])).astype(np.int8)
+    qw = rng.integers(-127, 128, (c["C"], 3, 3, 3, c["C"])).astype(np.int8)
+    wt = torch.from_numpy(np.ascontiguousarray(qw.reshape(c["C"], 27, c["C"]).transpose(1, 0, 2))).cuda()
+    acc = ops.spconv_i8(torch.from_numpy(q).cuda(), nm_tm, mask, wt)
+    torch.cuda.synchronize()
+    assert sha(acc.cpu().numpy()) == str(g["acc_sha"])
+
+
+@pytest.mark.parametrize("C", [16, 32, 64, 128, 256])
+def test_conv_all_widths_against_oracle(C):
+    """Every channel width, random int8 data, with and without tile masks (all-taps path)."""
+    from promptmoge_b200 import ops, synth
+    from oracle import structure as ost
+    coords_np = synth.make_surface_voxels(3000, seed=C)
+    coords = torch.from_numpy(coords_np).cuda()
+    ext = [1, 1 << 21, 1 << 21, 1 << 21]
+    tm, mask, _ = ops.nmap_hash(coords, ext)
+    rng = np.random.default_rng(C)
+    q = rng.integers(-127, 128, (coords_np.shape[0], C)).astype(np.int8)
+    qw = rng.integers(-127, 128, (C, 3, 3, 3, C)).astype(np.int8)
+    wt = torch.from_numpy(np.ascontiguousarray(qw.reshape(C, 27, C).transpose(1, 0, 2))).cuda()
+    want = oref.conv_acc(q, ost.nmap_sorted(coords_np, ext), qw)
+    for m in (mask, None):
+        got = ops.spconv_i8(torch.from_numpy(q).cuda(), tm, m, wt).cpu().numpy()
+        np.testing.assert_array_equal(got.astype(np.int64), want)
+
+
+@pytest.mark.parametrize("K,N", [(32, 64), (64, 128), (128, 256), (256, 256), (256, 128), (128, 64), (64, 32),
+                                 (1024, 256), (512, 256)])
+def test_dense_shapes_against_oracle(K, N):
+    from promptmoge_b200 import ops
+    rng = np.random.default_rng(K * 1000 + N)
+    M = 777
+    a = rng.integers(-127, 128, (M, K)).astype(np.int8)
+    w = rng.integers(-127, 128, (N, K)).astype(np.int8)
+    got = ops.dense_i8(torch.from_numpy(a).cuda(), torch.from_numpy(w).cuda()).cpu().numpy()
+    np.testing.assert_array_equal(got.astype(np.int64), oref.linear_acc(a, w))
+
+
+def test_count_limits_rows(golden):
+    """Rows past the device-side count are not written (graph-safe sizing by capacity)."""
+    from promptmoge_b200 import ops
+    rng = np.random.default_rng(5)
+    a = torch.from_numpy(rng.integers(-127, 128, (256, 64)).astype(np.int8)).cuda()
+    w = torch.from_numpy(rng.integers(-127, 128, (32, 64)).astype(np.int8)).cuda()
+    cnt = torch.tensor([100], dtype=torch.int32).cuda()
+    out = ops.dense_i8(a, w, count=cnt)
+    out_full = ops.dense_i8(a, w)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out[:100].cpu().numpy(), out_full[:100].cpu().numpy())
+
+
+def test_float_conv_matches_reference_semantics(golden):
+    """The fp32 operator behind the flex_gemm-compatible module: bias + sum_v W_v x[nmap_v] (within fp32 rounding)."""
+    from promptmoge_b200 import ops
+    g = golden("A_small")
+    nm = g["s0_L1_nmap"]
+    M = nm.shape[0]
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((M, 64)).astype(np.float32)
+    w = rng.standard_normal((48, 3, 3, 3, 64)).astype(np.float32) * 0.05
+    b = rng.standard_normal(48).astype(np.float32)
+    want = np.tile(b.astype(np.float64), (M, 1))
+    wv = w.reshape(48, 27, 64).astype(np.float64)
+    for v in range(27):
+        rows = np.nonzero(nm[:, v] >= 0)[0]
+        want[rows] += x[nm[rows, v]].astype(np.float64) @ wv[:, v, :].T
+    wt = torch.from_numpy(np.ascontiguousarray(w.reshape(48, 27, 64).transpose(1, 0, 2))).cuda()
+    got = ops.spconv_f32(torch.from_numpy(x).cuda(), _tap_major(nm), _mask(nm), wt, torch.from_numpy(b).cuda())
+    np.testing.assert_allclose(got.cpu().numpy(), want, rtol=1e-4, atol=1e-4)

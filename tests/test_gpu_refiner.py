@@ -1,0 +1,113 @@
+"""The fused refiner plan (one refine step as device work / one CUDA graph) against the oracle and the reference."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import sha
+
+pytestmark = pytest.mark.gpu
+
+
+def _engine(g, batch=1):
+    from promptmoge_b200 import synth
+    from promptmoge_b200.engine import Geometry, RefinerEngine
+    c = g.config
+    geo = Geometry(channels=synth.MODELS[c["model"]]["model_channels"], height=c["H"], width=c["W"], batch=batch)
+    return RefinerEngine(g.weights(), g.clips, geo)
+
+
+def _inputs(eng, sc):
+    eng.set_frame(torch.from_numpy(sc.encoder_feature).cuda(), torch.from_numpy(sc.uv_bias).cuda())
+    eng.set_inputs(torch.from_numpy(sc.point_coord).cuda(), torch.from_numpy(sc.lidar_depth).cuda(),
+                   torch.from_numpy(sc.lidar_conf).cuda())
+
+
+@pytest.mark.parametrize("name", ["B_small", "A_small"])
+def test_step_matches_oracle_and_reference(golden, name):
+    from oracle import refiner as oref
+    from promptmoge_b200 import synth
+    g = golden(name)
+    sc = g.scene()
+    eng = _engine(g)
+    _inputs(eng, sc)
+    out, fit = eng.run(1)
+    rc, counts = eng.status()
+    assert rc == 0
+    torch.cuda.synchronize()
+    # structure of the step, read back from the plan, bit-exact against the reference
+    widths = synth.MODELS[g.config["model"]]["model_channels"]
+    for k in range(1, len(widths)):
+        info = eng.level_info(k)
+        M = counts[k]
+        assert M == g[f"s0_L{k}_coords"].shape[0]
+        nm = eng.debug_tensor("nmap", k, (27, info["cap"]), torch.int32)[:, :M].t().cpu().numpy()
+        np.testing.assert_array_equal(nm, g[f"s0_L{k}_nmap"])
+    # refined log-depth vs the oracle's step on the same inputs, and vs the reference
+    qr = oref.QuantRefiner(g.weights(), g.clips, widths, [2] * (len(widths) - 1))
+    new_pc, info = oref.refine_step(qr, sc.point_coord, sc.lidar_depth, sc.lidar_conf,
+                                    sc.encoder_feature.astype(np.float32), sc.uv_bias)
+    got = out.cpu().numpy()
+    np.testing.assert_array_equal(got[..., :2], sc.point_coord[..., :2])
+    for ref_logz in (new_pc[..., 2], (g["s0_logz_in"] + g["s0_delta"]).astype(np.float32)):
+        d_g, d_r = np.exp(got[..., 2].astype(np.float64)), np.exp(ref_logz.astype(np.float64))
+        assert np.mean(np.abs(d_g - d_r) / d_r) < 2e-3          # AbsRel-delta of the refined depth
+        assert np.abs(got[..., 2] - ref_logz).max() < 2e-3
+
+
+def test_graph_replay_is_bitwise_deterministic(golden):
+    g = golden("A_small")
+    sc = g.scene()
+    eng = _engine(g)
+    _inputs(eng, sc)
+    ref, _ = eng.run(2)
+    ref = ref.clone()
+    out, _ = eng.capture(2)
+    for _ in range(3):
+        eng.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref)
+    assert eng.status()[0] == 0
+
+
+@pytest.mark.parametrize("name", ["B_full", "A_full"])
+def test_full_size_step_against_reference(golden, name):
+    """480x640 / 240x320: the plan's level structure hashes to the reference's, and the refined log-depth agrees on
+    the reference's sampled pixels (depth AbsRel-delta < 0.2 %)."""
+    from promptmoge_b200 import synth
+    g = golden(name)
+    sc = g.scene()
+    eng = _engine(g)
+    _inputs(eng, sc)
+    eng.capture(1)
+    out, fit = eng.replay()
+    rc, counts = eng.status()
+    assert rc == 0
+    widths = synth.MODELS[g.config["model"]]["model_channels"]
+    for k in range(1, len(widths)):
+        info = eng.level_info(k)
+        nm = eng.debug_tensor("nmap", k, (27, info["cap"]), torch.int32)[:, :counts[k]].t().contiguous().cpu().numpy()
+        assert sha(nm) == g.digests[f"s0_L{k}_nmap"], k
+    got = out.cpu().numpy()[..., 2].reshape(-1)
+    pix = g["s0_pix"]
+    ref_logz = (g["s0_logz_in_pix"] + g["s0_delta_pix"]).astype(np.float32)
+    d_g, d_r = np.exp(got[pix].astype(np.float64)), np.exp(ref_logz.astype(np.float64))
+    assert np.mean(np.abs(d_g - d_r) / d_r) < 2e-3
+    np.testing.assert_allclose(got[pix], ref_logz, atol=5e-3)
+
+
+def test_batched_frames_equal_single_frames(golden):
+    """Frames are independent: a batch of two gives each frame's single-frame result bit for bit."""
+    from promptmoge_b200 import synth
+    g = golden("B_small")
+    c = g.config
+    sc2 = synth.make_scene(c["seed"], c["H"], c["W"], c["encoder_downsample"], 256, batch=2)
+    eng2 = _engine(g, batch=2)
+    _inputs(eng2, sc2)
+    out2, _ = eng2.run(1)
+    out2 = out2.cpu().numpy()
+    for b in range(2):
+        sc1 = synth.make_scene(c["seed"] + b, c["H"], c["W"], c["encoder_downsample"], 256, batch=1)
+        eng1 = _engine(g)
+        _inputs(eng1, sc1)
+        out1, _ = eng1.run(1)
+        np.testing.assert_array_equal(out2[b], out1.cpu().numpy()[0])
