@@ -100,6 +100,18 @@ int pmg_nmap_hash(const int32_t* coords, int64_t M, const int64_t* extents_host,
                   int32_t row_major, uint32_t* tile_mask, void* workspace, size_t workspace_bytes, int32_t* status,
                   void* stream);
 
+/* pmg_nmap_hash without a workspace, for callers that cannot allocate device memory while they run (a per-frame
+ * loop that reserved its memory at start-up and must not stall on an allocation, or a host that owns all device
+ * memory through its own allocator).  This entry point has no counterpart in the reference.  Its hash table is a
+ * fixed 6 MiB array compiled into the library and resident on every GPU that loads it until the process exits;
+ * M must be <= 262144 voxels (larger M returns PMG_ERR_BAD_ARG without touching the device).  It calls no
+ * allocator.  The first call on a device looks the table's address up (cudaGetSymbolAddress) with that device
+ * current: make that first call before any stream capture.  Every call reuses the same table, clearing the part it
+ * needs at its start, so calls whose executions overlap on the GPU (other streams, other host threads) race and
+ * corrupt each other; serialise them.  Same arguments and results as pmg_nmap_hash. */
+int pmg_nmap_hash_noalloc(const int32_t* coords, int64_t M, const int64_t* extents_host, int32_t* nmap, int64_t ld,
+                          int32_t row_major, uint32_t* tile_mask, int32_t* status, void* stream);
+
 /* --------------------------------------------------------------------------------------------------------------
  * int8 submanifold convolution and dense int8 layers
  * ------------------------------------------------------------------------------------------------------------ */

@@ -13,6 +13,7 @@
 // column index, so their neighbour map comes from a hash table of 64-bit linearised keys probed by groups of 8
 // lanes that read one 64-byte bucket per step (warp-cooperative bucketed linear probing).
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -519,6 +520,79 @@ extern "C" int pmg_nmap_hash(const int32_t* coords, int64_t M, const int64_t* ex
     uint64_t* keys = reinterpret_cast<uint64_t*>(workspace);
     int32_t* vals = reinterpret_cast<int32_t*>(keys + nbk * kBucket);
     cudaStream_t s = as_stream(stream);
+    PMG_CUDA_TRY(cudaMemsetAsync(keys, 0xff, (size_t)nbk * kBucket * sizeof(uint64_t), s));
+    const int blocks_ins = (int)std::min<int64_t>((M * 8 + 255) / 256, (int64_t)kNumSMs * 16);
+    k_hash_insert<<<blocks_ins, 256, 0, s>>>(reinterpret_cast<const int4*>(coords), M, ex, keys, vals, nbk, status);
+    PMG_LAUNCH_CHECK();
+    k_hash_nmap<<<ceil_div(M, 256), 256, 0, s>>>(reinterpret_cast<const int4*>(coords), M, ex, keys, vals, nbk, nmap,
+                                                 ld, row_major, tile_mask);
+    PMG_LAUNCH_CHECK();
+    return PMG_OK;
+}
+
+// ================================================================================================================= //
+// Allocation-free variant of the hash neighbour map
+//
+// Some callers cannot allocate device memory once they are running: a capture/depth loop that reserves its whole
+// memory budget at start-up and must never pay the device-wide synchronisation a cudaMalloc/cudaFree can cost in
+// the middle of a frame, or a host process that hands this library a slice of memory owned by another allocator
+// and forbids allocations behind its back.  pmg_nmap_hash needs a caller workspace for its hash table; this variant
+// instead uses one fixed table compiled into the library (g_nmap_noalloc_table below, 6 MiB, resident on every GPU
+// that loads the library until the process exits), so the caller only passes inputs and outputs.
+// ================================================================================================================= //
+namespace pmg {
+
+constexpr int64_t kNoAllocMaxVoxels = int64_t(1) << 18;               // 262,144 voxels
+constexpr int64_t kNoAllocSlots = int64_t(1) << 19;                   // table slots for the maximum (load <= 1/2)
+constexpr size_t kNoAllocBytes = size_t(kNoAllocSlots) * (sizeof(uint64_t) + sizeof(int32_t));
+
+// keys: kNoAllocSlots x uint64 at offset 0; values: kNoAllocSlots x int32 after them
+static __device__ __align__(256) unsigned char g_nmap_noalloc_table[kNoAllocBytes];
+
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_addr[256] = {};
+
+// Device address of the table on the current device.  Host code cannot use the symbol itself (on the host it names a
+// shadow variable, not device memory), so the address is looked up once per device, with that device current.
+static int noalloc_table(void** out) {
+    int dev = 0;
+    PMG_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 256) return PMG_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void* p = nullptr;
+        PMG_CUDA_TRY(cudaGetSymbolAddress(&p, g_nmap_noalloc_table));
+        g_noalloc_addr[dev] = p;
+    }
+    *out = g_noalloc_addr[dev];
+    return PMG_OK;
+}
+
+}  // namespace pmg
+
+extern "C" int pmg_nmap_hash_noalloc(const int32_t* coords, int64_t M, const int64_t* extents, int32_t* nmap,
+                                     int64_t ld, int32_t row_major, uint32_t* tile_mask, int32_t* status,
+                                     void* stream) {
+    if (!coords || M < 0 || !nmap || !extents) return PMG_ERR_BAD_ARG;
+    if (M > kNoAllocMaxVoxels) return PMG_ERR_BAD_ARG;               // beyond the fixed table: refused
+    if (!row_major && ld < M) return PMG_ERR_BAD_ARG;
+    Extents ex;
+    unsigned __int128 prod = 1;
+    for (int d = 0; d < 4; ++d) {
+        if (extents[d] <= 0) return PMG_ERR_BAD_ARG;
+        ex.e[d] = extents[d];
+        prod *= (unsigned __int128)extents[d];
+        if (prod >> 64) return PMG_ERR_UNSUPPORTED;
+    }
+    void* table = nullptr;
+    const int rc = noalloc_table(&table);
+    if (rc != PMG_OK) return rc;
+    if (M == 0) return PMG_OK;
+    const int64_t nbk = hash_buckets(M);                               // <= kNoAllocSlots / kBucket for M <= max
+    uint64_t* keys = reinterpret_cast<uint64_t*>(table);
+    int32_t* vals = reinterpret_cast<int32_t*>(keys + kNoAllocSlots);
+    cudaStream_t s = as_stream(stream);
+    // The table keeps the previous call's keys: mark the slots this call uses empty before inserting.
     PMG_CUDA_TRY(cudaMemsetAsync(keys, 0xff, (size_t)nbk * kBucket * sizeof(uint64_t), s));
     const int blocks_ins = (int)std::min<int64_t>((M * 8 + 255) / 256, (int64_t)kNumSMs * 16);
     k_hash_insert<<<blocks_ins, 256, 0, s>>>(reinterpret_cast<const int4*>(coords), M, ex, keys, vals, nbk, status);
