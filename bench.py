@@ -135,14 +135,17 @@ def dominant_conv(torch, eng, reps: int = 20):
         ws = torch.full((C_,), 1e-3, device="cuda")
         b = torch.zeros(C_, device="cuda")
         nnz = int((nmap[:, :M] >= 0).sum().item())
-        ops.spconv_i8(q1, nmap, mask, w, ws, b, 0.01, ops.EPI_SILU_Q8, 0.02, count=cnt)
+        wp = ops.pack_weights_umma(w) if ops.tc_supported(C_, C_) else None
+        run = lambda: ops.spconv_i8(q1, nmap, mask, w, ws, b, 0.01, ops.EPI_SILU_Q8, 0.02, count=cnt, packed=wp,
+                                    tensor_cores=wp is not None)
+        run()
         torch.cuda.synchronize()
         tms = []
         for _ in range(reps):
             flush.zero_()
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
-            ops.spconv_i8(q1, nmap, mask, w, ws, b, 0.01, ops.EPI_SILU_Q8, 0.02, count=cnt)
+            run()
             e.record()
             torch.cuda.synchronize()
             tms.append(s.elapsed_time(e))

@@ -28,7 +28,7 @@ class RefinerConfig(C.Structure):
     _fields_ = [("batch", I32), ("height", I32), ("width", I32), ("levels", I32), ("channels", I32 * 8),
                 ("enc_channels", I32), ("lidar_h", I32), ("lidar_w", I32), ("depth_resolution", F32),
                 ("soft_gate", I32), ("fit_iters", I32), ("fit_trim", F32), ("fit_min_points", I32),
-                ("use_prompt", I32), ("capacity", I64 * 8)]
+                ("use_prompt", I32), ("capacity", I64 * 8), ("use_tensor_cores", I32)]
 
 
 # name -> (restype, argtypes)
@@ -45,8 +45,9 @@ SIGNATURES = {
     "pmg_nmap_hash_workspace_bytes": (SZ, [I64]),
     "pmg_nmap_hash": (I32, [P, I64, C.POINTER(I64), P, I64, I32, P, P, SZ, P, P]),
     "pmg_nmap_hash_noalloc": (I32, [P, I64, C.POINTER(I64), P, I64, I32, P, P, P]),
-    "pmg_spconv_i8": (I32, [P, P, I64, P, P, I64, I32, I32, P, P, P, F32, I32, F32, P, P, P]),
-    "pmg_dense_i8": (I32, [P, P, I64, I32, I32, P, P, P, F32, I32, F32, P, P, P]),
+    "pmg_pack_weights_umma": (I32, [P, I32, I32, I32, P, P]),
+    "pmg_spconv_i8": (I32, [P, P, I64, P, P, I64, I32, I32, P, P, P, P, F32, I32, F32, P, P, P, P]),
+    "pmg_dense_i8": (I32, [P, P, I64, I32, I32, P, P, P, P, F32, I32, F32, P, P, P, P]),
     "pmg_quantize": (I32, [P, I64, F32, P, P]),
     "pmg_ln_silu_q8": (I32, [P, P, P, P, P, P, I64, I32, P, P, F32, F32, P, P]),
     "pmg_pool_mean_q8": (I32, [P, P, P, P, I64, I32, F32, P, P]),
@@ -77,7 +78,8 @@ SIGNATURES = {
 }
 
 STATUS = {0: "ok", 1: "bad argument", 2: "CUDA runtime error", 3: "hash table full", 4: "level capacity overflow",
-          5: "unsupported configuration", 6: "coordinate outside the key range", 7: "no sm_100 device"}
+          5: "unsupported configuration", 6: "coordinate outside the key range", 7: "no sm_100 device",
+          8: "bounded wait expired inside a kernel"}
 
 EPI_ACC32, EPI_F32, EPI_F32_RESID, EPI_SILU_Q8 = 0, 1, 2, 3
 

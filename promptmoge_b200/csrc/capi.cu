@@ -18,6 +18,7 @@ extern "C" const char* pmg_status_string(int status) {
         case PMG_ERR_UNSUPPORTED: return "unsupported configuration";
         case PMG_ERR_RANGE: return "coordinate outside the key range";
         case PMG_ERR_NO_DEVICE: return "no sm_100 device";
+        case PMG_ERR_TIMEOUT: return "bounded wait expired inside a kernel";
         default: return "unknown status";
     }
 }

@@ -52,7 +52,7 @@ __global__ void __launch_bounds__(kThreads) k_gemm_i8_simt(const int8_t* __restr
     const int64_t M = rows_of(count, max_rows);
     const int tid = threadIdx.x;
     const int rg = tid >> 4, cg = tid & 15;
-    const int kc = Ci < kKC ? Ci : kKC;
+    const int kc = Ci <= kKC ? Ci : (Ci % kKC == 0 ? kKC : (Ci % 32 == 0 ? 32 : 16));
     const int kv = kc / 16;   // 16-byte vectors per row chunk
 
     for (int64_t m0 = (int64_t)blockIdx.x * kTM; m0 < M; m0 += (int64_t)gridDim.x * kTM) {
@@ -136,7 +136,6 @@ static int launch_i8(const int8_t* in, const int32_t* nmap, int64_t ld, const ui
 
 int gemm_i8_simt(const int8_t* in, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask, const int32_t* count,
                  int64_t max_rows, int Ci, int Co, int taps, const int8_t* w, const Epi& e, cudaStream_t s) {
-    if (Ci > kKC && Ci % kKC) return PMG_ERR_UNSUPPORTED;
     switch (Co) {
         case 16: return launch_i8<16>(in, nmap, ld, tile_mask, count, max_rows, Ci, taps, w, e, s);
         case 32: return launch_i8<32>(in, nmap, ld, tile_mask, count, max_rows, Ci, taps, w, e, s);
@@ -148,9 +147,11 @@ int gemm_i8_simt(const int8_t* in, const int32_t* nmap, int64_t ld, const uint32
 }
 
 int gemm_i8(const int8_t* in, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask, const int32_t* count,
-            int64_t max_rows, int Ci, int Co, int taps, const int8_t* w, const Epi& e, cudaStream_t s) {
-    const int rc = gemm_i8_tc(in, nmap, ld, tile_mask, count, max_rows, Ci, Co, taps, w, e, s);
-    if (rc != PMG_ERR_UNSUPPORTED) return rc;
+            int64_t max_rows, int Ci, int Co, int taps, const int8_t* w, const int8_t* w_packed, const Epi& e,
+            cudaStream_t s) {
+    if (w_packed && tc_supported(Ci, Co))
+        return gemm_i8_tc(in, nmap, ld, tile_mask, count, max_rows, Ci, Co, taps, w_packed, e, s);
+    if (!w) return PMG_ERR_UNSUPPORTED;
     return gemm_i8_simt(in, nmap, ld, tile_mask, count, max_rows, Ci, Co, taps, w, e, s);
 }
 
@@ -217,25 +218,29 @@ static bool mode_ok(int mode) { return mode >= PMG_EPI_ACC32 && mode <= PMG_EPI_
 
 extern "C" int pmg_spconv_i8(const int8_t* in_q8, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask,
                              const int32_t* count, int64_t max_rows, int32_t Ci, int32_t Co, const int8_t* weight,
-                             const float* w_scale, const float* bias, float act_scale, int32_t epilogue,
-                             float out_scale, const float* resid, void* out, void* stream) {
-    if (!in_q8 || !nmap || !weight || !out || max_rows < 0 || ld < max_rows || !mode_ok(epilogue)) return PMG_ERR_BAD_ARG;
+                             const int8_t* weight_packed, const float* w_scale, const float* bias, float act_scale,
+                             int32_t epilogue, float out_scale, const float* resid, void* out, int32_t* status,
+                             void* stream) {
+    if (!in_q8 || !nmap || (!weight && !weight_packed) || !out || max_rows < 0 || ld < max_rows || !mode_ok(epilogue))
+        return PMG_ERR_BAD_ARG;
     if (Ci % 16 || Co % 16 || Ci <= 0 || Co <= 0 || Ci > 1024 || Co > 256) return PMG_ERR_BAD_ARG;
     if (epilogue != PMG_EPI_ACC32 && (!w_scale || !bias)) return PMG_ERR_BAD_ARG;
     if (epilogue == PMG_EPI_F32_RESID && !resid) return PMG_ERR_BAD_ARG;
-    Epi e{epilogue, act_scale, out_scale, w_scale, bias, resid, out};
-    return gemm_i8(in_q8, nmap, ld, tile_mask, count, max_rows, Ci, Co, 27, weight, e, as_stream(stream));
+    Epi e{epilogue, act_scale, out_scale, w_scale, bias, resid, out, status};
+    return gemm_i8(in_q8, nmap, ld, tile_mask, count, max_rows, Ci, Co, 27, weight, weight_packed, e,
+                   as_stream(stream));
 }
 
 extern "C" int pmg_dense_i8(const int8_t* a_q8, const int32_t* count, int64_t max_rows, int32_t K, int32_t N,
-                            const int8_t* weight, const float* w_scale, const float* bias, float act_scale,
-                            int32_t epilogue, float out_scale, const float* resid, void* out, void* stream) {
-    if (!a_q8 || !weight || !out || max_rows < 0 || !mode_ok(epilogue)) return PMG_ERR_BAD_ARG;
+                            const int8_t* weight, const int8_t* weight_packed, const float* w_scale, const float* bias,
+                            float act_scale, int32_t epilogue, float out_scale, const float* resid, void* out,
+                            int32_t* status, void* stream) {
+    if (!a_q8 || (!weight && !weight_packed) || !out || max_rows < 0 || !mode_ok(epilogue)) return PMG_ERR_BAD_ARG;
     if (K % 16 || N % 16 || K <= 0 || N <= 0 || N > 256) return PMG_ERR_BAD_ARG;
     if (epilogue != PMG_EPI_ACC32 && (!w_scale || !bias)) return PMG_ERR_BAD_ARG;
     if (epilogue == PMG_EPI_F32_RESID && !resid) return PMG_ERR_BAD_ARG;
-    Epi e{epilogue, act_scale, out_scale, w_scale, bias, resid, out};
-    return gemm_i8(a_q8, nullptr, 0, nullptr, count, max_rows, K, N, 1, weight, e, as_stream(stream));
+    Epi e{epilogue, act_scale, out_scale, w_scale, bias, resid, out, status};
+    return gemm_i8(a_q8, nullptr, 0, nullptr, count, max_rows, K, N, 1, weight, weight_packed, e, as_stream(stream));
 }
 
 extern "C" int pmg_spconv_f32(const float* in, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask,

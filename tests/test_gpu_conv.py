@@ -38,8 +38,12 @@ def _mask(nmap_rm: np.ndarray):
     return torch.from_numpy(out.astype(np.uint32).view(np.int32)).cuda()
 
 
+TC = [pytest.param(False, id="simt"), pytest.param(True, id="tcgen05")]
+
+
+@pytest.mark.parametrize("tc", TC)
 @pytest.mark.parametrize("name", SMALL)
-def test_every_layer_accumulator_bit_exact(golden, name):
+def test_every_layer_accumulator_bit_exact(golden, name, tc):
     """Given the reference's int8 input of each of the 25/31 quantised layers, the GPU's int32 accumulators hash to
     the reference's exact accumulators, and each epilogue equals the oracle's fp32 arithmetic bit for bit."""
     from promptmoge_b200 import ops
@@ -48,23 +52,24 @@ def test_every_layer_accumulator_bit_exact(golden, name):
     widths = _widths(g)
     L = len(widths)
     w = g.weights()
+    status = torch.zeros(1, dtype=torch.int32).cuda()
     for n in g.layer_names(0):
         key = f"s0_Q_{n}"
         q = torch.from_numpy(g[key + "_q"]).cuda()
         qw, sw = quantise_weight(w[n + ".weight"])
         bias = w[n + ".bias"]
         sa = act_scale(g.clips[n])
+        ep = (torch.from_numpy(sw).cuda(), torch.from_numpy(bias).cuda(), sa, ops.EPI_F32)
         if ".conv" in n:
             nm = g[f"s0_L{_level_for_conv(n, L)}_nmap"]
             tm, mask = _tap_major(nm), _mask(nm)
             wt = torch.from_numpy(np.ascontiguousarray(qw.reshape(qw.shape[0], 27, -1).transpose(1, 0, 2))).cuda()
-            acc = ops.spconv_i8(q, tm, mask, wt)
-            f32 = ops.spconv_i8(q, tm, mask, wt, torch.from_numpy(sw).cuda(), torch.from_numpy(bias).cuda(), sa,
-                                ops.EPI_F32)
+            acc = ops.spconv_i8(q, tm, mask, wt, tensor_cores=tc, status=status)
+            f32 = ops.spconv_i8(q, tm, mask, wt, *ep, tensor_cores=tc, status=status)
         else:
             wt = torch.from_numpy(qw).cuda()
-            acc = ops.dense_i8(q, wt)
-            f32 = ops.dense_i8(q, wt, torch.from_numpy(sw).cuda(), torch.from_numpy(bias).cuda(), sa, ops.EPI_F32)
+            acc = ops.dense_i8(q, wt, tensor_cores=tc, status=status)
+            f32 = ops.dense_i8(q, wt, *ep, tensor_cores=tc, status=status)
         torch.cuda.synchronize()
         acc_np = acc.cpu().numpy()
         assert sha(acc_np) == g.digests[key + "_acc"], n
@@ -73,9 +78,11 @@ def test_every_layer_accumulator_bit_exact(golden, name):
         rows = g[key + "_rows"]
         yr = g[key + "_y_rows"]
         assert np.abs(f32.cpu().numpy()[rows] - yr).max() <= 1e-3 * np.abs(yr).max(), n
+    assert int(status.item()) == 0
 
 
-def test_fused_epilogues_match_oracle(golden):
+@pytest.mark.parametrize("tc", TC)
+def test_fused_epilogues_match_oracle(golden, tc):
     from promptmoge_b200 import ops
     from promptmoge_b200.engine import act_scale, quantise_weight
     g = golden("A_small")
@@ -88,20 +95,40 @@ def test_fused_epilogues_match_oracle(golden):
     wt = torch.from_numpy(np.ascontiguousarray(qw.reshape(qw.shape[0], 27, -1).transpose(1, 0, 2))).cuda()
     sa, s_next = act_scale(g.clips[n1]), act_scale(g.clips[n2])
     args = (torch.from_numpy(sw).cuda(), torch.from_numpy(w[n1 + ".bias"]).cuda(), sa)
-    acc = ops.spconv_i8(q, tm, mask, wt).cpu().numpy().astype(np.int64)
+    acc = ops.spconv_i8(q, tm, mask, wt, tensor_cores=tc).cpu().numpy().astype(np.int64)
     y = oref.dequant(acc, sa, sw, w[n1 + ".bias"])
-    q8 = ops.spconv_i8(q, tm, mask, wt, *args, ops.EPI_SILU_Q8, s_next).cpu().numpy()
+    q8 = ops.spconv_i8(q, tm, mask, wt, *args, ops.EPI_SILU_Q8, s_next, tensor_cores=tc).cpu().numpy()
     want = np.clip(np.rint(oref.silu(y) / np.float32(s_next)), -127, 127).astype(np.int8)
     # SiLU's exp may differ by an ulp between CUDA and numpy: allow rare one-step flips, nothing larger.
     d = np.abs(q8.astype(np.int32) - want.astype(np.int32))
     assert d.max() <= 1 and (d > 0).mean() < 1e-3
     resid = torch.randn(acc.shape, generator=torch.Generator().manual_seed(0)).cuda()
-    r = ops.spconv_i8(q, tm, mask, wt, *args, ops.EPI_F32_RESID, 1.0, resid).cpu().numpy()
+    r = ops.spconv_i8(q, tm, mask, wt, *args, ops.EPI_F32_RESID, 1.0, resid, tensor_cores=tc).cpu().numpy()
     np.testing.assert_array_equal(r, (y + resid.cpu().numpy()).astype(np.float32))
 
 
+def test_tensor_core_path_equals_simt_path(golden):
+    """The two int8 paths agree bit for bit on every epilogue (same accumulators, same epilogue arithmetic)."""
+    from promptmoge_b200 import ops
+    g = golden("A_small")
+    nm = g["s0_L2_nmap"]
+    tm, mask = _tap_major(nm), _mask(nm)
+    rng = np.random.default_rng(7)
+    C = 128
+    q = torch.from_numpy(rng.integers(-127, 128, (nm.shape[0], C)).astype(np.int8)).cuda()
+    wt = torch.from_numpy(rng.integers(-127, 128, (27, C, C)).astype(np.int8)).cuda()
+    ws = torch.from_numpy(rng.uniform(1e-4, 1e-3, C).astype(np.float32)).cuda()
+    b = torch.from_numpy(rng.standard_normal(C).astype(np.float32)).cuda()
+    resid = torch.from_numpy(rng.standard_normal((nm.shape[0], C)).astype(np.float32)).cuda()
+    for mode in (ops.EPI_ACC32, ops.EPI_F32, ops.EPI_F32_RESID, ops.EPI_SILU_Q8):
+        a = ops.spconv_i8(q, tm, mask, wt, ws, b, 0.03, mode, 0.05, resid, tensor_cores=False)
+        t = ops.spconv_i8(q, tm, mask, wt, ws, b, 0.03, mode, 0.05, resid, tensor_cores=True)
+        assert torch.equal(a, t), mode
+
+
+@pytest.mark.parametrize("tc", TC)
 @pytest.mark.parametrize("name", ["conv_20k_c32", "conv_100k_c16"])
-def test_conv_sweep_accumulators(golden, name):
+def test_conv_sweep_accumulators(golden, name, tc):
     from promptmoge_b200 import ops, synth
     g = golden(name)
     c = g.config
@@ -111,13 +138,14 @@ def test_conv_sweep_accumulators(golden, name):
     q = rng.integers(-127, 128, (coords.shape[0], c["C"])).astype(np.int8)
     qw = rng.integers(-127, 128, (c["C"], 3, 3, 3, c["C"])).astype(np.int8)
     wt = torch.from_numpy(np.ascontiguousarray(qw.reshape(c["C"], 27, c["C"]).transpose(1, 0, 2))).cuda()
-    acc = ops.spconv_i8(torch.from_numpy(q).cuda(), nm_tm, mask, wt)
+    acc = ops.spconv_i8(torch.from_numpy(q).cuda(), nm_tm, mask, wt, tensor_cores=tc)
     torch.cuda.synchronize()
     assert sha(acc.cpu().numpy()) == str(g["acc_sha"])
 
 
+@pytest.mark.parametrize("tc", TC)
 @pytest.mark.parametrize("C", [16, 32, 64, 128, 256])
-def test_conv_all_widths_against_oracle(C):
+def test_conv_all_widths_against_oracle(C, tc):
     """Every channel width, random int8 data, with and without tile masks (all-taps path)."""
     from promptmoge_b200 import ops, synth
     from oracle import structure as ost
@@ -131,31 +159,33 @@ def test_conv_all_widths_against_oracle(C):
     wt = torch.from_numpy(np.ascontiguousarray(qw.reshape(C, 27, C).transpose(1, 0, 2))).cuda()
     want = oref.conv_acc(q, ost.nmap_sorted(coords_np, ext), qw)
     for m in (mask, None):
-        got = ops.spconv_i8(torch.from_numpy(q).cuda(), tm, m, wt).cpu().numpy()
+        got = ops.spconv_i8(torch.from_numpy(q).cuda(), tm, m, wt, tensor_cores=tc).cpu().numpy()
         np.testing.assert_array_equal(got.astype(np.int64), want)
 
 
+@pytest.mark.parametrize("tc", TC)
 @pytest.mark.parametrize("K,N", [(32, 64), (64, 128), (128, 256), (256, 256), (256, 128), (128, 64), (64, 32),
-                                 (1024, 256), (512, 256)])
-def test_dense_shapes_against_oracle(K, N):
+                                 (1024, 256), (512, 256), (96, 32)])
+def test_dense_shapes_against_oracle(K, N, tc):
     from promptmoge_b200 import ops
     rng = np.random.default_rng(K * 1000 + N)
     M = 777
     a = rng.integers(-127, 128, (M, K)).astype(np.int8)
     w = rng.integers(-127, 128, (N, K)).astype(np.int8)
-    got = ops.dense_i8(torch.from_numpy(a).cuda(), torch.from_numpy(w).cuda()).cpu().numpy()
+    got = ops.dense_i8(torch.from_numpy(a).cuda(), torch.from_numpy(w).cuda(), tensor_cores=tc).cpu().numpy()
     np.testing.assert_array_equal(got.astype(np.int64), oref.linear_acc(a, w))
 
 
-def test_count_limits_rows(golden):
+@pytest.mark.parametrize("tc", TC)
+def test_count_limits_rows(golden, tc):
     """Rows past the device-side count are not written (graph-safe sizing by capacity)."""
     from promptmoge_b200 import ops
     rng = np.random.default_rng(5)
-    a = torch.from_numpy(rng.integers(-127, 128, (256, 64)).astype(np.int8)).cuda()
+    a = torch.from_numpy(rng.integers(-127, 128, (300, 64)).astype(np.int8)).cuda()
     w = torch.from_numpy(rng.integers(-127, 128, (32, 64)).astype(np.int8)).cuda()
     cnt = torch.tensor([100], dtype=torch.int32).cuda()
-    out = ops.dense_i8(a, w, count=cnt)
-    out_full = ops.dense_i8(a, w)
+    out = ops.dense_i8(a, w, count=cnt, tensor_cores=tc)
+    out_full = ops.dense_i8(a, w, tensor_cores=tc)
     torch.cuda.synchronize()
     np.testing.assert_array_equal(out[:100].cpu().numpy(), out_full[:100].cpu().numpy())
 

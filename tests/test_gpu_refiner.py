@@ -111,3 +111,22 @@ def test_batched_frames_equal_single_frames(golden):
         _inputs(eng1, sc1)
         out1, _ = eng1.run(1)
         np.testing.assert_array_equal(out2[b], out1.cpu().numpy()[0])
+
+
+def test_tensor_core_plan_equals_simt_plan(golden):
+    """The plan with tcgen05 int8 layers and the plan with SIMT int8 layers refine to the same bits."""
+    from promptmoge_b200 import synth
+    from promptmoge_b200.engine import Geometry, RefinerEngine
+    g = golden("A_small")
+    sc = g.scene()
+    c = g.config
+    geo = Geometry(channels=synth.MODELS[c["model"]]["model_channels"], height=c["H"], width=c["W"])
+    outs = []
+    for tc in (False, True):
+        eng = RefinerEngine(g.weights(), g.clips, geo, tensor_cores=tc)
+        _inputs(eng, sc)
+        out, _ = eng.run(2)
+        assert eng.status()[0] == 0
+        outs.append(out.clone())
+        eng.close()
+    assert torch.equal(outs[0], outs[1])
