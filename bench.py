@@ -308,6 +308,34 @@ def cpu_baseline(batch=1, steps=1):
                       f"(float64-exact int8 GEMMs via BLAS on all host threads): {dt:.2f} s/step"}
 
 
+def profile_conv(args):
+    """Profiling driver (run under ncu): the real 480x640 level structure of the benchmark frame, random int8
+    activations and weights, `--steps` launches of that level's conv (fused SiLU + requantise epilogue).  Only the
+    profiled kernel is an int8 GEMM launch, so `ncu -k regex:k_gemm_i8 -s 1 -c 2` captures two warm launches."""
+    import torch
+    from promptmoge_b200 import ops, synth
+    from promptmoge_b200.levels import build_levels
+    torch.cuda.set_device(0)
+    sc = synth.make_scene(0, 480, 640, 16, 256)
+    lv, _ = build_levels(torch.from_numpy(sc.point_coord).cuda(), 5, with_coords=False)
+    k = args.profile_conv
+    C_ = synth.MODELS["A"]["model_channels"][k]
+    l = lv[k]
+    M = l["count"]
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q = torch.randint(-127, 127, (M, C_), dtype=torch.int8, device="cuda", generator=g)
+    w = torch.randint(-127, 127, (27, C_, C_), dtype=torch.int8, device="cuda", generator=g)
+    wp = ops.pack_weights_umma(w) if (ops.tc_supported(C_, C_) and not args.simt) else None
+    ws_ = torch.full((C_,), 1e-3, device="cuda")
+    b = torch.zeros(C_, device="cuda")
+    for _ in range(max(1, args.steps)):
+        ops.spconv_i8(q, l["nmap_tm"], l["mask"], w, ws_, b, 0.01, ops.EPI_SILU_Q8, 0.02, rows=M, packed=wp,
+                      tensor_cores=wp is not None)
+    torch.cuda.synchronize()
+    nnz = int((l["nmap_tm"][:, :M] >= 0).sum().item())
+    return {"profile_conv": k, "M": M, "C": C_, "occupied_taps": nnz, "path": "tcgen05" if wp is not None else "simt"}
+
+
 def run_reference(args, ws, rank):
     """Reference arm: the reference's CPU algorithm (the oracle port) on the host cores, rank 0 only."""
     if rank != 0:
@@ -349,7 +377,13 @@ def main():
     ap.add_argument("--batch", type=int, default=1, help="frames per GPU per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu", action="store_true", help="profiling mode: warm-up + timed replays only, no extras")
+    ap.add_argument("--profile-conv", type=int, default=None, metavar="LEVEL",
+                    help="profiling driver: launch one level's conv --steps times on the benchmark frame's structure")
+    ap.add_argument("--simt", action="store_true", help="with --profile-conv: the SIMT kernel instead of tcgen05")
     args = ap.parse_args()
+    if args.profile_conv is not None:
+        print(json.dumps(profile_conv(args)), flush=True)
+        return
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     if args.impl == "reference":

@@ -1,19 +1,21 @@
 // tcgen05 (5th-generation tensor core) int8 implicit-GEMM path for the submanifold conv and the dense layers.
 //
-// One persistent CTA per SM walks 128-row output tiles.  For a tile it streams (tap, K-block) items through an
-// NST-stage shared-memory ring:
-//   * warps 0-3 (128 threads, one output row each) gather the row's input voxel for the tap through the tap-major
-//     neighbour map with 16-byte cp.async (absent neighbours are zero-filled by the copy itself) into the UMMA
-//     K-major core-matrix layout (8 rows x 16 bytes contiguous; LBO = next 16 K-bytes, SBO = next 8 rows);
-//   * thread 0 also bulk-copies the matching weight block, pre-packed in global memory in the same layout, with
-//     cp.async.bulk (TMA engine) completing on the stage's mbarrier (expect_tx);
-//   * warp 4 owns the TMEM accumulator (128 lanes x Co int32 columns) and one of its threads issues
-//     tcgen05.mma.cta_group::1.kind::i8 (M = 128, N = Co, K = 32 per instruction), then tcgen05.commit to release the
-//     stage and, after the last item, to publish the accumulator;
-//   * warps 0-3 then read their 32 TMEM lanes each (tcgen05.ld 32x32b.x16) and apply the fused epilogue
-//     (dequant -> +bias -> [SiLU -> requantise] or [+residual]) with the reference's rounding, writing int8 / fp32.
-// Every mbarrier wait is bounded: on timeout the CTA records PMG_ERR_TIMEOUT in the status word, drains its copies,
-// frees its TMEM and returns.
+// One persistent CTA per SM walks 128-row output tiles (UMMA M = 128, N = Co).  A tile's work is a stream of items
+// through an NST-stage shared-memory ring; an item is K = 128 bytes: up to 128 / Ci taps of a narrow layer (4 taps at
+// Ci = 32, 2 at Ci = 64), or one 128-byte K-block of a wide one.  Warp roles:
+//   * warps 0-3 (one output row per thread) gather the row's input voxel for each tap of the item through the
+//     tap-major neighbour map with 16-byte cp.async (absent neighbours zero-filled by the copy itself);
+//   * thread 0 also bulk-copies the taps' weight blocks (packed in global memory so that per-tap blocks concatenate)
+//     with cp.async.bulk, completing on the stage's mbarrier (expect_tx);
+//   * warp 4 owns two TMEM accumulators (128 lanes x Co int32 columns each); one of its threads issues
+//     tcgen05.mma.cta_group::1.kind::i8 (K = 32 per instruction) and tcgen05.commit to release stages and to
+//     publish a finished accumulator;
+//   * warps 5-8 read their 32 TMEM lanes each (tcgen05.ld 32x32b.x16) and apply the fused epilogue (dequant ->
+//     +bias -> [SiLU -> requantise] or [+residual]) with the reference's rounding, while the next tile already
+//     accumulates into the other TMEM buffer.
+// Both operands use the K-major no-swizzle core-matrix layout with the 16-byte K chunks outermost
+// ([K/16][rows/8][8][16]; LBO = bytes between K chunks, SBO = 128).  Every mbarrier wait is bounded: on timeout the
+// CTA records PMG_ERR_TIMEOUT in the status word, drains its copies, frees its TMEM and returns.
 #include <algorithm>
 
 #include "common.cuh"
@@ -24,8 +26,7 @@ namespace pmg {
 namespace tc {
 
 constexpr int kM = 128;              // rows per tile = UMMA M
-constexpr int kProducers = 128;      // warps 0-3
-constexpr int kThreads = 160;        // + warp 4 (MMA issuer, TMEM owner)
+constexpr int kProducers = 128;      // warps 0-3 (and, as a count, the epilogue warps 5-8)
 constexpr uint32_t kSpin = 1u << 22; // bounded waits
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -120,11 +121,14 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+
 template <int CO>
 constexpr int tmem_cols() {
     return CO <= 32 ? 32 : (CO <= 64 ? 64 : (CO <= 128 ? 128 : 256));
 }
 
+// KB = K bytes per pipeline item.  Ci <= 128 with 128 % Ci == 0: several taps share an item (128 / Ci taps);
+// Ci > 128: one tap, Ci / 128 K-blocks; other Ci <= 128 (96): one tap, KB = Ci.
 template <int CO, int KB>
 struct Cfg {
     static constexpr int kA = kM * KB;                       // A bytes per stage
@@ -134,7 +138,8 @@ struct Cfg {
     static constexpr int kStages = (kBudget / kStage) > 8 ? 8 : (kBudget / kStage);
     static constexpr int kLag = kStages - 1 < 4 ? kStages - 1 : 4;
     static constexpr int kSmem = kStages * kStage + 1024 + 256;
-    static constexpr uint32_t kSbo = (KB / 16) * 128;        // bytes between 8-row groups
+    static constexpr uint32_t kLboA = (kM / 8) * 128;        // A: bytes between 16-byte K chunks
+    static constexpr uint32_t kLboB = (CO / 8) * 128;        // B: bytes between 16-byte K chunks
 };
 
 __device__ __forceinline__ void epi_store16(const Epi& e, int64_t m, int n0, int Co, const uint32_t (&r)[16]) {
@@ -181,8 +186,12 @@ __device__ __forceinline__ void epi_store16(const Epi& e, int64_t m, int n0, int
     }
 }
 
+// Warp roles: 0-3 gather A (one output row per thread) and thread 0 bulk-copies B; 4 issues MMAs and owns TMEM;
+// 5-8 run the epilogue from one of two TMEM accumulators while the next tile accumulates into the other.
+constexpr int kThreads2 = 288;
+
 template <int CO, int KB>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads2, 1)
     k_gemm_i8_tc(const int8_t* __restrict__ in, const int32_t* __restrict__ nmap, int64_t ld,
                  const uint32_t* __restrict__ tile_mask, const int32_t* __restrict__ count, int64_t max_rows, int Ci,
                  int taps, const int8_t* __restrict__ wpk, Epi e) {
@@ -195,9 +204,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + NST * C::kStage);
     uint64_t* empty = full + NST;
-    uint64_t* acc_full = empty + NST;
-    uint64_t* acc_empty = acc_full + 1;
-    uint64_t* drain = acc_empty + 1;
+    uint64_t* acc_full = empty + NST;      // [2]
+    uint64_t* acc_empty = acc_full + 2;    // [2]
+    uint64_t* drain = acc_empty + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
     __shared__ volatile int s_abort;
 
@@ -207,15 +216,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&full[s], kProducers + 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(acc_full, 1);
-        mbar_init(acc_empty, kProducers);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], kProducers);
+        }
         mbar_init(drain, 1);
         s_abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 4) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(NCOLS)
+                     "r"(2 * NCOLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -226,8 +237,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int64_t M = rows_of(count, max_rows);
     const int64_t ntiles = (M + kM - 1) / kM;
-    const int nkb = Ci / KB;
-    const int64_t wtap = (int64_t)CO * Ci;          // packed weight bytes per tap
+    const int kbw = Ci < KB ? Ci : KB;                 // K bytes of one tap inside an item
+    const int tpi = (taps == 27 && Ci < KB) ? KB / Ci : 1;   // taps per item
+    const int nkb = Ci > KB ? Ci / KB : 1;             // K-blocks per tap
+    const int64_t blk = (int64_t)CO * kbw;             // packed weight bytes per (tap, K-block)
     const uint32_t sbase = smem_u32(smem);
 
     auto tile_taps = [&](int64_t m0) -> uint32_t {
@@ -239,36 +252,53 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (m0 + 32 * g < M) mk |= tile_mask[(m0 >> 5) + g];
         return mk & 0x7ffffffu;
     };
+    // next group of up to tpi taps from the mask
+    auto take = [&](uint32_t& mk, int (&tv)[4]) -> int {
+        int nt = 0;
+        while (mk && nt < tpi) {
+            tv[nt++] = __ffs(mk) - 1;
+            mk &= mk - 1;
+        }
+        return nt;
+    };
 
     if (warp < 4) {
-        // ------------------------------------------ producers + epilogue ------------------------------------------ //
+        // --------------------------------------------- producers ---------------------------------------------- //
         const int r = threadIdx.x;
-        const uint32_t a_row_off = (uint32_t)((r >> 3) * C::kSbo + (r & 7) * 16);
-        uint32_t it = 0, tcount = 0;
+        const uint32_t a_row_off = (uint32_t)((r >> 3) * 128 + (r & 7) * 16);
+        uint32_t it = 0, pend_first = 0;
+        int pending = 0;
         bool ok = true;
-        for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++tcount) {
-            const int64_t m0 = tile * kM;
-            const int64_t row = m0 + r;
-            uint32_t mk = tile_taps(m0);
-            int pending = 0;
-            uint32_t pend_first = it;
+        for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+            const int64_t row = tile * kM + r;
+            uint32_t mk = tile_taps(tile * kM);
             while (mk && ok) {
-                const int v = __ffs(mk) - 1;
-                mk &= mk - 1;
-                int32_t idx = -1;
-                if (row < M) idx = (taps == 27) ? __ldg(nmap + (int64_t)v * ld + row) : (int32_t)row;
-                const int8_t* src_row = in + (int64_t)(idx >= 0 ? idx : 0) * Ci;
+                int tv[4];
+                const int nt = take(mk, tv);
+                int32_t idx[4];
+#pragma unroll
+                for (int g = 0; g < 4; ++g) {
+                    idx[g] = -1;
+                    if (g < nt && row < M) idx[g] = (taps == 27) ? __ldg(nmap + (int64_t)tv[g] * ld + row) : (int32_t)row;
+                }
                 for (int kb = 0; kb < nkb; ++kb) {
                     const uint32_t s = it % NST, ph = (it / NST) & 1u;
                     if (!mbar_wait(&empty[s], ph ^ 1u, &s_abort)) { ok = false; break; }
                     const uint32_t sa = sbase + s * C::kStage;
-                    const int8_t* src = src_row + kb * KB;
 #pragma unroll
-                    for (int c = 0; c < KB / 16; ++c) cp_async16(sa + a_row_off + c * 128, src + c * 16, idx >= 0);
+                    for (int g = 0; g < 4; ++g) {
+                        if (g < nt) {
+                            const int8_t* src = in + (int64_t)(idx[g] >= 0 ? idx[g] : 0) * Ci + kb * kbw;
+                            const uint32_t dst = sa + a_row_off + (uint32_t)(g * (kbw / 16)) * C::kLboA;
+                            for (int c = 0; c < kbw / 16; ++c) cp_async16(dst + c * C::kLboA, src + c * 16, idx[g] >= 0);
+                        }
+                    }
                     cp_async_commit();
                     if (threadIdx.x == 0) {
-                        mbar_arrive_expect_tx(&full[s], (uint32_t)C::kB);
-                        bulk_g2s(sa + C::kA, wpk + v * wtap + (int64_t)kb * CO * KB, (uint32_t)C::kB, &full[s]);
+                        mbar_arrive_expect_tx(&full[s], (uint32_t)(nt * blk));
+                        for (int g = 0; g < nt; ++g)
+                            bulk_g2s(sa + C::kA + (uint32_t)(g * blk), wpk + ((int64_t)tv[g] * nkb + kb) * blk,
+                                     (uint32_t)blk, &full[s]);
                     }
                     ++it;
                     ++pending;
@@ -281,54 +311,43 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
             }
-            cp_async_wait<0>();
-            fence_proxy_async();
-            while (pending > 0) {
-                mbar_arrive(&full[pend_first % NST]);
-                ++pend_first;
-                --pending;
-            }
-            if (!ok) break;
-            // epilogue: this warp's 32 TMEM lanes = rows m0 + 32*warp + lane
-            if (!mbar_wait(acc_full, tcount & 1u, &s_abort)) { ok = false; break; }
-            tc_fence_after();
-            const int64_t m = m0 + 32 * warp + lane;
-#pragma unroll 1
-            for (int j = 0; j < CO / 16; ++j) {
-                uint32_t acc[16];
-                tmem_ld16(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(j * 16), acc);
-                if (m < M) epi_store16(e, m, j * 16, CO, acc);
-            }
-            tc_fence_before();
-            mbar_arrive(acc_empty);
+        }
+        cp_async_wait<0>();
+        fence_proxy_async();
+        while (pending > 0) {
+            mbar_arrive(&full[pend_first % NST]);
+            ++pend_first;
+            --pending;
         }
         if (!ok) {
             s_abort = 1;
             flag(e.status, PMG_ERR_TIMEOUT);
         }
-        cp_async_wait<0>();
-    } else {
-        // ------------------------------------------ MMA issuer (warp 4) ------------------------------------------- //
-        uint32_t it = 0, tcount = 0;
-        bool ok = true;
+    } else if (warp == 4) {
+        // ------------------------------------------- MMA issuer ----------------------------------------------- //
         if (lane == 0) {
-            for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++tcount) {
+            uint32_t it = 0, t = 0;
+            bool ok = true;
+            for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++t) {
+                const uint32_t b = t & 1u;
                 uint32_t mk = tile_taps(tile * kM);
-                if (!mbar_wait(acc_empty, (tcount & 1u) ^ 1u, &s_abort)) { ok = false; break; }
+                if (!mbar_wait(&acc_empty[b], ((t >> 1) & 1u) ^ 1u, &s_abort)) { ok = false; break; }
                 tc_fence_after();
+                const uint32_t d = tmem + b * NCOLS;
                 uint32_t accumulate = 0;
                 while (mk && ok) {
-                    mk &= mk - 1;
+                    int tv[4];
+                    const int nt = take(mk, tv);
+                    const int ksteps = nt * kbw / 32;
                     for (int kb = 0; kb < nkb; ++kb) {
                         const uint32_t s = it % NST, ph = (it / NST) & 1u;
                         if (!mbar_wait(&full[s], ph, &s_abort)) { ok = false; break; }
                         tc_fence_after();
                         const uint32_t sa = sbase + s * C::kStage;
-#pragma unroll
-                        for (int kk = 0; kk < KB / 32; ++kk) {
-                            const uint64_t ad = smem_desc(sa + kk * 256, 128, C::kSbo);
-                            const uint64_t bd = smem_desc(sa + C::kA + kk * 256, 128, C::kSbo);
-                            mma_i8(tmem, ad, bd, IDESC, accumulate);
+                        for (int kk = 0; kk < ksteps; ++kk) {
+                            const uint64_t ad = smem_desc(sa + 2 * kk * C::kLboA, C::kLboA, 128);
+                            const uint64_t bd = smem_desc(sa + C::kA + 2 * kk * C::kLboB, C::kLboB, 128);
+                            mma_i8(d, ad, bd, IDESC, accumulate);
                             accumulate = 1;
                         }
                         mma_commit(&empty[s]);
@@ -336,24 +355,46 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 if (!ok) break;
-                mma_commit(acc_full);
+                mma_commit(&acc_full[b]);
             }
             if (!ok) {
                 s_abort = 1;
                 flag(e.status, PMG_ERR_TIMEOUT);
-                // let every MMA already issued retire before the TMEM is released (bounded)
                 mma_commit(drain);
                 for (uint32_t i = 0; i < kSpin && !mbar_try_wait(drain, 0); ++i) {
                 }
             }
         }
         __syncwarp();
+    } else {
+        // -------------------------------------------- epilogue ------------------------------------------------ //
+        const int q = warp & 3;                         // TMEM lane quarter this warp may access
+        uint32_t t = 0;
+        bool ok = true;
+        for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++t) {
+            const uint32_t b = t & 1u;
+            if (!mbar_wait(&acc_full[b], (t >> 1) & 1u, &s_abort)) { ok = false; break; }
+            tc_fence_after();
+            const int64_t m = tile * kM + 32 * q + lane;
+#pragma unroll 1
+            for (int j = 0; j < CO / 16; ++j) {
+                uint32_t acc[16];
+                tmem_ld16(tmem + b * NCOLS + ((uint32_t)(32 * q) << 16) + (uint32_t)(j * 16), acc);
+                if (m < M) epi_store16(e, m, j * 16, CO, acc);
+            }
+            tc_fence_before();
+            mbar_arrive(&acc_empty[b]);
+        }
+        if (!ok) {
+            s_abort = 1;
+            flag(e.status, PMG_ERR_TIMEOUT);
+        }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 4) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(NCOLS) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * NCOLS) : "memory");
     }
 }
 
@@ -373,13 +414,14 @@ static int launch_tc(const int8_t* in, const int32_t* nmap, int64_t ld, const ui
     const int64_t tiles = (max_rows + tc::kM - 1) / tc::kM;
     const int grid = (int)std::min<int64_t>(tiles, (int64_t)kNumSMs);
     if (grid <= 0) return PMG_OK;
-    tc::k_gemm_i8_tc<CO, KB><<<grid, tc::kThreads, C::kSmem, s>>>(in, nmap, ld, tile_mask, count, max_rows, Ci, taps,
-                                                                   wpk, e);
+    tc::k_gemm_i8_tc<CO, KB><<<grid, tc::kThreads2, C::kSmem, s>>>(in, nmap, ld, tile_mask, count, max_rows, Ci, taps,
+                                                                    wpk, e);
     PMG_LAUNCH_CHECK();
     return PMG_OK;
 }
 
-// Shapes the tensor-core path covers: Co in {32, 64, 128, 256}, Ci a multiple of 32 (K-block = min(Ci, 128)).
+// Shapes the tensor-core path covers: Co in {32, 64, 128, 256}; Ci a multiple of 32 that divides 128, is <= 128, or
+// is a multiple of 128.
 bool tc_supported(int Ci, int Co) {
     if (!(Co == 32 || Co == 64 || Co == 128 || Co == 256)) return false;
     if (Ci < 32 || Ci % 32) return false;
@@ -387,7 +429,8 @@ bool tc_supported(int Ci, int Co) {
     return true;
 }
 
-int tc_kblock(int Ci) { return Ci <= 128 ? Ci : 128; }
+// K bytes per pipeline item (see Cfg).
+int tc_kblock(int Ci) { return (Ci > 128 || 128 % Ci == 0) ? 128 : Ci; }
 
 int gemm_i8_tc(const int8_t* in, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask, const int32_t* count,
                int64_t max_rows, int Ci, int Co, int taps, const int8_t* wpk, const Epi& e, cudaStream_t s) {
@@ -395,25 +438,27 @@ int gemm_i8_tc(const int8_t* in, const int32_t* nmap, int64_t ld, const uint32_t
     const int kb = tc_kblock(Ci);
 #define PMG_TC_CASE(CO_, KB_)                                                                            \
     if (Co == CO_ && kb == KB_) return launch_tc<CO_, KB_>(in, nmap, ld, tile_mask, count, max_rows, Ci, taps, wpk, e, s);
-    PMG_TC_CASE(32, 32) PMG_TC_CASE(32, 64) PMG_TC_CASE(32, 96) PMG_TC_CASE(32, 128)
-    PMG_TC_CASE(64, 32) PMG_TC_CASE(64, 64) PMG_TC_CASE(64, 96) PMG_TC_CASE(64, 128)
-    PMG_TC_CASE(128, 32) PMG_TC_CASE(128, 64) PMG_TC_CASE(128, 96) PMG_TC_CASE(128, 128)
-    PMG_TC_CASE(256, 32) PMG_TC_CASE(256, 64) PMG_TC_CASE(256, 96) PMG_TC_CASE(256, 128)
+    PMG_TC_CASE(32, 96) PMG_TC_CASE(32, 128)
+    PMG_TC_CASE(64, 96) PMG_TC_CASE(64, 128)
+    PMG_TC_CASE(128, 96) PMG_TC_CASE(128, 128)
+    PMG_TC_CASE(256, 96) PMG_TC_CASE(256, 128)
 #undef PMG_TC_CASE
     return PMG_ERR_UNSUPPORTED;
 }
 
-// Packed weight layout for the tensor-core path: per tap, per K-block of KB bytes, the Co x KB block in UMMA K-major
-// core-matrix order [Co/8][KB/16][8 rows][16 bytes], so one contiguous bulk copy fills a stage.
-__global__ void k_pack_umma(const int8_t* __restrict__ w, int taps, int Co, int Ci, int KB, int8_t* __restrict__ out) {
+// Packed weight layout for the tensor-core path: per tap and K-block of kbw = min(Ci, KB) bytes, the Co x kbw block
+// with its 16-byte K chunks outermost: [kbw/16][Co/8][8 rows][16 bytes].  Blocks of consecutive taps concatenate
+// into a valid operand for an item that groups several taps.
+__global__ void k_pack_umma(const int8_t* __restrict__ w, int taps, int Co, int Ci, int kbw, int8_t* __restrict__ out) {
     const int64_t total = (int64_t)taps * Co * Ci;
+    const int nkb = Ci / kbw;
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
         const int v = (int)(e / ((int64_t)Co * Ci));
         const int rem = (int)(e - (int64_t)v * Co * Ci);
         const int n = rem / Ci, k = rem - (rem / Ci) * Ci;
-        const int kb = k / KB, kk = k - kb * KB;
-        const int64_t dst = (int64_t)v * Co * Ci + (int64_t)kb * Co * KB +
-                            ((int64_t)(n >> 3) * (KB / 16) + (kk >> 4)) * 128 + (n & 7) * 16 + (kk & 15);
+        const int kb = k / kbw, kk = k - kb * kbw;
+        const int64_t dst = ((int64_t)v * nkb + kb) * Co * kbw + ((int64_t)(kk >> 4) * (Co / 8) + (n >> 3)) * 128 +
+                            (n & 7) * 16 + (kk & 15);
         out[dst] = w[e];
     }
 }
@@ -424,8 +469,9 @@ extern "C" int pmg_pack_weights_umma(const int8_t* w, int32_t taps, int32_t Co, 
                                      void* stream) {
     if (!w || !packed || taps <= 0 || !pmg::tc_supported(Ci, Co)) return PMG_ERR_BAD_ARG;
     const int64_t total = (int64_t)taps * Co * Ci;
+    const int kbw = Ci < pmg::tc_kblock(Ci) ? Ci : pmg::tc_kblock(Ci);
     pmg::k_pack_umma<<<(int)std::min<int64_t>((total + 255) / 256, 4096), 256, 0, pmg::as_stream(stream)>>>(
-        w, taps, Co, Ci, pmg::tc_kblock(Ci), packed);
+        w, taps, Co, Ci, kbw, packed);
     PMG_LAUNCH_CHECK();
     return PMG_OK;
 }
