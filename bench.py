@@ -135,21 +135,24 @@ def dominant_conv(torch, eng, reps: int = 20):
         ws = torch.full((C_,), 1e-3, device="cuda")
         b = torch.zeros(C_, device="cuda")
         nnz = int((nmap[:, :M] >= 0).sum().item())
-        wp = ops.pack_weights_umma(w) if ops.tc_supported(C_, C_) else None
-        run = lambda: ops.spconv_i8(q1, nmap, mask, w, ws, b, 0.01, ops.EPI_SILU_Q8, 0.02, count=cnt, packed=wp,
-                                    tensor_cores=wp is not None)
-        run()
-        torch.cuda.synchronize()
-        tms = []
-        for _ in range(reps):
-            flush.zero_()
-            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s.record()
-            run()
-            e.record()
+        tc = bool(eng.tensor_cores) and ops.tc_supported(C_, C_)
+        run = lambda: ops.spconv_i8(q1, nmap, mask, w, ws, b, 0.01, ops.EPI_SILU_Q8, 0.02, count=cnt,
+                                    tensor_cores=tc)
+
+        def timed(fn):
+            fn()
             torch.cuda.synchronize()
-            tms.append(s.elapsed_time(e))
-        t = float(np.median(tms))
+            tms = []
+            for _ in range(reps):
+                flush.zero_()
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+                fn()
+                e.record()
+                torch.cuda.synchronize()
+                tms.append(s.elapsed_time(e))
+            return float(np.median(tms))
+        t = timed(run)
         ops_ = 2.0 * nnz * C_ * C_
         byts = M * C_ + M * C_ + 27 * 4 * M + 27 * C_ * C_
         # this level's convs per step: 2 down + 2 up (4 at L<L-1), 2 down + 2 bottleneck at the last level
@@ -311,7 +314,7 @@ def cpu_baseline(batch=1, steps=1):
 def profile_conv(args):
     """Profiling driver (run under ncu): the real 480x640 level structure of the benchmark frame, random int8
     activations and weights, `--steps` launches of that level's conv (fused SiLU + requantise epilogue).  Only the
-    profiled kernel is an int8 GEMM launch, so `ncu -k regex:k_gemm_i8 -s 1 -c 2` captures two warm launches."""
+    profiled kernels are int8 GEMM launches, so `ncu -k regex:k_gemm -s 1 -c 2` captures two warm launches."""
     import torch
     from promptmoge_b200 import ops, synth
     from promptmoge_b200.levels import build_levels
@@ -325,15 +328,15 @@ def profile_conv(args):
     g = torch.Generator(device="cuda").manual_seed(0)
     q = torch.randint(-127, 127, (M, C_), dtype=torch.int8, device="cuda", generator=g)
     w = torch.randint(-127, 127, (27, C_, C_), dtype=torch.int8, device="cuda", generator=g)
-    wp = ops.pack_weights_umma(w) if (ops.tc_supported(C_, C_) and not args.simt) else None
+    tc_path = ops.tc_supported(C_, C_) and not args.simt
     ws_ = torch.full((C_,), 1e-3, device="cuda")
     b = torch.zeros(C_, device="cuda")
     for _ in range(max(1, args.steps)):
-        ops.spconv_i8(q, l["nmap_tm"], l["mask"], w, ws_, b, 0.01, ops.EPI_SILU_Q8, 0.02, rows=M, packed=wp,
-                      tensor_cores=wp is not None)
+        ops.spconv_i8(q, l["nmap_tm"], l["mask"], w, ws_, b, 0.01, ops.EPI_SILU_Q8, 0.02, rows=M,
+                      tensor_cores=tc_path)
     torch.cuda.synchronize()
     nnz = int((l["nmap_tm"][:, :M] >= 0).sum().item())
-    return {"profile_conv": k, "M": M, "C": C_, "occupied_taps": nnz, "path": "tcgen05" if wp is not None else "simt"}
+    return {"profile_conv": k, "M": M, "C": C_, "occupied_taps": nnz, "path": "tcgen05" if tc_path else "simt"}
 
 
 def run_reference(args, ws, rank):

@@ -125,30 +125,29 @@ int pmg_nmap_hash_noalloc(const int32_t* coords, int64_t M, const int64_t* exten
  * with q(x, s) = clamp(rint(x / s), -127, 127) and fp32 round-to-nearest at every step (no fused multiply-add). */
 enum pmg_epilogue { PMG_EPI_ACC32 = 0, PMG_EPI_F32 = 1, PMG_EPI_F32_RESID = 2, PMG_EPI_SILU_Q8 = 3 };
 
-/* Repack int8 weights [taps][Co][Ci] (conv: tap-major; dense: taps = 1, [N][K]) for the tcgen05 path: per tap and
- * K-block of min(Ci, 128) bytes, a Co x KB block in UMMA K-major core-matrix order [Co/8][KB/16][8][16].  Same byte
- * count as the input.  Co in {32, 64, 128, 256}; Ci a multiple of 32 (and of 128 above 128). */
-int pmg_pack_weights_umma(const int8_t* weight, int32_t taps, int32_t Co, int32_t Ci, int8_t* packed, void* stream);
+/* Flags of the int8 layers. */
+enum pmg_flags { PMG_FLAG_SIMT = 1 /* force the SIMT dp4a kernel instead of the tcgen05 tensor-core kernel */ };
 
 /* Submanifold 3x3x3 conv, int8 x int8 -> int32.  Replaces submanifold_conv (_core.py:399-441) under the QAT
- * quantisers (moge/model/modules/qat.py:40-115).  in_q8 [M_in,Ci], weight tap-major [27][Co][Ci] int8 (the
+ * quantisers (moge/model/modules/qat.py:40-115).  in_q8 [in_rows,Ci], weight tap-major [27][Co][Ci] int8 (the
  * reference's (Co,3,3,3,Ci) weight with the tap axis moved first), w_scale/bias [Co] fp32, nmap tap-major
  * [27][ld] over `count` output rows, tile_mask per 32 rows (NULL = all taps).  Ci, Co multiples of 16, <= 256.
- * When `weight_packed` (pmg_pack_weights_umma) is given and the shape is covered, the tcgen05 tensor-core kernel
- * runs (int32 accumulators in TMEM); otherwise the SIMT dp4a kernel over `weight`.  Both give identical results.
- * `status` (may be NULL) receives PMG_ERR_TIMEOUT if a bounded wait of the tensor-core kernel expires. */
-int pmg_spconv_i8(const int8_t* in_q8, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask,
+ * Co in {32, 64, 128, 256} with Ci in {32, 64} or a multiple of 128 runs the tcgen05 tensor-core kernel (cp.async
+ * gather of the neighbour rows, int32 accumulators in TMEM) unless flags has PMG_FLAG_SIMT; other shapes run the
+ * SIMT dp4a kernel.  Both give identical results.  `status` (may be NULL) receives PMG_ERR_TIMEOUT if a bounded wait of the
+ * tensor-core kernel expires.  Pointers must be 16-byte aligned. */
+int pmg_spconv_i8(const int8_t* in_q8, int64_t in_rows, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask,
                   const int32_t* count, int64_t max_rows, int32_t Ci, int32_t Co, const int8_t* weight,
-                  const int8_t* weight_packed, const float* w_scale, const float* bias, float act_scale,
-                  int32_t epilogue, float out_scale, const float* resid, void* out, int32_t* status, void* stream);
+                  const float* w_scale, const float* bias, float act_scale, int32_t epilogue, float out_scale,
+                  const float* resid, void* out, int32_t flags, int32_t* status, void* stream);
 
 /* Dense int8 layer: out = epilogue(A[M,K] . W[N,K]^T).  Replaces the QAT nn.Linear layers of the refiner
  * (pool/up projections, encoder_fuse, fuse_proj; sparse_unet.py:81-87, flex_sparse_blocks.py:78-105).
- * weight_packed as for pmg_spconv_i8 (taps = 1). */
+ * Kernel choice and flags as for pmg_spconv_i8 (K plays Ci, N plays Co). */
 int pmg_dense_i8(const int8_t* a_q8, const int32_t* count, int64_t max_rows, int32_t K, int32_t N,
-                 const int8_t* weight, const int8_t* weight_packed, const float* w_scale, const float* bias,
-                 float act_scale, int32_t epilogue, float out_scale, const float* resid, void* out, int32_t* status,
-                 void* stream);
+                 const int8_t* weight, const float* w_scale, const float* bias, float act_scale, int32_t epilogue,
+                 float out_scale, const float* resid, void* out, int32_t flags, int32_t* status, void* stream);
+
 
 /* --------------------------------------------------------------------------------------------------------------
  * Refiner glue

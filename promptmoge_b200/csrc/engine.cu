@@ -37,7 +37,6 @@ namespace {
 
 struct QL {
     const int8_t* w = nullptr;
-    const int8_t* wp = nullptr;    // packed for the tcgen05 path (plan-owned), or null
     const float* ws = nullptr;
     const float* b = nullptr;
     float sa = 0.f;
@@ -120,7 +119,6 @@ struct pmg_refiner {
     cudaStream_t cap_stream = nullptr;
     cudaGraphExec_t exec = nullptr;
     std::vector<void*> allocs;
-    std::vector<void*> walloc;     // packed weights: live until destroy (not resized with the levels)
     int launches = 0;
 };
 
@@ -295,16 +293,18 @@ int check_weights(pmg_refiner* r) {
         ++nl;               \
     } while (0)
 
-int conv(int32_t* status, const LevelBuf& l, const int8_t* in, const QL& q, int mode, float out_scale,
+int flags_of(const pmg_refiner* r) { return r->cfg.use_tensor_cores ? 0 : PMG_FLAG_SIMT; }
+
+int conv(const pmg_refiner* r, const LevelBuf& l, const int8_t* in, const QL& q, int mode, float out_scale,
          const float* resid, void* out, const int32_t* count, cudaStream_t s) {
-    Epi e{mode, q.sa, out_scale, q.ws, q.b, resid, out, status};
-    return gemm_i8(in, l.nmap, l.cap, l.mask, count, l.cap, l.C, l.C, 27, q.w, q.wp, e, s);
+    Epi e{mode, q.sa, out_scale, q.ws, q.b, resid, out, r->status};
+    return gemm_i8(in, l.cap, l.nmap, l.cap, l.mask, count, l.cap, l.C, l.C, 27, q.w, flags_of(r), e, s);
 }
 
-int dense(int32_t* status, const int8_t* a, const int32_t* count, int64_t rows, int K, int N, const QL& q, int mode,
-          float out_scale, const float* resid, void* out, cudaStream_t s) {
-    Epi e{mode, q.sa, out_scale, q.ws, q.b, resid, out, status};
-    return gemm_i8(a, nullptr, 0, nullptr, count, rows, K, N, 1, q.w, q.wp, e, s);
+int dense(const pmg_refiner* r, const int8_t* a, const int32_t* count, int64_t rows, int K, int N, const QL& q,
+          int mode, float out_scale, const float* resid, void* out, cudaStream_t s) {
+    Epi e{mode, q.sa, out_scale, q.ws, q.b, resid, out, r->status};
+    return gemm_i8(a, rows, nullptr, 0, nullptr, count, rows, K, N, 1, q.w, flags_of(r), e, s);
 }
 
 // Residual block at level k: X -> S  (S = conv2(silu(conv1(silu(LN(X))))) + X).  When `up` is given, X is first
@@ -313,8 +313,8 @@ int resblock(pmg_refiner* r, int k, const RB& b, const float* up_src, const int3
     LevelBuf& l = r->lv[k];
     const int32_t* cnt = r->counts + 2 * k;
     LAUNCH(ln_silu_q8(l.X, up_src, parent, l.S, l.X, cnt, l.cap, l.C, b.norm.g, b.norm.b, 1e-6, b.c1.sa, l.q1, s));
-    LAUNCH(conv(r->status, l, l.q1, b.c1, PMG_EPI_SILU_Q8, b.c2.sa, nullptr, l.q2, cnt, s));
-    LAUNCH(conv(r->status, l, l.q2, b.c2, PMG_EPI_F32_RESID, 0.f, l.X, l.S, cnt, s));
+    LAUNCH(conv(r, l, l.q1, b.c1, PMG_EPI_SILU_Q8, b.c2.sa, nullptr, l.q2, cnt, s));
+    LAUNCH(conv(r, l, l.q2, b.c2, PMG_EPI_F32_RESID, 0.f, l.X, l.S, cnt, s));
     return PMG_OK;
 }
 
@@ -361,15 +361,15 @@ int enqueue_step(pmg_refiner* r, cudaStream_t s) {
             LevelBuf& n = r->lv[k + 1];
             const int32_t* ncnt = r->counts + 2 * (k + 1);
             LAUNCH(pool_mean(f.S, f.seg_idx, f.seg_off, ncnt, n.cap, f.C, r->pool[k].sa, f.pq, nullptr, s));
-            LAUNCH(dense(r->status, f.pq, ncnt, n.cap, f.C, n.C, r->pool[k], PMG_EPI_F32, 0.f, nullptr, n.X, s));
+            LAUNCH(dense(r, f.pq, ncnt, n.cap, f.C, n.C, r->pool[k], PMG_EPI_F32, 0.f, nullptr, n.X, s));
         }
     }
     {
         LevelBuf& l = r->lv[L - 1];
         const int32_t* cnt = r->counts + 2 * (L - 1);
         LAUNCH(concat_q8(l.S, r->enc_tok, l.col ? l.col : nullptr, cnt, l.cap, l.C, r->fuse0.sa, r->aq, s));
-        LAUNCH(dense(r->status, r->aq, cnt, l.cap, 2 * l.C, l.C, r->fuse0, PMG_EPI_SILU_Q8, r->fuse2.sa, nullptr, r->g8, s));
-        LAUNCH(dense(r->status, r->g8, cnt, l.cap, l.C, l.C, r->fuse2, PMG_EPI_F32, 0.f, nullptr, l.X, s));
+        LAUNCH(dense(r, r->aq, cnt, l.cap, 2 * l.C, l.C, r->fuse0, PMG_EPI_SILU_Q8, r->fuse2.sa, nullptr, r->g8, s));
+        LAUNCH(dense(r, r->g8, cnt, l.cap, l.C, l.C, r->fuse2, PMG_EPI_F32, 0.f, nullptr, l.X, s));
         PMG_TRY(resblock(r, L - 1, r->bott, nullptr, nullptr, s, nl));
     }
     for (int i = 0; i + 1 < L; ++i) {
@@ -378,7 +378,7 @@ int enqueue_step(pmg_refiner* r, cudaStream_t s) {
         LevelBuf& lt = r->lv[t];
         const int32_t* scnt = r->counts + 2 * src;
         LAUNCH(quantize(ls.S, ls.cap * ls.C, r->upl[i].sa, ls.uq, s));
-        LAUNCH(dense(r->status, ls.uq, scnt, ls.cap, ls.C, lt.C, r->upl[i], PMG_EPI_F32, 0.f, nullptr, ls.uc, s));
+        LAUNCH(dense(r, ls.uq, scnt, ls.cap, ls.C, lt.C, r->upl[i], PMG_EPI_F32, 0.f, nullptr, ls.uc, s));
         PMG_TRY(resblock(r, t, r->up[i], ls.uc, lt.parent, s, nl));
     }
     LAUNCH(out_apply(l0.S, r->N, l0.C, r->out_proj.w, r->out_proj.b, r->pc, r->pc, r->delta, s));
@@ -430,7 +430,6 @@ extern "C" void pmg_refiner_destroy(pmg_refiner* r) {
     if (!r) return;
     cudaDeviceSynchronize();
     free_all(r);
-    for (void* p : r->walloc) cudaFree(p);
     if (r->cap_stream) cudaStreamDestroy(r->cap_stream);
     delete r;
 }
@@ -466,15 +465,6 @@ extern "C" int pmg_refiner_set_qlayer(pmg_refiner* r, const char* name, const in
     int taps = 0, Ci = 0, Co = 0;
     if (!layer_shape(r, name, &taps, &Ci, &Co)) return PMG_ERR_BAD_ARG;
     q->w = weight;
-    q->wp = nullptr;
-    if (r->cfg.use_tensor_cores && tc_supported(Ci, Co)) {
-        void* p = nullptr;
-        PMG_CUDA_TRY(cudaMalloc(&p, (size_t)taps * Ci * Co));
-        r->walloc.push_back(p);
-        PMG_TRY(pmg_pack_weights_umma(weight, taps, Co, Ci, reinterpret_cast<int8_t*>(p), nullptr));
-        PMG_CUDA_TRY(cudaDeviceSynchronize());
-        q->wp = reinterpret_cast<const int8_t*>(p);
-    }
     q->ws = w_scale;
     q->b = bias;
     q->sa = act_scale;
@@ -512,7 +502,8 @@ extern "C" int pmg_refiner_set_frame(pmg_refiner* r, const uint16_t* enc_f16, co
     if (uv_bias) PMG_TRY(planar_to_rows(uv_bias, B, C, r->T, r->uv_rows, s));
     Epi e{uv_bias ? PMG_EPI_F32_RESID : PMG_EPI_F32, r->enc.sa, 0.f, r->enc.ws, r->enc.b, uv_bias ? r->uv_rows : nullptr,
           r->enc_tok, r->status};
-    return gemm_i8(r->tok_q, nullptr, 0, nullptr, nullptr, (int64_t)B * r->T, K, C, 1, r->enc.w, r->enc.wp, e, s);
+    return gemm_i8(r->tok_q, (int64_t)B * r->T, nullptr, 0, nullptr, nullptr, (int64_t)B * r->T, K, C, 1, r->enc.w,
+                   flags_of(r), e, s);
 }
 
 extern "C" int pmg_refiner_set_inputs(pmg_refiner* r, const float* point_coord, const float* lidar_depth,

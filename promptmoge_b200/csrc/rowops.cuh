@@ -18,14 +18,17 @@ struct Epi {
 
 int gemm_i8_simt(const int8_t* in, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask, const int32_t* count,
                  int64_t max_rows, int Ci, int Co, int taps, const int8_t* w, const Epi& e, cudaStream_t s);
-// tcgen05 implicit-GEMM path over weights packed by pmg_pack_weights_umma; PMG_ERR_UNSUPPORTED for other shapes.
-int gemm_i8_tc(const int8_t* in, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask, const int32_t* count,
-               int64_t max_rows, int Ci, int Co, int taps, const int8_t* w_packed, const Epi& e, cudaStream_t s);
+// tcgen05 implicit-GEMM path: dense layers (taps == 1) by TMA tile loads, 27-tap convs by a cp.async gather;
+// PMG_ERR_UNSUPPORTED for shapes it does not cover.  `in_rows` = rows of `in` (neighbour indices outside
+// [0, in_rows) read as zero rows).
+int gemm_i8_tc(const int8_t* in, int64_t in_rows, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask,
+               const int32_t* count, int64_t max_rows, int Ci, int Co, int taps, const int8_t* w, const Epi& e,
+               cudaStream_t s);
 bool tc_supported(int Ci, int Co);
-// Dispatch: tcgen05 when packed weights are given and the shape is covered, SIMT otherwise.
-int gemm_i8(const int8_t* in, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask, const int32_t* count,
-            int64_t max_rows, int Ci, int Co, int taps, const int8_t* w, const int8_t* w_packed, const Epi& e,
-            cudaStream_t s);
+// Dispatch: tcgen05 where the shape is covered (unless flags has PMG_FLAG_SIMT), SIMT otherwise.
+int gemm_i8(const int8_t* in, int64_t in_rows, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask,
+            const int32_t* count, int64_t max_rows, int Ci, int Co, int taps, const int8_t* w, int flags,
+            const Epi& e, cudaStream_t s);
 
 int quantize(const float* x, int64_t n, float s, int8_t* q, cudaStream_t st);
 int ln_silu_q8(const float* x, const float* up_src, const int32_t* parent, const float* skip, float* x_out,

@@ -146,12 +146,11 @@ int gemm_i8_simt(const int8_t* in, const int32_t* nmap, int64_t ld, const uint32
     }
 }
 
-int gemm_i8(const int8_t* in, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask, const int32_t* count,
-            int64_t max_rows, int Ci, int Co, int taps, const int8_t* w, const int8_t* w_packed, const Epi& e,
-            cudaStream_t s) {
-    if (w_packed && tc_supported(Ci, Co))
-        return gemm_i8_tc(in, nmap, ld, tile_mask, count, max_rows, Ci, Co, taps, w_packed, e, s);
-    if (!w) return PMG_ERR_UNSUPPORTED;
+int gemm_i8(const int8_t* in, int64_t in_rows, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask,
+            const int32_t* count, int64_t max_rows, int Ci, int Co, int taps, const int8_t* w, int flags,
+            const Epi& e, cudaStream_t s) {
+    if (!(flags & PMG_FLAG_SIMT) && tc_supported(Ci, Co))
+        return gemm_i8_tc(in, in_rows, nmap, ld, tile_mask, count, max_rows, Ci, Co, taps, w, e, s);
     return gemm_i8_simt(in, nmap, ld, tile_mask, count, max_rows, Ci, Co, taps, w, e, s);
 }
 
@@ -216,31 +215,33 @@ using namespace pmg;
 
 static bool mode_ok(int mode) { return mode >= PMG_EPI_ACC32 && mode <= PMG_EPI_SILU_Q8; }
 
-extern "C" int pmg_spconv_i8(const int8_t* in_q8, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask,
-                             const int32_t* count, int64_t max_rows, int32_t Ci, int32_t Co, const int8_t* weight,
-                             const int8_t* weight_packed, const float* w_scale, const float* bias, float act_scale,
-                             int32_t epilogue, float out_scale, const float* resid, void* out, int32_t* status,
-                             void* stream) {
-    if (!in_q8 || !nmap || (!weight && !weight_packed) || !out || max_rows < 0 || ld < max_rows || !mode_ok(epilogue))
+extern "C" int pmg_spconv_i8(const int8_t* in_q8, int64_t in_rows, const int32_t* nmap, int64_t ld,
+                             const uint32_t* tile_mask, const int32_t* count, int64_t max_rows, int32_t Ci, int32_t Co,
+                             const int8_t* weight, const float* w_scale, const float* bias, float act_scale,
+                             int32_t epilogue, float out_scale, const float* resid, void* out, int32_t flags,
+                             int32_t* status, void* stream) {
+    if (!in_q8 || in_rows <= 0 || !nmap || !weight || !out || max_rows < 0 || ld < max_rows || !mode_ok(epilogue))
         return PMG_ERR_BAD_ARG;
     if (Ci % 16 || Co % 16 || Ci <= 0 || Co <= 0 || Ci > 1024 || Co > 256) return PMG_ERR_BAD_ARG;
     if (epilogue != PMG_EPI_ACC32 && (!w_scale || !bias)) return PMG_ERR_BAD_ARG;
     if (epilogue == PMG_EPI_F32_RESID && !resid) return PMG_ERR_BAD_ARG;
     Epi e{epilogue, act_scale, out_scale, w_scale, bias, resid, out, status};
-    return gemm_i8(in_q8, nmap, ld, tile_mask, count, max_rows, Ci, Co, 27, weight, weight_packed, e,
+    return gemm_i8(in_q8, in_rows, nmap, ld, tile_mask, count, max_rows, Ci, Co, 27, weight, flags, e,
                    as_stream(stream));
 }
 
 extern "C" int pmg_dense_i8(const int8_t* a_q8, const int32_t* count, int64_t max_rows, int32_t K, int32_t N,
-                            const int8_t* weight, const int8_t* weight_packed, const float* w_scale, const float* bias,
-                            float act_scale, int32_t epilogue, float out_scale, const float* resid, void* out,
+                            const int8_t* weight, const float* w_scale, const float* bias, float act_scale,
+                            int32_t epilogue, float out_scale, const float* resid, void* out, int32_t flags,
                             int32_t* status, void* stream) {
-    if (!a_q8 || (!weight && !weight_packed) || !out || max_rows < 0 || !mode_ok(epilogue)) return PMG_ERR_BAD_ARG;
+    if (!a_q8 || !weight || !out || max_rows < 0 || !mode_ok(epilogue)) return PMG_ERR_BAD_ARG;
     if (K % 16 || N % 16 || K <= 0 || N <= 0 || N > 256) return PMG_ERR_BAD_ARG;
     if (epilogue != PMG_EPI_ACC32 && (!w_scale || !bias)) return PMG_ERR_BAD_ARG;
     if (epilogue == PMG_EPI_F32_RESID && !resid) return PMG_ERR_BAD_ARG;
+    if (max_rows == 0) return PMG_OK;
     Epi e{epilogue, act_scale, out_scale, w_scale, bias, resid, out, status};
-    return gemm_i8(a_q8, nullptr, 0, nullptr, count, max_rows, K, N, 1, weight, weight_packed, e, as_stream(stream));
+    return gemm_i8(a_q8, max_rows, nullptr, 0, nullptr, count, max_rows, K, N, 1, weight, flags, e,
+                   as_stream(stream));
 }
 
 extern "C" int pmg_spconv_f32(const float* in, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask,

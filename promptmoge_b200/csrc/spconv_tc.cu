@@ -1,354 +1,357 @@
-// tcgen05 (5th-generation tensor core) int8 implicit-GEMM path for the submanifold conv and the dense layers.
+// tcgen05 (5th-generation tensor core) int8 implicit-GEMM kernels: the refiner's submanifold convs and dense layers.
 //
-// One persistent CTA per SM walks 128-row output tiles (UMMA M = 128, N = Co).  A tile's work is a stream of items
-// through an NST-stage shared-memory ring; an item is K = 128 bytes: up to 128 / Ci taps of a narrow layer (4 taps at
-// Ci = 32, 2 at Ci = 64), or one 128-byte K-block of a wide one.  Warp roles:
-//   * warps 0-3 (one output row per thread) gather the row's input voxel for each tap of the item through the
-//     tap-major neighbour map with 16-byte cp.async (absent neighbours zero-filled by the copy itself);
-//   * thread 0 also bulk-copies the taps' weight blocks (packed in global memory so that per-tap blocks concatenate)
-//     with cp.async.bulk, completing on the stage's mbarrier (expect_tx);
-//   * warp 4 owns two TMEM accumulators (128 lanes x Co int32 columns each); one of its threads issues
-//     tcgen05.mma.cta_group::1.kind::i8 (K = 32 per instruction) and tcgen05.commit to release stages and to
-//     publish a finished accumulator;
-//   * warps 5-8 read their 32 TMEM lanes each (tcgen05.ld 32x32b.x16) and apply the fused epilogue (dequant ->
-//     +bias -> [SiLU -> requantise] or [+residual]) with the reference's rounding, while the next tile already
-//     accumulates into the other TMEM buffer.
-// Both operands use the K-major no-swizzle core-matrix layout with the 16-byte K chunks outermost
-// ([K/16][rows/8][8][16]; LBO = bytes between K chunks, SBO = 128).  Every mbarrier wait is bounded: on timeout the
-// CTA records PMG_ERR_TIMEOUT in the status word, drains its copies, frees its TMEM and returns.
+// One persistent CTA per SM walks work units = (128-row output tile, N block of NT <= 128 output channels).  A unit's
+// reduction is a stream of items through an NST-stage shared-memory ring; an item is K = 128 bytes: 128 / Ci taps of
+// a narrow conv (4 taps at Ci = 32, 2 at Ci = 64), or one 128-byte K-block of a wide layer.  Warp roles:
+//   warps 0-3   producers:
+//     DENSE   (dense layers) thread 0 issues a 2-D TMA tile load of the 128 A rows (swizzled) and of the weights;
+//     GATHER  (convs) per item the warps gather the tap rows' 16-byte chunks with cp.async, lanes spread along K
+//             (absent neighbours zero-filled by the copy); completion is tracked with a lag of half the ring
+//             (cp.async.wait_group + proxy fence + arrive), so the MMA always has finished items queued.  The
+//             neighbour indices of the next tile are copied into shared memory (4-byte cp.async per row and tap,
+//             completion tracked by an mbarrier) while the current tile's items run, and thread 0 publishes each
+//             tile's record (rows, tap mask) through shared memory, so no producer waits on a dependent global
+//             load between tiles and no index is held in registers.
+//   warp 4      owns two TMEM accumulators (128 lanes x NT int32 columns); lane 0 issues
+//               tcgen05.mma.cta_group::1.kind::i8 (K = 32 bytes per instruction) and tcgen05.commit to release stages
+//               and to publish a finished accumulator.
+//   warps 5-8   epilogue, one warp per TMEM lane quarter: tcgen05.ld 32x32b.x16, then dequant -> +bias -> [SiLU ->
+//               requantise] or [+residual] with the reference's rounding, while the next unit accumulates into the
+//               other buffer.  (Nine warps leave each thread up to 168 registers; a thirteenth warp on an SM
+//               sub-partition would cap them at 128.)
+// Weights arrive by 2-D TMA tile loads from the plain tap-major [taps][Co][Ci] tensor (swizzle matching the row
+// width W = min(Ci, 128)); a conv whose whole 27-tap weight fits (Co = NT, Ci < 128) keeps it resident in shared
+// memory for the kernel's lifetime.  Gathered A operands use the K-major no-swizzle core-matrix layout with the 8-row
+// groups outermost ([16 row groups][8 K chunks][8 rows][16 bytes]), so a warp's 16-byte writes hit distinct banks.
+// No multicast anywhere.  Every wait is bounded: on timeout the CTA records PMG_ERR_TIMEOUT in the status word, lets
+// issued MMAs retire, frees its TMEM and returns.
 #include <algorithm>
+#include <mutex>
 
-#include "common.cuh"
-#include "rowops.cuh"
+#include "tc_common.cuh"
 
 namespace pmg {
 
 namespace tc {
 
-constexpr int kM = 128;              // rows per tile = UMMA M
-constexpr int kProducers = 128;      // warps 0-3 (and, as a count, the epilogue warps 5-8)
-constexpr uint32_t kSpin = 1u << 22; // bounded waits
+constexpr int kProducers = 128;                   // warps 0-3
+constexpr int kEpiWarps = 4;                      // warps 5-8
+constexpr int kThreads = 32 * (5 + kEpiWarps);
+constexpr int kItemK = 128;
+constexpr int kBudget = 196 * 1024;               // shared memory for resident weights + ring
+constexpr int kResMax = 110592;                   // 27-tap weights kept resident up to this size (64 x 64 x 27)
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
+enum Kind { DENSE = 0, GATHER = 1 };
 
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar)) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
-                 "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-// Bounded wait; false on timeout or when another warp already aborted.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-    for (uint32_t i = 0; i < kSpin; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if (*abort_flag) return false;
-    }
-    return false;
-}
-
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// K-major, no swizzle: start, LBO (K direction), SBO (M/N direction), version 1 (sm100), layout type 0.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
-    uint64_t d = 0;
-    d |= (uint64_t)((addr >> 4) & 0x3FFF);
-    d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
-    d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
-    d |= (uint64_t)1 << 46;
-    return d;
-}
-
-// kind::i8 instruction descriptor: D = s32, A = B = signed int8, both K-major, N >> 3, M >> 4.
-__host__ __device__ constexpr uint32_t instr_desc(int M, int N) {
-    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
-        : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
-        "[%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-
-template <int CO>
-constexpr int tmem_cols() {
-    return CO <= 32 ? 32 : (CO <= 64 ? 64 : (CO <= 128 ? 128 : 256));
-}
-
-// KB = K bytes per pipeline item.  Ci <= 128 with 128 % Ci == 0: several taps share an item (128 / Ci taps);
-// Ci > 128: one tap, Ci / 128 K-blocks; other Ci <= 128 (96): one tap, KB = Ci.
-template <int CO, int KB>
+template <int KIND, int NT, int W, bool RES>
 struct Cfg {
-    static constexpr int kA = kM * KB;                       // A bytes per stage
-    static constexpr int kB = CO * KB;                       // B bytes per stage
+    static constexpr int kRes = RES ? 27 * NT * W : 0;
+    static constexpr int kIdx = KIND == GATHER ? 2 * 27 * kM * 4 : 0;   // neighbour indices of two tiles
+    static constexpr int kA = kM * kItemK;
+    static constexpr int kB = RES ? 0 : NT * kItemK;
     static constexpr int kStage = kA + kB;
-    static constexpr int kBudget = 200 * 1024;
-    static constexpr int kStages = (kBudget / kStage) > 8 ? 8 : (kBudget / kStage);
-    static constexpr int kLag = kStages - 1 < 4 ? kStages - 1 : 4;
-    static constexpr int kSmem = kStages * kStage + 1024 + 256;
-    static constexpr uint32_t kLboA = (kM / 8) * 128;        // A: bytes between 16-byte K chunks
-    static constexpr uint32_t kLboB = (CO / 8) * 128;        // B: bytes between 16-byte K chunks
+    static constexpr int kStagesRaw = (kBudget - kRes) / kStage;
+    static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
+    static constexpr int kLag = KIND == GATHER ? (kStages / 2 > 1 ? kStages / 2 : 1) : 0;
+    static constexpr int kSmem = kRes + kIdx + kStages * kStage + 1024 + 512;
+    static_assert(RES || kStagesRaw >= 2, "shared memory budget");
 };
 
-__device__ __forceinline__ void epi_store16(const Epi& e, int64_t m, int n0, int Co, const uint32_t (&r)[16]) {
-    const int64_t o = m * Co + n0;
-    if (e.mode == PMG_EPI_ACC32) {
-        int4* d = reinterpret_cast<int4*>(reinterpret_cast<int32_t*>(e.out) + o);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) d[q] = make_int4((int)r[4 * q], (int)r[4 * q + 1], (int)r[4 * q + 2], (int)r[4 * q + 3]);
-    } else if (e.mode == PMG_EPI_SILU_Q8) {
-        uint32_t packed[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            uint32_t w = 0;
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                const int n = n0 + 4 * q + t;
-                const int v = quant8(silu(dequant((int)r[4 * q + t], e.sa, __ldg(e.ws + n), __ldg(e.bias + n))),
-                                     e.out_scale);
-                w |= ((uint32_t)(v & 0xFF)) << (8 * t);
-            }
-            packed[q] = w;
-        }
-        *reinterpret_cast<int4*>(reinterpret_cast<int8_t*>(e.out) + o) =
-            make_int4((int)packed[0], (int)packed[1], (int)packed[2], (int)packed[3]);
-    } else {
-        float* d = reinterpret_cast<float*>(e.out) + o;
-        const float* rs = e.mode == PMG_EPI_F32_RESID ? e.resid + o : nullptr;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            float4 v;
-            float* pv = reinterpret_cast<float*>(&v);
-            float4 rr = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (rs) rr = *reinterpret_cast<const float4*>(rs + 4 * q);
-            const float* prr = reinterpret_cast<const float*>(&rr);
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-                const int n = n0 + 4 * q + t;
-                float y = dequant((int)r[4 * q + t], e.sa, __ldg(e.ws + n), __ldg(e.bias + n));
-                if (rs) y = __fadd_rn(y, prr[t]);
-                pv[t] = y;
-            }
-            *reinterpret_cast<float4*>(d + 4 * q) = v;
-        }
-    }
-}
-
-// Warp roles: 0-3 gather A (one output row per thread) and thread 0 bulk-copies B; 4 issues MMAs and owns TMEM;
-// 5-8 run the epilogue from one of two TMEM accumulators while the next tile accumulates into the other.
-constexpr int kThreads2 = 288;
-
-template <int CO, int KB>
-__global__ void __launch_bounds__(kThreads2, 1)
-    k_gemm_i8_tc(const int8_t* __restrict__ in, const int32_t* __restrict__ nmap, int64_t ld,
-                 const uint32_t* __restrict__ tile_mask, const int32_t* __restrict__ count, int64_t max_rows, int Ci,
-                 int taps, const int8_t* __restrict__ wpk, Epi e) {
-    using C = Cfg<CO, KB>;
+template <int KIND, int NT, int W, bool RES>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+              const int8_t* __restrict__ in, int64_t in_rows, const int32_t* __restrict__ nmap, int64_t ld,
+              const uint32_t* __restrict__ tile_mask, const int32_t* __restrict__ count, int64_t max_rows, int Ci,
+              int Co, int taps, Epi e) {
+    using C = Cfg<KIND, NT, W, RES>;
     constexpr int NST = C::kStages;
     constexpr int LAG = C::kLag;
-    constexpr int NCOLS = tmem_cols<CO>();
-    constexpr uint32_t IDESC = instr_desc(kM, CO);
+    constexpr int NCOLS = tmem_cols<NT>();
+    constexpr uint32_t IDESC = instr_desc(kM, NT);
+    constexpr uint32_t kSboA = 8 * 128;              // gathered A: bytes between 8-row groups (8 K chunks of 128 B)
+    constexpr uint32_t kLboA = 128;                  // gathered A: bytes between K-adjacent core matrices
+    constexpr int TPI = W < kItemK ? kItemK / W : 1;  // most taps per item
+    constexpr int CPR = W / 16;                      // 16-byte chunks of one tap row in an item
+    constexpr int RPP = 32 / CPR;                    // rows a warp covers per pass
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + NST * C::kStage);
+    uint8_t* res = smem;                             // resident weights [27][NT][W] (RES)
+    int32_t* idx = reinterpret_cast<int32_t*>(res + C::kRes);   // [2][27][128] neighbour indices
+    uint8_t* ring = res + C::kRes + C::kIdx;
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + NST * C::kStage);
     uint64_t* empty = full + NST;
-    uint64_t* acc_full = empty + NST;      // [2]
-    uint64_t* acc_empty = acc_full + 2;    // [2]
-    uint64_t* drain = acc_empty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* acc_full = empty + NST;       // [2]
+    uint64_t* acc_empty = acc_full + 2;     // [2]
+    uint64_t* idx_full = acc_empty + 2;     // [2] indices of a tile landed
+    uint64_t* rec_full = idx_full + 2;      // [2] record of a tile published
+    uint64_t* rec_free = rec_full + 2;      // [2] record read by every producer
+    uint64_t* drain = rec_free + 2;
+    uint64_t* wres = drain + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(wres + 1);
     __shared__ volatile int s_abort;
+    __shared__ float s_ws[256], s_bias[256];           // epilogue per-channel weight scale and bias
+    __shared__ int4 s_rec[2];                          // producers: {m0, rows, tap mask} of the current / next unit
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
+        const uint32_t full_count = KIND == DENSE ? 1 : (RES ? kProducers : kProducers + 1);
         for (int s = 0; s < NST; ++s) {
-            mbar_init(&full[s], kProducers + 1);
+            mbar_init(&full[s], full_count);
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], kProducers);
+            mbar_init(&acc_empty[b], 32 * kEpiWarps);
+            mbar_init(&idx_full[b], kProducers + 1);
+            mbar_init(&rec_full[b], 1);
+            mbar_init(&rec_free[b], kProducers);
         }
         mbar_init(drain, 1);
+        mbar_init(wres, 1);
         s_abort = 0;
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        fence_mbar_init();
     }
-    if (warp == 4) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(2 * NCOLS)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-    }
+    if (e.ws && e.bias)
+        for (int n = threadIdx.x; n < Co; n += blockDim.x) {
+            s_ws[n] = e.ws[n];
+            s_bias[n] = e.bias[n];
+        }
+    if (warp == 4) tmem_alloc(tmem_slot, 2 * NCOLS);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // ---- work units ---------------------------------------------------------------------------------------- //
     const int64_t M = rows_of(count, max_rows);
-    const int64_t ntiles = (M + kM - 1) / kM;
-    const int kbw = Ci < KB ? Ci : KB;                 // K bytes of one tap inside an item
-    const int tpi = (taps == 27 && Ci < KB) ? KB / Ci : 1;   // taps per item
-    const int nkb = Ci > KB ? Ci / KB : 1;             // K-blocks per tap
-    const int64_t blk = (int64_t)CO * kbw;             // packed weight bytes per (tap, K-block)
-    const uint32_t sbase = smem_u32(smem);
+    const int64_t ntile = (M + kM - 1) / kM;
+    const int nblk = Co / NT;
+    const int64_t nunits = ntile * nblk;
+    const int tpi = (taps == 27 && Ci < kItemK) ? kItemK / Ci : 1;   // taps per item
+    const int nkb = Ci > W ? Ci / W : 1;                               // K-blocks per tap
 
-    auto tile_taps = [&](int64_t m0) -> uint32_t {
-        if (taps != 27) return 1u;
-        if (!tile_mask) return 0x7ffffffu;
-        uint32_t mk = 0;
-#pragma unroll
-        for (int g = 0; g < 4; ++g)
-            if (m0 + 32 * g < M) mk |= tile_mask[(m0 >> 5) + g];
-        return mk & 0x7ffffffu;
+    // Rows and tap mask of a tile.
+    auto tile_of = [&](int64_t t, int64_t& m0, int& mc, uint32_t& mk) {
+        m0 = t * kM;
+        mc = (int)min((int64_t)kM, M - m0);
+        mk = 0x7ffffffu;
+        if (taps != 27) {
+            mk = 1u;
+        } else if (tile_mask) {
+            mk = 0;
+            for (int64_t g = m0 >> 5; g <= ((m0 + mc - 1) >> 5); ++g) mk |= tile_mask[g];
+            mk &= 0x7ffffffu;
+        }
+        if (!mk) mk = 1u;       // an all-absent tile still runs one (zero) item so its accumulator is defined
     };
-    // next group of up to tpi taps from the mask
-    auto take = [&](uint32_t& mk, int (&tv)[4]) -> int {
+    // Next <= tpi taps of the unit's tap mask.  Fully unrolled so tv stays in registers (a dynamically indexed array
+    // would live in local memory, and with most of the SM's unified L1 carved out as shared memory every access
+    // would go to L2).
+    auto take = [&](uint32_t& mk, int (&tv)[TPI]) -> int {
         int nt = 0;
-        while (mk && nt < tpi) {
-            tv[nt++] = __ffs(mk) - 1;
-            mk &= mk - 1;
+#pragma unroll
+        for (int g = 0; g < TPI; ++g) {
+            const bool has = mk != 0u && g < tpi;
+            tv[g] = has ? __ffs(mk) - 1 : 0;
+            nt += has ? 1 : 0;
+            if (has) mk &= mk - 1u;
         }
         return nt;
     };
+    const uint32_t ring_base = smem_u32(ring);
+    const uint32_t res_base = smem_u32(res);
 
     if (warp < 4) {
-        // --------------------------------------------- producers ---------------------------------------------- //
-        const int r = threadIdx.x;
-        const uint32_t a_row_off = (uint32_t)((r >> 3) * 128 + (r & 7) * 16);
-        uint32_t it = 0, pend_first = 0;
-        int pending = 0;
+        // =========================================== producers =========================================== //
+        uint32_t it = 0;
         bool ok = true;
-        for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-            const int64_t row = tile * kM + r;
-            uint32_t mk = tile_taps(tile * kM);
-            while (mk && ok) {
-                int tv[4];
-                const int nt = take(mk, tv);
-                int32_t idx[4];
-#pragma unroll
-                for (int g = 0; g < 4; ++g) {
-                    idx[g] = -1;
-                    if (g < nt && row < M) idx[g] = (taps == 27) ? __ldg(nmap + (int64_t)tv[g] * ld + row) : (int32_t)row;
-                }
-                for (int kb = 0; kb < nkb; ++kb) {
-                    const uint32_t s = it % NST, ph = (it / NST) & 1u;
-                    if (!mbar_wait(&empty[s], ph ^ 1u, &s_abort)) { ok = false; break; }
-                    const uint32_t sa = sbase + s * C::kStage;
-#pragma unroll
-                    for (int g = 0; g < 4; ++g) {
-                        if (g < nt) {
-                            const int8_t* src = in + (int64_t)(idx[g] >= 0 ? idx[g] : 0) * Ci + kb * kbw;
-                            const uint32_t dst = sa + a_row_off + (uint32_t)(g * (kbw / 16)) * C::kLboA;
-                            for (int c = 0; c < kbw / 16; ++c) cp_async16(dst + c * C::kLboA, src + c * 16, idx[g] >= 0);
-                        }
-                    }
-                    cp_async_commit();
-                    if (threadIdx.x == 0) {
-                        mbar_arrive_expect_tx(&full[s], (uint32_t)(nt * blk));
-                        for (int g = 0; g < nt; ++g)
-                            bulk_g2s(sa + C::kA + (uint32_t)(g * blk), wpk + ((int64_t)tv[g] * nkb + kb) * blk,
-                                     (uint32_t)blk, &full[s]);
-                    }
-                    ++it;
-                    ++pending;
-                    if (pending > LAG) {
-                        cp_async_wait<LAG>();
-                        fence_proxy_async();
-                        mbar_arrive(&full[pend_first % NST]);
-                        ++pend_first;
-                        --pending;
+        if (RES && threadIdx.x == 0) {
+            mbar_arrive_expect_tx(wres, (uint32_t)(27 * NT * W));
+            for (int v = 0; v < 27; ++v) tma_tile2d(res_base + v * NT * W, &tmB, 0, v * Co, wres);
+        }
+        if (KIND == DENSE) {
+            if (threadIdx.x == 0) {
+                for (int64_t u = blockIdx.x; u < nunits && ok; u += gridDim.x) {
+                    int64_t m0;
+                    int mc;
+                    uint32_t mk;
+                    tile_of(u / nblk, m0, mc, mk);
+                    const int n0 = (int)(u % nblk) * NT;
+                    for (int kb = 0; kb < nkb; ++kb) {
+                        const uint32_t s = it % NST, ph = (it / NST) & 1u;
+                        if (!mbar_wait(&empty[s], ph ^ 1u, &s_abort)) { ok = false; break; }
+                        const uint32_t sa = ring_base + s * C::kStage;
+                        mbar_arrive_expect_tx(&full[s], (uint32_t)(kM * W + NT * W));
+                        tma_tile2d(sa, &tmA, kb * W, (int)m0, &full[s]);
+                        tma_tile2d(sa + C::kA, &tmB, kb * W, n0, &full[s]);
+                        ++it;
                     }
                 }
             }
-        }
-        cp_async_wait<0>();
-        fence_proxy_async();
-        while (pending > 0) {
-            mbar_arrive(&full[pend_first % NST]);
-            ++pend_first;
-            --pending;
+        } else {
+            // Per unit k (this CTA's k-th unit): thread 0 publishes the unit's record in s_rec[k & 1] (rec_full);
+            // every producer then copies its row's neighbour indices of the unit's taps into idx[k & 1] with 4-byte
+            // cp.async (idx_full tracks their completion).  Both happen one unit ahead, after the first item of the
+            // previous unit.
+            const int r = threadIdx.x;
+            const int my_c = lane % CPR, my_sub = lane / CPR;
+            uint32_t pend_first = 0;
+            int pending = 0;
+            const uint32_t idx_base = smem_u32(idx);
+            auto publish = [&](int64_t u, uint32_t k) -> bool {      // thread 0
+                const uint32_t b = k & 1u, use = k >> 1;
+                int64_t m0;
+                int mc;
+                uint32_t mk;
+                tile_of(u / nblk, m0, mc, mk);
+                if (use >= 1 && !mbar_wait(&rec_free[b], (use - 1) & 1u, &s_abort)) return false;
+                s_rec[b] = make_int4((int)m0, mc, (int)mk, 0);
+                mbar_arrive(&rec_full[b]);
+                return true;
+            };
+            auto issue_ids = [&](uint32_t k) -> bool {               // every producer
+                const uint32_t b = k & 1u;
+                if (!mbar_wait(&rec_full[b], (k >> 1) & 1u, &s_abort)) return false;
+                const int4 a = s_rec[b];
+                __syncwarp();        // the warp's lanes are done reading idx[b] (their rows) of unit k - 2
+                if (r < a.y) {
+                    const uint32_t mk = (uint32_t)a.z;
+                    const int32_t* src = nmap + a.x + r;
+#pragma unroll
+                    for (int v = 0; v < 27; ++v)
+                        if ((mk >> v) & 1u)
+                            cp_async4(idx_base + (uint32_t)(((int)b * 27 + v) * kM + r) * 4u, src + (int64_t)v * ld);
+                }
+                cp_async_mbar_arrive(&idx_full[b]);
+                if (threadIdx.x == 0) mbar_arrive(&idx_full[b]);
+                return true;
+            };
+
+            int64_t u = blockIdx.x;
+            uint32_t k = 0;
+            if (u < nunits) {
+                if (threadIdx.x == 0) ok = publish(u, 0);
+                ok = __all_sync(0xffffffffu, ok);
+                ok = ok && issue_ids(0);
+            }
+            for (; u < nunits && ok; u += gridDim.x, ++k) {
+                const bool has_next = u + gridDim.x < nunits;
+                const uint32_t cb = k & 1u;
+                ok = __all_sync(0xffffffffu, mbar_wait(&idx_full[cb], (k >> 1) & 1u, &s_abort));
+                if (!ok) break;
+                const int4 ra = s_rec[cb];
+                mbar_arrive(&rec_free[cb]);
+                const int mc = ra.y;
+                const int n0 = (int)(u % nblk) * NT;
+                const int32_t* cidx = idx + cb * 27 * kM;
+                bool prefetched = false;
+                uint32_t mk = (uint32_t)ra.z;
+                while (mk && ok) {
+                    int tv[TPI];
+                    const int nt = take(mk, tv);
+                    for (int kb = 0; kb < nkb; ++kb) {
+                        const uint32_t s = it % NST, ph = (it / NST) & 1u;
+                        ok = __all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1u, &s_abort));
+                        if (!ok) break;
+                        const uint32_t sa = ring_base + s * C::kStage;
+                        if (!RES && threadIdx.x == 0) {
+                            mbar_arrive_expect_tx(&full[s], (uint32_t)(nt * NT * W));
+#pragma unroll
+                            for (int g = 0; g < TPI; ++g)
+                                if (g < nt) tma_tile2d(sa + C::kA + g * NT * W, &tmB, kb * W, tv[g] * Co + n0, &full[s]);
+                        }
+                        const int koff = kb * W + my_c * 16;
+#pragma unroll
+                        for (int g = 0; g < TPI; ++g) {
+                            if (g >= nt) break;
+                            const int v = tv[g];
+                            const int kc = g * CPR + my_c;                          // 16-byte K chunk in the item
+#pragma unroll
+                            for (int p = 0; p < CPR; ++p) {
+                                const int rr = 32 * warp + p * RPP + my_sub;          // row within the tile
+                                int32_t id = rr < mc ? cidx[v * kM + rr] : -1;
+                                if (id >= in_rows) id = -1;
+                                const uint32_t dst = sa + (uint32_t)((rr >> 3) * kSboA + kc * kLboA + (rr & 7) * 16);
+                                cp_async16(dst, in + (int64_t)(id >= 0 ? id : 0) * Ci + koff, id >= 0);
+                            }
+                        }
+                        cp_async_commit();
+                        ++pending;
+                        if (pending > LAG) {
+                            cp_async_wait<LAG>();
+                            fence_proxy_async();
+                            mbar_arrive(&full[pend_first % NST]);
+                            ++pend_first;
+                            --pending;
+                        }
+                        ++it;
+                        if (!prefetched) {
+                            // after the first item: publish the next unit and start its index copies
+                            prefetched = true;
+                            if (has_next) {
+                                if (threadIdx.x == 0) ok = publish(u + gridDim.x, k + 1);
+                                ok = __all_sync(0xffffffffu, ok);
+                                ok = ok && issue_ids(k + 1);
+                            }
+                        }
+                    }
+                }
+                ok = __all_sync(0xffffffffu, ok);
+            }
+            cp_async_wait_all();
+            fence_proxy_async();
+            while (pending > 0) {
+                mbar_arrive(&full[pend_first % NST]);
+                ++pend_first;
+                --pending;
+            }
         }
         if (!ok) {
             s_abort = 1;
             flag(e.status, PMG_ERR_TIMEOUT);
         }
     } else if (warp == 4) {
-        // ------------------------------------------- MMA issuer ----------------------------------------------- //
+        // =========================================== MMA issuer =========================================== //
         if (lane == 0) {
             uint32_t it = 0, t = 0;
-            bool ok = true;
-            for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++t) {
+            bool ok = true, issued = false;
+            if (RES && nunits > (int64_t)blockIdx.x) ok = mbar_wait(wres, 0, &s_abort);
+            int64_t xm0;
+            int xmc;
+            uint32_t xmk = 1;
+            if ((int64_t)blockIdx.x < nunits) tile_of(blockIdx.x / nblk, xm0, xmc, xmk);
+            for (int64_t u = blockIdx.x; u < nunits && ok; u += gridDim.x, ++t) {
+                uint32_t mk = xmk;
+                if (u + gridDim.x < nunits) tile_of((u + gridDim.x) / nblk, xm0, xmc, xmk);
                 const uint32_t b = t & 1u;
-                uint32_t mk = tile_taps(tile * kM);
                 if (!mbar_wait(&acc_empty[b], ((t >> 1) & 1u) ^ 1u, &s_abort)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t d = tmem + b * NCOLS;
                 uint32_t accumulate = 0;
                 while (mk && ok) {
-                    int tv[4];
+                    int tv[TPI];
                     const int nt = take(mk, tv);
-                    const int ksteps = nt * kbw / 32;
                     for (int kb = 0; kb < nkb; ++kb) {
                         const uint32_t s = it % NST, ph = (it / NST) & 1u;
                         if (!mbar_wait(&full[s], ph, &s_abort)) { ok = false; break; }
                         tc_fence_after();
-                        const uint32_t sa = sbase + s * C::kStage;
-                        for (int kk = 0; kk < ksteps; ++kk) {
-                            const uint64_t ad = smem_desc(sa + 2 * kk * C::kLboA, C::kLboA, 128);
-                            const uint64_t bd = smem_desc(sa + C::kA + 2 * kk * C::kLboB, C::kLboB, 128);
-                            mma_i8(d, ad, bd, IDESC, accumulate);
-                            accumulate = 1;
+                        const uint32_t sa = ring_base + s * C::kStage;
+                        const uint32_t sb = sa + C::kA;
+#pragma unroll
+                        for (int g = 0; g < TPI; ++g) {
+                            if (g >= nt) break;
+#pragma unroll
+                            for (int kk = 0; kk < W / 32; ++kk) {
+                                const uint64_t ad = KIND == DENSE
+                                                        ? desc_sw<W>(sa + 32 * kk)
+                                                        : desc_plain(sa + (uint32_t)(g * CPR + 2 * kk) * kLboA, kLboA,
+                                                                     kSboA);
+                                const uint64_t bd = RES ? desc_sw<W>(res_base + tv[g] * NT * W + 32 * kk)
+                                                        : desc_sw<W>(sb + g * NT * W + 32 * kk);
+                                mma_i8(d, ad, bd, IDESC, accumulate);
+                                accumulate = 1;
+                                issued = true;
+                            }
                         }
                         mma_commit(&empty[s]);
                         ++it;
@@ -360,27 +363,37 @@ __global__ void __launch_bounds__(kThreads2, 1)
             if (!ok) {
                 s_abort = 1;
                 flag(e.status, PMG_ERR_TIMEOUT);
-                mma_commit(drain);
-                for (uint32_t i = 0; i < kSpin && !mbar_try_wait(drain, 0); ++i) {
+                if (issued) {
+                    mma_commit(drain);
+                    const uint64_t t0 = global_ns();
+                    while (!mbar_try_wait_sleep(drain, 0, 4000) && global_ns() - t0 < kWaitNs) {
+                    }
                 }
             }
         }
         __syncwarp();
     } else {
-        // -------------------------------------------- epilogue ------------------------------------------------ //
+        // ============================================ epilogue ============================================ //
         const int q = warp & 3;                         // TMEM lane quarter this warp may access
         uint32_t t = 0;
         bool ok = true;
-        for (int64_t tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++t) {
+        int64_t xm0 = 0;
+        int xmc = 0;
+        uint32_t xmk;
+        if ((int64_t)blockIdx.x < nunits) tile_of(blockIdx.x / nblk, xm0, xmc, xmk);
+        for (int64_t u = blockIdx.x; u < nunits && ok; u += gridDim.x, ++t) {
+            const int64_t m0 = xm0;
+            const int mc = xmc, n0 = (int)(u % nblk) * NT;
+            if (u + gridDim.x < nunits) tile_of((u + gridDim.x) / nblk, xm0, xmc, xmk);
             const uint32_t b = t & 1u;
             if (!mbar_wait(&acc_full[b], (t >> 1) & 1u, &s_abort)) { ok = false; break; }
             tc_fence_after();
-            const int64_t m = tile * kM + 32 * q + lane;
+            const int rr = 32 * q + lane;
 #pragma unroll 1
-            for (int j = 0; j < CO / 16; ++j) {
+            for (int j = 0; j < NT / 16; ++j) {
                 uint32_t acc[16];
                 tmem_ld16(tmem + b * NCOLS + ((uint32_t)(32 * q) << 16) + (uint32_t)(j * 16), acc);
-                if (m < M) epi_store16(e, m, j * 16, CO, acc);
+                if (rr < mc) epi_store16(e, s_ws, s_bias, m0 + rr, n0 + j * 16, Co, acc);
             }
             tc_fence_before();
             mbar_arrive(&acc_empty[b]);
@@ -394,84 +407,133 @@ __global__ void __launch_bounds__(kThreads2, 1)
     __syncthreads();
     if (warp == 4) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * NCOLS) : "memory");
+        tmem_dealloc(tmem, 2 * NCOLS);
     }
 }
 
 }  // namespace tc
 
-template <int CO, int KB>
-static int launch_tc(const int8_t* in, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask,
-                     const int32_t* count, int64_t max_rows, int Ci, int taps, const int8_t* wpk, const Epi& e,
-                     cudaStream_t s) {
-    using C = tc::Cfg<CO, KB>;
-    static bool attr_set = false;
-    if (!attr_set) {
-        PMG_CUDA_TRY(cudaFuncSetAttribute(tc::k_gemm_i8_tc<CO, KB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+// ------------------------------------------------------------------------------------------------------------- //
+// Host side
+// ------------------------------------------------------------------------------------------------------------- //
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+int make_tensor_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_w, uint32_t box_h) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return PMG_ERR_UNSUPPORTED;
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (cols & 15) || rows == 0) return PMG_ERR_BAD_ARG;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols};
+    const cuuint32_t box[2] = {box_w, box_h};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapSwizzle sw = box_w == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                  : box_w == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                                : CU_TENSOR_MAP_SWIZZLE_128B;
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? PMG_OK : PMG_ERR_BAD_ARG;
+}
+
+namespace {
+
+struct TcArgs {
+    const int8_t* in;
+    int64_t in_rows;
+    const int32_t* nmap;
+    int64_t ld;
+    const uint32_t* tile_mask;
+    const int32_t* count;
+    int64_t max_rows;
+    int Ci, Co, taps;
+    const int8_t* w;
+};
+
+template <int KIND, int NT, int W, bool RES>
+int launch(const TcArgs& a, const Epi& e, cudaStream_t s) {
+    using C = tc::Cfg<KIND, NT, W, RES>;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    PMG_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return PMG_ERR_UNSUPPORTED;
+    if (!attr_set[dev]) {
+        PMG_CUDA_TRY(cudaFuncSetAttribute(tc::k_gemm_tc<KIND, NT, W, RES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           C::kSmem));
-        attr_set = true;
+        attr_set[dev] = true;
     }
-    const int64_t tiles = (max_rows + tc::kM - 1) / tc::kM;
-    const int grid = (int)std::min<int64_t>(tiles, (int64_t)kNumSMs);
+    const int64_t units = (a.max_rows + tc::kM - 1) / tc::kM * (a.Co / NT);
+    const int grid = (int)std::min<int64_t>(units, (int64_t)kNumSMs);
     if (grid <= 0) return PMG_OK;
-    tc::k_gemm_i8_tc<CO, KB><<<grid, tc::kThreads2, C::kSmem, s>>>(in, nmap, ld, tile_mask, count, max_rows, Ci, taps,
-                                                                    wpk, e);
+    CUtensorMap ma, mb;
+    int rc = PMG_OK;
+    if (KIND == tc::DENSE) rc = make_tensor_map(&ma, a.in, (uint64_t)a.in_rows, (uint64_t)a.Ci, W, tc::kM);
+    else memset(&ma, 0, sizeof(ma));
+    if (rc != PMG_OK) return rc;
+    rc = make_tensor_map(&mb, a.w, (uint64_t)a.taps * a.Co, (uint64_t)a.Ci, W, NT);
+    if (rc != PMG_OK) return rc;
+    tc::k_gemm_tc<KIND, NT, W, RES><<<grid, tc::kThreads, C::kSmem, s>>>(
+        ma, mb, a.in, a.in_rows, a.nmap, a.ld, a.tile_mask, a.count, a.max_rows, a.Ci, a.Co, a.taps, e);
     PMG_LAUNCH_CHECK();
     return PMG_OK;
 }
 
-// Shapes the tensor-core path covers: Co in {32, 64, 128, 256}; Ci a multiple of 32 that divides 128, is <= 128, or
-// is a multiple of 128.
-bool tc_supported(int Ci, int Co) {
-    if (!(Co == 32 || Co == 64 || Co == 128 || Co == 256)) return false;
-    if (Ci < 32 || Ci % 32) return false;
-    if (Ci > 128 && Ci % 128) return false;
-    return true;
+template <int KIND, int NT, int W>
+int launch_res(const TcArgs& a, const Epi& e, cudaStream_t s) {
+    // whole 27-tap weight resident in shared memory when it is one N block and leaves a ring of >= 4 stages
+    if constexpr (KIND == tc::GATHER && W < tc::kItemK && 27 * NT * W <= tc::kResMax) {
+        if constexpr (tc::Cfg<KIND, NT, W, true>::kStagesRaw >= 4) {
+            if (a.Co == NT && a.Ci == W) return launch<KIND, NT, W, true>(a, e, s);
+        }
+    }
+    return launch<KIND, NT, W, false>(a, e, s);
 }
 
-// K bytes per pipeline item (see Cfg).
-int tc_kblock(int Ci) { return (Ci > 128 || 128 % Ci == 0) ? 128 : Ci; }
-
-int gemm_i8_tc(const int8_t* in, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask, const int32_t* count,
-               int64_t max_rows, int Ci, int Co, int taps, const int8_t* wpk, const Epi& e, cudaStream_t s) {
-    if (!wpk || !tc_supported(Ci, Co)) return PMG_ERR_UNSUPPORTED;
-    const int kb = tc_kblock(Ci);
-#define PMG_TC_CASE(CO_, KB_)                                                                            \
-    if (Co == CO_ && kb == KB_) return launch_tc<CO_, KB_>(in, nmap, ld, tile_mask, count, max_rows, Ci, taps, wpk, e, s);
-    PMG_TC_CASE(32, 96) PMG_TC_CASE(32, 128)
-    PMG_TC_CASE(64, 96) PMG_TC_CASE(64, 128)
-    PMG_TC_CASE(128, 96) PMG_TC_CASE(128, 128)
-    PMG_TC_CASE(256, 96) PMG_TC_CASE(256, 128)
+template <int KIND>
+int dispatch(const TcArgs& a, const Epi& e, cudaStream_t s) {
+    const int NTv = a.Co < 128 ? a.Co : 128;
+    const int Wv = a.Ci < 128 ? a.Ci : 128;
+#define PMG_TC_CASE(NT_, W_) \
+    if (NTv == NT_ && Wv == W_) return launch_res<KIND, NT_, W_>(a, e, s);
+    PMG_TC_CASE(32, 32) PMG_TC_CASE(32, 64) PMG_TC_CASE(32, 128)
+    PMG_TC_CASE(64, 32) PMG_TC_CASE(64, 64) PMG_TC_CASE(64, 128)
+    PMG_TC_CASE(128, 32) PMG_TC_CASE(128, 64) PMG_TC_CASE(128, 128)
 #undef PMG_TC_CASE
     return PMG_ERR_UNSUPPORTED;
 }
 
-// Packed weight layout for the tensor-core path: per tap and K-block of kbw = min(Ci, KB) bytes, the Co x kbw block
-// with its 16-byte K chunks outermost: [kbw/16][Co/8][8 rows][16 bytes].  Blocks of consecutive taps concatenate
-// into a valid operand for an item that groups several taps.
-__global__ void k_pack_umma(const int8_t* __restrict__ w, int taps, int Co, int Ci, int kbw, int8_t* __restrict__ out) {
-    const int64_t total = (int64_t)taps * Co * Ci;
-    const int nkb = Ci / kbw;
-    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-        const int v = (int)(e / ((int64_t)Co * Ci));
-        const int rem = (int)(e - (int64_t)v * Co * Ci);
-        const int n = rem / Ci, k = rem - (rem / Ci) * Ci;
-        const int kb = k / kbw, kk = k - kb * kbw;
-        const int64_t dst = ((int64_t)v * nkb + kb) * Co * kbw + ((int64_t)(kk >> 4) * (Co / 8) + (n >> 3)) * 128 +
-                            (n & 7) * 16 + (kk & 15);
-        out[dst] = w[e];
-    }
+}  // namespace
+
+// Shapes the tensor-core path covers: Co a multiple of 32 up to 256 with NT = min(Co, 128) dividing it; Ci in
+// {32, 64} or a multiple of 128.
+bool tc_supported(int Ci, int Co) {
+    if (!(Co == 32 || Co == 64 || Co == 128 || Co == 256)) return false;
+    return Ci == 32 || Ci == 64 || (Ci >= 128 && Ci % 128 == 0);
+}
+
+int gemm_i8_tc(const int8_t* in, int64_t in_rows, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask,
+               const int32_t* count, int64_t max_rows, int Ci, int Co, int taps, const int8_t* w, const Epi& e,
+               cudaStream_t s) {
+    if (!tc_supported(Ci, Co) || (taps != 1 && taps != 27)) return PMG_ERR_UNSUPPORTED;
+    if (in_rows <= 0 || in_rows >= INT32_MAX) return PMG_ERR_BAD_ARG;
+    TcArgs a{in, in_rows, nmap, ld, tile_mask, count, max_rows, Ci, Co, taps, w};
+    if (taps == 1) return dispatch<tc::DENSE>(a, e, s);
+    return dispatch<tc::GATHER>(a, e, s);
 }
 
 }  // namespace pmg
-
-extern "C" int pmg_pack_weights_umma(const int8_t* w, int32_t taps, int32_t Co, int32_t Ci, int8_t* packed,
-                                     void* stream) {
-    if (!w || !packed || taps <= 0 || !pmg::tc_supported(Ci, Co)) return PMG_ERR_BAD_ARG;
-    const int64_t total = (int64_t)taps * Co * Ci;
-    const int kbw = Ci < pmg::tc_kblock(Ci) ? Ci : pmg::tc_kblock(Ci);
-    pmg::k_pack_umma<<<(int)std::min<int64_t>((total + 255) / 256, 4096), 256, 0, pmg::as_stream(stream)>>>(
-        w, taps, Co, Ci, kbw, packed);
-    PMG_LAUNCH_CHECK();
-    return PMG_OK;
-}

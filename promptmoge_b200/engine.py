@@ -88,6 +88,7 @@ class RefinerEngine:
         self.geo = geometry
         self.device = torch.device(device)
         self.use_prompt = use_prompt
+        self.tensor_cores = tensor_cores
         L = geometry.levels
         cfg = RefinerConfig()
         cfg.batch, cfg.height, cfg.width, cfg.levels = geometry.batch, geometry.height, geometry.width, L

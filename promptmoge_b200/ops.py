@@ -118,56 +118,40 @@ def _epi_out(mode, rows, n, dev):
     return torch.empty((rows, n), dtype=torch.float32, device=dev)
 
 
+FLAG_SIMT = 1
+
+
 def tc_supported(Ci: int, Co: int) -> bool:
-    """Shapes the tcgen05 path covers (pmg_pack_weights_umma)."""
-    return Co in (32, 64, 128, 256) and Ci >= 32 and Ci % 32 == 0 and (Ci <= 128 or Ci % 128 == 0)
-
-
-def pack_weights_umma(weight: torch.Tensor) -> torch.Tensor:
-    """[taps, Co, Ci] (or [N, K]) int8 -> the tcgen05 path's packed layout (same byte count)."""
-    _dev(weight, torch.int8, "weight")
-    w3 = weight if weight.dim() == 3 else weight.unsqueeze(0)
-    taps, Co, Ci = w3.shape
-    out = torch.empty_like(w3)
-    call("pmg_pack_weights_umma", _p(w3), taps, Co, Ci, _p(out), _stream())
-    return out
-
-
-def _packed(weight, tensor_cores):
-    if not tensor_cores:
-        return None
-    Co, Ci = weight.shape[-2], weight.shape[-1]
-    return pack_weights_umma(weight) if tc_supported(Ci, Co) else None
+    """Shapes the tcgen05 path covers."""
+    return Co in (32, 64, 128, 256) and (Ci in (32, 64) or (Ci >= 128 and Ci % 128 == 0))
 
 
 def spconv_i8(q_in, nmap, tile_mask, weight_tap_major, w_scale=None, bias=None, act_scale=1.0, mode=EPI_ACC32,
-              out_scale=1.0, resid=None, count=None, rows=None, tensor_cores=True, packed=None, status=None):
-    """Submanifold conv: q_in [M_in, Ci] int8, nmap [27, ld] int32, weight [27, Co, Ci] int8.  With tensor_cores the
-    weights are packed (or `packed` is used) and the tcgen05 kernel runs where the shape allows."""
+              out_scale=1.0, resid=None, count=None, rows=None, tensor_cores=True, status=None):
+    """Submanifold conv: q_in [M_in, Ci] int8, nmap [27, ld] int32, weight [27, Co, Ci] int8.  The tcgen05 kernel
+    runs where the shape allows unless tensor_cores is False."""
     _dev(q_in, torch.int8, "q_in")
     _dev(weight_tap_major, torch.int8, "weight")
     ld = nmap.shape[1]
     rows = ld if rows is None else rows
     Co, Ci = weight_tap_major.shape[1], weight_tap_major.shape[2]
-    wp = packed if packed is not None else _packed(weight_tap_major, tensor_cores)
     out = _epi_out(mode, rows, Co, q_in.device)
-    call("pmg_spconv_i8", _p(q_in), _p(nmap), ld, _p(tile_mask), _p(count), rows, Ci, Co, _p(weight_tap_major),
-         _p(wp), _p(w_scale), _p(bias), float(act_scale), mode, float(out_scale), _p(resid), _p(out), _p(status),
-         _stream())
+    call("pmg_spconv_i8", _p(q_in), q_in.shape[0], _p(nmap), ld, _p(tile_mask), _p(count), rows, Ci, Co,
+         _p(weight_tap_major), _p(w_scale), _p(bias), float(act_scale), mode, float(out_scale), _p(resid), _p(out),
+         0 if tensor_cores else FLAG_SIMT, _p(status), _stream())
     return out
 
 
 def dense_i8(a, weight, w_scale=None, bias=None, act_scale=1.0, mode=EPI_ACC32, out_scale=1.0, resid=None,
-             count=None, rows=None, tensor_cores=True, packed=None, status=None):
+             count=None, rows=None, tensor_cores=True, status=None):
     """Dense int8 layer: a [M, K] int8, weight [N, K] int8."""
     _dev(a, torch.int8, "a")
     _dev(weight, torch.int8, "weight")
     rows = a.shape[0] if rows is None else rows
     N, K = weight.shape
-    wp = packed if packed is not None else _packed(weight, tensor_cores)
     out = _epi_out(mode, rows, N, a.device)
-    call("pmg_dense_i8", _p(a), _p(count), rows, K, N, _p(weight), _p(wp), _p(w_scale), _p(bias), float(act_scale),
-         mode, float(out_scale), _p(resid), _p(out), _p(status), _stream())
+    call("pmg_dense_i8", _p(a), _p(count), rows, K, N, _p(weight), _p(w_scale), _p(bias), float(act_scale), mode,
+         float(out_scale), _p(resid), _p(out), 0 if tensor_cores else FLAG_SIMT, _p(status), _stream())
     return out
 
 

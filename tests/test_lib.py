@@ -43,10 +43,9 @@ def test_bad_arguments_rejected_without_device_work():
     lib = _lib.load()
     # null pointers / bad sizes are refused before any launch
     assert lib.pmg_voxelize_l0(None, 1, 4, 4, 256.0, None, None, None, None, 16, None, None) == 1
-    assert lib.pmg_spconv_i8(None, None, 0, None, None, 0, 16, 16, None, None, None, None, 1.0, 0, 1.0, None, None,
+    assert lib.pmg_spconv_i8(None, 0, None, 0, None, None, 0, 16, 16, None, None, None, 1.0, 0, 1.0, None, None, 0,
                              None, None) == 1
-    assert lib.pmg_dense_i8(None, None, 0, 16, 16, None, None, None, None, 1.0, 0, 1.0, None, None, None, None) == 1
-    assert lib.pmg_pack_weights_umma(None, 27, 48, 64, None, None) == 1     # Co = 48 has no tensor-core tiling
+    assert lib.pmg_dense_i8(None, None, 0, 16, 16, None, None, None, 1.0, 0, 1.0, None, None, 0, None, None) == 1
 
 
 def test_product_path_has_no_cpu_fallback(monkeypatch, tmp_path):
