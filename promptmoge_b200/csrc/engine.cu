@@ -296,8 +296,9 @@ int check_weights(pmg_refiner* r) {
 int flags_of(const pmg_refiner* r) { return r->cfg.use_tensor_cores ? 0 : PMG_FLAG_SIMT; }
 
 int conv(const pmg_refiner* r, const LevelBuf& l, const int8_t* in, const QL& q, int mode, float out_scale,
-         const float* resid, void* out, const int32_t* count, cudaStream_t s) {
-    Epi e{mode, q.sa, out_scale, q.ws, q.b, resid, out, r->status};
+         const float* resid, void* out, const int32_t* count, cudaStream_t s, int8_t* q2 = nullptr,
+         float q2_scale = 0.f) {
+    Epi e{mode, q.sa, out_scale, q.ws, q.b, resid, out, r->status, q2, q2_scale};
     return gemm_i8(in, l.cap, l.nmap, l.cap, l.mask, count, l.cap, l.C, l.C, 27, q.w, flags_of(r), e, s);
 }
 
@@ -308,13 +309,15 @@ int dense(const pmg_refiner* r, const int8_t* a, const int32_t* count, int64_t r
 }
 
 // Residual block at level k: X -> S  (S = conv2(silu(conv1(silu(LN(X))))) + X).  When `up` is given, X is first
-// formed as up.uc[parent] + S (the skip) -- NearestUp + skip add -- and written to X.
-int resblock(pmg_refiner* r, int k, const RB& b, const float* up_src, const int32_t* parent, cudaStream_t s, int& nl) {
+// formed as up.uc[parent] + S (the skip) -- NearestUp + skip add -- and written to X.  When `uq` is given, conv2's
+// epilogue also writes S quantised with `uq_scale` (the input of the next up projection).
+int resblock(pmg_refiner* r, int k, const RB& b, const float* up_src, const int32_t* parent, cudaStream_t s, int& nl,
+             int8_t* uq = nullptr, float uq_scale = 0.f) {
     LevelBuf& l = r->lv[k];
     const int32_t* cnt = r->counts + 2 * k;
     LAUNCH(ln_silu_q8(l.X, up_src, parent, l.S, l.X, cnt, l.cap, l.C, b.norm.g, b.norm.b, 1e-6, b.c1.sa, l.q1, s));
     LAUNCH(conv(r, l, l.q1, b.c1, PMG_EPI_SILU_Q8, b.c2.sa, nullptr, l.q2, cnt, s));
-    LAUNCH(conv(r, l, l.q2, b.c2, PMG_EPI_F32_RESID, 0.f, l.X, l.S, cnt, s));
+    LAUNCH(conv(r, l, l.q2, b.c2, PMG_EPI_F32_RESID, 0.f, l.X, l.S, cnt, s, uq, uq_scale));
     return PMG_OK;
 }
 
@@ -370,16 +373,18 @@ int enqueue_step(pmg_refiner* r, cudaStream_t s) {
         LAUNCH(concat_q8(l.S, r->enc_tok, l.col ? l.col : nullptr, cnt, l.cap, l.C, r->fuse0.sa, r->aq, s));
         LAUNCH(dense(r, r->aq, cnt, l.cap, 2 * l.C, l.C, r->fuse0, PMG_EPI_SILU_Q8, r->fuse2.sa, nullptr, r->g8, s));
         LAUNCH(dense(r, r->g8, cnt, l.cap, l.C, l.C, r->fuse2, PMG_EPI_F32, 0.f, nullptr, l.X, s));
-        PMG_TRY(resblock(r, L - 1, r->bott, nullptr, nullptr, s, nl));
+        PMG_TRY(resblock(r, L - 1, r->bott, nullptr, nullptr, s, nl, l.uq, r->upl[0].sa));
     }
     for (int i = 0; i + 1 < L; ++i) {
         const int src = L - 1 - i, t = src - 1;
         LevelBuf& ls = r->lv[src];
         LevelBuf& lt = r->lv[t];
         const int32_t* scnt = r->counts + 2 * src;
-        LAUNCH(quantize(ls.S, ls.cap * ls.C, r->upl[i].sa, ls.uq, s));
+        // ls.uq was written by the epilogue of the resblock that produced ls.S
         LAUNCH(dense(r, ls.uq, scnt, ls.cap, ls.C, lt.C, r->upl[i], PMG_EPI_F32, 0.f, nullptr, ls.uc, s));
-        PMG_TRY(resblock(r, t, r->up[i], ls.uc, lt.parent, s, nl));
+        const bool feeds_up = i + 2 < L;
+        PMG_TRY(resblock(r, t, r->up[i], ls.uc, lt.parent, s, nl, feeds_up ? lt.uq : nullptr,
+                         feeds_up ? r->upl[i + 1].sa : 0.f));
     }
     LAUNCH(out_apply(l0.S, r->N, l0.C, r->out_proj.w, r->out_proj.b, r->pc, r->pc, r->delta, s));
     r->launches = nl;

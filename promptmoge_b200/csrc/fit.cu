@@ -96,27 +96,47 @@ struct FitArgs {
     double* partials;  // [B][nblk][5]
     uint32_t* hist;    // [B][kBins]
     uint32_t* arrive;  // [B]
+    uint32_t* rbits;   // [B][N] relative residual bits of the current iteration (0xFFFFFFFF: not in the mask)
 };
 
-// Sums over the current weights (iteration 0: the mask; later: mask & r <= thr with the state's s, t), then the
-// last CTA of the frame solves.  gridDim = (nblk, B).
+constexpr int kFitPer = 4;   // elements per thread and sweep (loads issued together)
+
+// Sums over the current weights (iteration 0: the mask; later: mask & r <= thr with the residuals cached by the
+// previous iteration's first select pass), then the last CTA of the frame solves.  gridDim = (nblk, B).
 __global__ void __launch_bounds__(kFitThreads) k_fit_sums(FitArgs a, int iter) {
     const int b = blockIdx.y;
     pmg_fit_state* st = a.st + b;
     const float* z = a.z + (int64_t)b * a.N;
     const float* y = a.y + (int64_t)b * a.N;
     const uint8_t* fl = a.flags + (int64_t)b * a.N;
-    const float s0 = st->s, t0 = st->t, thr = st->thr;
+    const uint32_t* rb = a.rbits + (int64_t)b * a.N;
+    const float thr = st->thr;
+    const bool use_r = iter > 0 && !isinf(thr);   // thr = inf: the k-th value was a fill value, weights = mask
     double acc[5] = {0, 0, 0, 0, 0};
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.N; i += (int64_t)a.nblk * blockDim.x) {
-        if (!(fl[i] & 2)) continue;
-        const float zi = z[i], yi = y[i];
-        if (iter > 0 && !(rel_resid(s0, t0, zi, yi) <= thr)) continue;
-        acc[0] += 1.0;
-        acc[1] += (double)zi;
-        acc[2] += (double)yi;
-        acc[3] += (double)__fmul_rn(zi, zi);
-        acc[4] += (double)__fmul_rn(zi, yi);
+    const int64_t sweep = (int64_t)a.nblk * blockDim.x * kFitPer;
+    for (int64_t base = (int64_t)blockIdx.x * blockDim.x * kFitPer + threadIdx.x; base < a.N; base += sweep) {
+        uint8_t f[kFitPer];
+        float zi[kFitPer], yi[kFitPer];
+        uint32_t ri[kFitPer];
+#pragma unroll
+        for (int k = 0; k < kFitPer; ++k) {
+            const int64_t i = base + (int64_t)k * blockDim.x;
+            const bool in = i < a.N;
+            f[k] = in ? fl[i] : 0;
+            zi[k] = in ? z[i] : 0.f;
+            yi[k] = in ? y[i] : 0.f;
+            ri[k] = (in && use_r) ? rb[i] : 0u;
+        }
+#pragma unroll
+        for (int k = 0; k < kFitPer; ++k) {
+            if (!(f[k] & 2)) continue;
+            if (use_r && !(__uint_as_float(ri[k]) <= thr)) continue;
+            acc[0] += 1.0;
+            acc[1] += (double)zi[k];
+            acc[2] += (double)yi[k];
+            acc[3] += (double)__fmul_rn(zi[k], zi[k]);
+            acc[4] += (double)__fmul_rn(zi[k], yi[k]);
+        }
     }
     __shared__ double red[kFitThreads / 32][5];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -138,12 +158,18 @@ __global__ void __launch_bounds__(kFitThreads) k_fit_sums(FitArgs a, int iter) {
         last = atomicAdd(&a.arrive[b], 1u) == (unsigned)a.nblk - 1;
     }
     __syncthreads();
-    if (!last || threadIdx.x != 0) return;
+    if (!last) return;
     __threadfence();
-    double tot[5] = {0, 0, 0, 0, 0};
-    const volatile double* part = a.partials + (int64_t)b * a.nblk * 5;
-    for (int k = 0; k < a.nblk; ++k)
-        for (int q = 0; q < 5; ++q) tot[q] += part[k * 5 + q];
+    // last CTA: the per-CTA partials in a fixed order (thread q sums column q), then thread 0 solves
+    __shared__ double tot[5];
+    if (threadIdx.x < 5) {
+        const volatile double* part = a.partials + (int64_t)b * a.nblk * 5;
+        double v = 0;
+        for (int k = 0; k < a.nblk; ++k) v += part[k * 5 + threadIdx.x];
+        tot[threadIdx.x] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x != 0) return;
     a.arrive[b] = 0;
     if (iter == 0) {
         const int count = (int)tot[0];
@@ -169,7 +195,8 @@ __global__ void __launch_bounds__(kFitThreads) k_fit_sums(FitArgs a, int iter) {
     st->remaining = st->k;
 }
 
-// One radix pass of the k-th smallest r over the masked points.  pass 0: bits 31..21, 1: 20..10, 2: 9..0.
+// One radix pass of the k-th smallest r over the masked points.  pass 0: bits 31..21 (and caches every masked
+// point's r for the later passes and the next sums), 1: 20..10, 2: 9..0.
 __global__ void __launch_bounds__(kFitThreads) k_fit_select(FitArgs a, int pass) {
     const int b = blockIdx.y;
     pmg_fit_state* st = a.st + b;
@@ -187,12 +214,43 @@ __global__ void __launch_bounds__(kFitThreads) k_fit_select(FitArgs a, int pass)
     const float* z = a.z + (int64_t)b * a.N;
     const float* y = a.y + (int64_t)b * a.N;
     const uint8_t* fl = a.flags + (int64_t)b * a.N;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < a.N; i += (int64_t)a.nblk * blockDim.x) {
-        if (!(fl[i] & 2)) continue;
-        const uint32_t bits = __float_as_uint(rel_resid(s0, t0, z[i], y[i]));
-        const uint32_t hi = (pass == 0) ? 0u : (bits >> (shift + nbits));
-        if (hi != prefix) continue;
-        atomicAdd(&h[(bits >> shift) & ((1u << nbits) - 1)], 1u);
+    uint32_t* rb = a.rbits + (int64_t)b * a.N;
+    const int lane = threadIdx.x & 31;
+    const int64_t sweep = (int64_t)a.nblk * blockDim.x * kFitPer;
+    for (int64_t base = (int64_t)blockIdx.x * blockDim.x * kFitPer + threadIdx.x; base < a.N; base += sweep) {
+        uint32_t bits[kFitPer];
+        if (pass == 0) {
+            uint8_t f[kFitPer];
+            float zi[kFitPer], yi[kFitPer];
+#pragma unroll
+            for (int k = 0; k < kFitPer; ++k) {
+                const int64_t i = base + (int64_t)k * blockDim.x;
+                const bool in = i < a.N;
+                f[k] = in ? fl[i] : 0;
+                zi[k] = in ? z[i] : 0.f;
+                yi[k] = in ? y[i] : 0.f;
+            }
+#pragma unroll
+            for (int k = 0; k < kFitPer; ++k) {
+                const int64_t i = base + (int64_t)k * blockDim.x;
+                bits[k] = (f[k] & 2) ? __float_as_uint(rel_resid(s0, t0, zi[k], yi[k])) : 0xFFFFFFFFu;
+                if (i < a.N) rb[i] = bits[k];
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < kFitPer; ++k) {
+                const int64_t i = base + (int64_t)k * blockDim.x;
+                bits[k] = i < a.N ? rb[i] : 0xFFFFFFFFu;
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kFitPer; ++k) {
+            // residuals are >= 0, so a match has sign bit 0; the not-in-mask code 0xFFFFFFFF never matches
+            const uint32_t hi = (pass == 0) ? (bits[k] >> 31) : (bits[k] >> (shift + nbits));
+            const int bin = hi == prefix ? (int)((bits[k] >> shift) & ((1u << nbits) - 1)) : -1;
+            const unsigned peers = __match_any_sync(0xffffffffu, bin);
+            if (bin >= 0 && lane == __ffs(peers) - 1) atomicAdd(&h[bin], (uint32_t)__popc(peers));
+        }
     }
     __syncthreads();
     uint32_t* gh = a.hist + (int64_t)b * kBins;
@@ -279,11 +337,16 @@ static int grid_for(int64_t work) {
     return (int)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, (int64_t)kNumSMs * 16));
 }
 
-static int fit_nblk(int64_t N) { return (int)std::max<int64_t>(1, std::min<int64_t>((N + 4095) / 4096, kNumSMs)); }
+static int fit_nblk(int64_t N) {
+    const int64_t per_cta = (int64_t)kFitThreads * kFitPer;
+    return (int)std::max<int64_t>(1, std::min<int64_t>((N + per_cta - 1) / per_cta, (int64_t)kNumSMs * 8));
+}
 
+// [B][nblk][5] double partials | [B][kBins] histogram | [B] arrival counters | [B][N] residual bits
 size_t fit_workspace_bytes(int B, int64_t N) {
     const int nblk = fit_nblk(N);
-    return (size_t)B * nblk * 5 * sizeof(double) + (size_t)B * kBins * sizeof(uint32_t) + (size_t)B * sizeof(uint32_t) + 256;
+    return (size_t)B * nblk * 5 * sizeof(double) + (size_t)B * kBins * sizeof(uint32_t) + (size_t)B * sizeof(uint32_t) +
+           (size_t)B * N * sizeof(uint32_t) + 512;
 }
 
 // Prompt-fit inputs are prepared by k_fit_prep_prompt; the workspace must be zeroed once before first use (the
@@ -302,6 +365,7 @@ int fit_solve(const float* z, const float* y, const uint8_t* flags, int B, int64
     a.partials = reinterpret_cast<double*>(ws);
     a.hist = reinterpret_cast<uint32_t*>(a.partials + (size_t)B * a.nblk * 5);
     a.arrive = a.hist + (size_t)B * kBins;
+    a.rbits = reinterpret_cast<uint32_t*>((reinterpret_cast<uintptr_t>(a.arrive + B) + 255) & ~uintptr_t(255));
     const dim3 grid(a.nblk, B);
     for (int it = 0; it <= iters; ++it) {
         k_fit_sums<<<grid, kFitThreads, 0, s>>>(a, it);

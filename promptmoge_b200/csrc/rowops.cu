@@ -7,6 +7,9 @@
 // rounded once, so they equal a correctly rounded fp32 result.
 #include <cuda_fp16.h>
 
+#include <algorithm>
+#include <initializer_list>
+
 #include "common.cuh"
 #include "rowops.cuh"
 
@@ -184,6 +187,248 @@ __global__ void k_out_apply(const float* __restrict__ x, int64_t N, int C, const
     }
 }
 
+// ---------------------------------------------------------------------------------------------------------------- //
+// Row-parallel forms for C in {32, 64, 128, 256}: G = C / 8 lanes per row, each lane owning two float4 chunks of the
+// row (chunks sub and sub + G), so every warp-wide load or store covers whole rows contiguously and a warp handles
+// 32 / G rows; per-row reductions are log2(G)-step shuffle trees.  Same operations and roundings as the element-wise
+// forms above.
+// ---------------------------------------------------------------------------------------------------------------- //
+template <int C>
+struct RowMap {
+    static constexpr int G = C / 8;
+    static constexpr int RPB = 256 / G;       // rows per 256-thread block
+};
+
+template <int C>
+__device__ __forceinline__ void load8(const float* __restrict__ row, int sub, float (&v)[8]) {
+    constexpr int G = RowMap<C>::G;
+    const float4 a = reinterpret_cast<const float4*>(row)[sub];
+    const float4 b = reinterpret_cast<const float4*>(row)[sub + G];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+template <int C>
+__device__ __forceinline__ void store8(float* __restrict__ row, int sub, const float (&v)[8]) {
+    constexpr int G = RowMap<C>::G;
+    reinterpret_cast<float4*>(row)[sub] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(row)[sub + G] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+template <int C>
+__device__ __forceinline__ void store8_q8(int8_t* __restrict__ row, int sub, const int (&q)[8]) {
+    constexpr int G = RowMap<C>::G;
+    uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        w0 |= (uint32_t)(q[k] & 0xFF) << (8 * k);
+        w1 |= (uint32_t)(q[4 + k] & 0xFF) << (8 * k);
+    }
+    reinterpret_cast<uint32_t*>(row)[sub] = w0;
+    reinterpret_cast<uint32_t*>(row)[sub + G] = w1;
+}
+
+// channel of element k (0..7) of lane `sub`
+template <int C>
+__device__ __forceinline__ int chan8(int sub, int k) {
+    return 4 * (sub + (k >> 2) * RowMap<C>::G) + (k & 3);
+}
+
+template <int G>
+__device__ __forceinline__ double group_sum(double v) {
+#pragma unroll
+    for (int o = 1; o < G; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+template <int C>
+__global__ void __launch_bounds__(256) k_ln_silu_rows(const float* __restrict__ x, const float* __restrict__ up_src,
+                                                      const int32_t* __restrict__ parent,
+                                                      const float* __restrict__ skip, float* __restrict__ x_out,
+                                                      const int32_t* __restrict__ count, int64_t max_rows,
+                                                      const float* __restrict__ gamma, const float* __restrict__ beta,
+                                                      double eps, float scale, int8_t* __restrict__ q) {
+    constexpr int G = RowMap<C>::G, RPB = RowMap<C>::RPB;
+    __shared__ float sg[C], sb[C];
+    for (int i = threadIdx.x; i < C; i += blockDim.x) {
+        sg[i] = gamma[i];
+        sb[i] = beta[i];
+    }
+    __syncthreads();
+    const int64_t M = rows_of(count, max_rows);
+    const int sub = threadIdx.x % G;
+    for (int64_t base = (int64_t)blockIdx.x * RPB; base < M; base += (int64_t)gridDim.x * RPB) {
+        const int64_t m = base + threadIdx.x / G;
+        const bool live = m < M;
+        float v[8];
+        if (live) {
+            if (up_src) {
+                float u[8];
+                load8<C>(up_src + (int64_t)parent[m] * C, sub, u);
+                load8<C>(skip + m * C, sub, v);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) v[k] = __fadd_rn(u[k], v[k]);
+                store8<C>(x_out + m * C, sub, v);
+            } else {
+                load8<C>(x + m * C, sub, v);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[k] = 0.f;
+        }
+        double s = 0.0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s += (double)v[k];
+        const double mean = group_sum<G>(s) / C;
+        double ss = 0.0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const double d = (double)v[k] - mean;
+            ss += d * d;
+        }
+        ss = group_sum<G>(ss);
+        if (!live) continue;
+        const float rstd = __double2float_rn(1.0 / sqrt(ss / C + eps));
+        const float shift = __fmul_rn(-rstd, __double2float_rn(mean));
+        int qv[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int c = chan8<C>(sub, k);
+            const float y = __fadd_rn(__fmul_rn(__fadd_rn(__fmul_rn(v[k], rstd), shift), sg[c]), sb[c]);
+            qv[k] = quant8(silu(y), scale);
+        }
+        store8_q8<C>(q + m * C, sub, qv);
+    }
+}
+
+template <int C, bool QUANT>
+__device__ __forceinline__ void pool_mean_rows(const float* __restrict__ x, const int32_t* __restrict__ seg_idx,
+                                               const int32_t* __restrict__ seg_off, const int32_t* __restrict__ count,
+                                               int64_t max_rows, float scale, int8_t* __restrict__ q,
+                                               float* __restrict__ out) {
+    constexpr int G = RowMap<C>::G, RPB = RowMap<C>::RPB;
+    const int64_t M = rows_of(count, max_rows);
+    const int sub = threadIdx.x % G;
+    for (int64_t o = (int64_t)blockIdx.x * RPB + threadIdx.x / G; o < M; o += (int64_t)gridDim.x * RPB) {
+        const int lo = seg_off[o], hi = seg_off[o + 1];
+        float acc[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+        for (int j = lo; j < hi; ++j) {
+            float v[8];
+            load8<C>(x + (int64_t)seg_idx[j] * C, sub, v);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) acc[k] = __fadd_rn(acc[k], v[k]);
+        }
+        const float n = (float)max(hi - lo, 1);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[k] = __fdiv_rn(acc[k], n);
+        if (QUANT) {
+            int qv[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) qv[k] = quant8(acc[k], scale);
+            store8_q8<C>(q + o * C, sub, qv);
+        } else {
+            store8<C>(out + o * C, sub, acc);
+        }
+    }
+}
+
+template <int C>
+__global__ void __launch_bounds__(256) k_pool_mean_rows_q(const float* __restrict__ x, const int32_t* __restrict__ seg_idx,
+                                                          const int32_t* __restrict__ seg_off,
+                                                          const int32_t* __restrict__ count, int64_t max_rows,
+                                                          float scale, int8_t* __restrict__ q, float* __restrict__ out) {
+    pool_mean_rows<C, true>(x, seg_idx, seg_off, count, max_rows, scale, q, out);
+}
+
+template <int C>
+__global__ void __launch_bounds__(256) k_pool_mean_rows_f(const float* __restrict__ x, const int32_t* __restrict__ seg_idx,
+                                                          const int32_t* __restrict__ seg_off,
+                                                          const int32_t* __restrict__ count, int64_t max_rows,
+                                                          float scale, int8_t* __restrict__ q, float* __restrict__ out) {
+    pool_mean_rows<C, false>(x, seg_idx, seg_off, count, max_rows, scale, q, out);
+}
+
+template <int C>
+__global__ void __launch_bounds__(256) k_input_proj_rows(const float* __restrict__ pc, const float* __restrict__ prompt,
+                                                         int64_t N, const float* __restrict__ wi,
+                                                         const float* __restrict__ bi, const float* __restrict__ wp,
+                                                         const float* __restrict__ bp, float* __restrict__ x0) {
+    constexpr int G = RowMap<C>::G, RPB = RowMap<C>::RPB;
+    __shared__ float s_wi[3 * C], s_bi[C], s_wp[2 * C], s_bp[C];
+    for (int i = threadIdx.x; i < C; i += blockDim.x) {
+        s_wi[3 * i] = wi[3 * i];
+        s_wi[3 * i + 1] = wi[3 * i + 1];
+        s_wi[3 * i + 2] = wi[3 * i + 2];
+        s_bi[i] = bi[i];
+        if (prompt) {
+            s_wp[2 * i] = wp[2 * i];
+            s_wp[2 * i + 1] = wp[2 * i + 1];
+            s_bp[i] = bp[i];
+        }
+    }
+    __syncthreads();
+    const int sub = threadIdx.x % G;
+    for (int64_t m = (int64_t)blockIdx.x * RPB + threadIdx.x / G; m < N; m += (int64_t)gridDim.x * RPB) {
+        const double p0 = pc[m * 3], p1 = pc[m * 3 + 1], p2 = pc[m * 3 + 2];
+        double r0 = 0.0, r1 = 0.0;
+        if (prompt) {
+            r0 = prompt[m * 2];
+            r1 = prompt[m * 2 + 1];
+        }
+        float y[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int n = chan8<C>(sub, k);
+            double a = p0 * (double)s_wi[n * 3];
+            a = fma(p1, (double)s_wi[n * 3 + 1], a);
+            a = fma(p2, (double)s_wi[n * 3 + 2], a);
+            float v = __double2float_rn(a + (double)s_bi[n]);
+            if (prompt) {
+                double b2 = r0 * (double)s_wp[n * 2];
+                b2 = fma(r1, (double)s_wp[n * 2 + 1], b2);
+                v = __fadd_rn(v, __double2float_rn(b2 + (double)s_bp[n]));
+            }
+            y[k] = v;
+        }
+        store8<C>(x0 + m * C, sub, y);
+    }
+}
+
+template <int C>
+__global__ void __launch_bounds__(256) k_out_apply_rows(const float* __restrict__ x, int64_t N,
+                                                        const float* __restrict__ wo, const float* __restrict__ bo,
+                                                        const float* __restrict__ pc_in, float* __restrict__ pc_out,
+                                                        float* __restrict__ delta_out) {
+    constexpr int G = RowMap<C>::G, RPB = RowMap<C>::RPB;
+    __shared__ float s_wo[C];
+    for (int i = threadIdx.x; i < C; i += blockDim.x) s_wo[i] = wo[i];
+    __syncthreads();
+    const int sub = threadIdx.x % G;
+    const double b0 = bo[0];
+    for (int64_t base = (int64_t)blockIdx.x * RPB; base < N; base += (int64_t)gridDim.x * RPB) {
+        const int64_t m = base + threadIdx.x / G;
+        const bool live = m < N;
+        double a = 0.0;
+        if (live) {
+            float v[8];
+            load8<C>(x + m * C, sub, v);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) a = fma((double)v[k], (double)s_wo[chan8<C>(sub, k)], a);
+        }
+        a = group_sum<G>(a);
+        if (live && sub == 0) {
+            const float d = __double2float_rn(a + b0);
+            if (delta_out) delta_out[m] = d;
+            const float lz = pc_in[m * 3 + 2];
+            pc_out[m * 3 + 0] = pc_in[m * 3 + 0];
+            pc_out[m * 3 + 1] = pc_in[m * 3 + 1];
+            pc_out[m * 3 + 2] = __fadd_rn(lz, d);
+        }
+    }
+}
+
 static int grid_for(int64_t work, int threads) {
     const int64_t g = (work + threads - 1) / threads;
     return (int)std::max<int64_t>(1, std::min<int64_t>(g, (int64_t)kNumSMs * 16));
@@ -196,10 +441,38 @@ int quantize(const float* x, int64_t n, float s, int8_t* q, cudaStream_t st) {
     return PMG_OK;
 }
 
+static int rows_grid(int64_t rows, int C) {
+    const int64_t rpb = 256 / (C / 8);
+    return (int)std::max<int64_t>(1, std::min<int64_t>((rows + rpb - 1) / rpb, (int64_t)kNumSMs * 16));
+}
+
+// 16-byte alignment of every row pointer the row-parallel forms touch
+static bool rows_ok(int C, std::initializer_list<const void*> ptrs) {
+    if (!(C == 32 || C == 64 || C == 128 || C == 256)) return false;
+    for (const void* p : ptrs)
+        if (reinterpret_cast<uintptr_t>(p) & 15) return false;
+    return true;
+}
+
+#define PMG_ROWS_DISPATCH(C, KERNEL, GRID_ROWS, ...)                                                        \
+    switch (C) {                                                                                            \
+        case 32: KERNEL<32><<<rows_grid(GRID_ROWS, 32), 256, 0, st>>>(__VA_ARGS__); break;                 \
+        case 64: KERNEL<64><<<rows_grid(GRID_ROWS, 64), 256, 0, st>>>(__VA_ARGS__); break;                 \
+        case 128: KERNEL<128><<<rows_grid(GRID_ROWS, 128), 256, 0, st>>>(__VA_ARGS__); break;              \
+        case 256: KERNEL<256><<<rows_grid(GRID_ROWS, 256), 256, 0, st>>>(__VA_ARGS__); break;              \
+        default: return PMG_ERR_UNSUPPORTED;                                                                \
+    }
+
 int ln_silu_q8(const float* x, const float* up_src, const int32_t* parent, const float* skip, float* x_out,
                const int32_t* count, int64_t max_rows, int C, const float* gamma, const float* beta, double eps,
                float scale, int8_t* q, cudaStream_t st) {
     if (max_rows == 0) return PMG_OK;
+    if (rows_ok(C, {x, up_src, skip, x_out, q})) {
+        PMG_ROWS_DISPATCH(C, k_ln_silu_rows, max_rows, x, up_src, parent, skip, x_out, count, max_rows, gamma, beta,
+                          eps, scale, q)
+        PMG_LAUNCH_CHECK();
+        return PMG_OK;
+    }
     const int grid = grid_for(max_rows * 32, 256);
     if (C <= 32) k_ln_silu_q8<1><<<grid, 256, 0, st>>>(x, up_src, parent, skip, x_out, count, max_rows, C, gamma, beta, eps, scale, q);
     else if (C <= 64) k_ln_silu_q8<2><<<grid, 256, 0, st>>>(x, up_src, parent, skip, x_out, count, max_rows, C, gamma, beta, eps, scale, q);
@@ -213,6 +486,15 @@ int ln_silu_q8(const float* x, const float* up_src, const int32_t* parent, const
 int pool_mean(const float* x, const int32_t* seg_idx, const int32_t* seg_off, const int32_t* count, int64_t max_rows,
               int C, float scale, int8_t* q, float* out, cudaStream_t st) {
     if (max_rows == 0) return PMG_OK;
+    if (rows_ok(C, {x, q, out})) {
+        if (q) {
+            PMG_ROWS_DISPATCH(C, k_pool_mean_rows_q, max_rows, x, seg_idx, seg_off, count, max_rows, scale, q, out)
+        } else {
+            PMG_ROWS_DISPATCH(C, k_pool_mean_rows_f, max_rows, x, seg_idx, seg_off, count, max_rows, scale, q, out)
+        }
+        PMG_LAUNCH_CHECK();
+        return PMG_OK;
+    }
     if (q) k_pool_mean<true><<<grid_for(max_rows * C, 256), 256, 0, st>>>(x, seg_idx, seg_off, count, max_rows, C, scale, q, nullptr);
     else k_pool_mean<false><<<grid_for(max_rows * C, 256), 256, 0, st>>>(x, seg_idx, seg_off, count, max_rows, C, scale, nullptr, out);
     PMG_LAUNCH_CHECK();
@@ -249,6 +531,12 @@ int planar_to_rows(const float* f, int B, int C, int T, float* out, cudaStream_t
 
 int input_proj(const float* pc, const float* prompt, int64_t N, int C, const float* wi, const float* bi,
                const float* wp, const float* bp, float* x0, cudaStream_t st) {
+    if (N == 0) return PMG_OK;
+    if (rows_ok(C, {x0})) {
+        PMG_ROWS_DISPATCH(C, k_input_proj_rows, N, pc, prompt, N, wi, bi, wp, bp, x0)
+        PMG_LAUNCH_CHECK();
+        return PMG_OK;
+    }
     k_input_proj<<<grid_for(N * C, 256), 256, 0, st>>>(pc, prompt, N, C, wi, bi, wp, bp, x0);
     PMG_LAUNCH_CHECK();
     return PMG_OK;
@@ -256,6 +544,12 @@ int input_proj(const float* pc, const float* prompt, int64_t N, int C, const flo
 
 int out_apply(const float* x, int64_t N, int C, const float* wo, const float* bo, const float* pc_in, float* pc_out,
               float* delta, cudaStream_t st) {
+    if (N == 0) return PMG_OK;
+    if (rows_ok(C, {x})) {
+        PMG_ROWS_DISPATCH(C, k_out_apply_rows, N, x, N, wo, bo, pc_in, pc_out, delta)
+        PMG_LAUNCH_CHECK();
+        return PMG_OK;
+    }
     k_out_apply<<<grid_for(N * 32, 256), 256, 0, st>>>(x, N, C, wo, bo, pc_in, pc_out, delta);
     PMG_LAUNCH_CHECK();
     return PMG_OK;

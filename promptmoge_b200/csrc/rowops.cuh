@@ -14,6 +14,8 @@ struct Epi {
     const float* resid;
     void* out;
     int32_t* status = nullptr;   // device status word for bounded-wait timeouts (tensor-core path)
+    int8_t* q2 = nullptr;        // F32 / F32_RESID: also write q(y, q2_scale) here (the next layer's int8 input)
+    float q2_scale = 0.f;
 };
 
 int gemm_i8_simt(const int8_t* in, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask, const int32_t* count,

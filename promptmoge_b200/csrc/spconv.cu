@@ -26,11 +26,13 @@ __device__ __forceinline__ void store_epi(const Epi& e, int64_t m, int n, int Co
             reinterpret_cast<int32_t*>(e.out)[o] = acc;
             break;
         case PMG_EPI_F32:
-            reinterpret_cast<float*>(e.out)[o] = dequant(acc, e.sa, e.ws[n], e.bias[n]);
+        case PMG_EPI_F32_RESID: {
+            float y = dequant(acc, e.sa, e.ws[n], e.bias[n]);
+            if (e.mode == PMG_EPI_F32_RESID) y = __fadd_rn(y, e.resid[o]);
+            reinterpret_cast<float*>(e.out)[o] = y;
+            if (e.q2) e.q2[o] = (int8_t)quant8(y, e.q2_scale);
             break;
-        case PMG_EPI_F32_RESID:
-            reinterpret_cast<float*>(e.out)[o] = __fadd_rn(dequant(acc, e.sa, e.ws[n], e.bias[n]), e.resid[o]);
-            break;
+        }
         default:
             reinterpret_cast<int8_t*>(e.out)[o] =
                 (int8_t)quant8(silu(dequant(acc, e.sa, e.ws[n], e.bias[n])), e.out_scale);

@@ -204,6 +204,7 @@ __device__ __forceinline__ void epi_store16(const Epi& e, const float* ws, const
     } else {
         float* d = reinterpret_cast<float*>(e.out) + o;
         const float* rs = e.mode == PMG_EPI_F32_RESID ? e.resid + o : nullptr;
+        uint32_t packed[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             float4 v;
@@ -211,15 +212,20 @@ __device__ __forceinline__ void epi_store16(const Epi& e, const float* ws, const
             float4 rr = make_float4(0.f, 0.f, 0.f, 0.f);
             if (rs) rr = *reinterpret_cast<const float4*>(rs + 4 * q);
             const float* prr = reinterpret_cast<const float*>(&rr);
+            uint32_t w = 0;
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
                 const int n = n0 + 4 * q + t;
                 float y = dequant((int)r[4 * q + t], e.sa, ws[n], bias[n]);
                 if (rs) y = __fadd_rn(y, prr[t]);
                 pv[t] = y;
+                if (e.q2) w |= ((uint32_t)(quant8(y, e.q2_scale) & 0xFF)) << (8 * t);
             }
+            packed[q] = w;
             *reinterpret_cast<float4*>(d + 4 * q) = v;
         }
+        if (e.q2)
+            *reinterpret_cast<int4*>(e.q2 + o) = make_int4((int)packed[0], (int)packed[1], (int)packed[2], (int)packed[3]);
     }
 }
 
