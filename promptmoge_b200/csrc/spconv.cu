@@ -151,8 +151,10 @@ int gemm_i8_simt(const int8_t* in, const int32_t* nmap, int64_t ld, const uint32
 int gemm_i8(const int8_t* in, int64_t in_rows, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask,
             const int32_t* count, int64_t max_rows, int Ci, int Co, int taps, const int8_t* w, int flags,
             const Epi& e, cudaStream_t s) {
-    if (!(flags & PMG_FLAG_SIMT) && tc_supported(Ci, Co))
-        return gemm_i8_tc(in, in_rows, nmap, ld, tile_mask, count, max_rows, Ci, Co, taps, w, e, s);
+    if (!(flags & PMG_FLAG_SIMT) && tc_supported(Ci, Co)) {
+        const int rc = gemm_i8_tc(in, in_rows, nmap, ld, tile_mask, count, max_rows, Ci, Co, taps, w, e, s);
+        if (rc != PMG_ERR_UNSUPPORTED) return rc;   // shapes the tensor-core kernel does not cover run SIMT
+    }
     return gemm_i8_simt(in, nmap, ld, tile_mask, count, max_rows, Ci, Co, taps, w, e, s);
 }
 

@@ -68,7 +68,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int LAG = C::kLag;
     constexpr int NCOLS = tmem_cols<NT>();
     constexpr uint32_t IDESC = instr_desc(kM, NT);
-    constexpr uint32_t kSboA = 8 * 128;              // gathered A: bytes between 8-row groups (8 K chunks of 128 B)
+    constexpr uint32_t kSboA = (kItemK / 16) * 128;  // gathered A: bytes between 8-row groups (K/16 chunks of 128 B)
     constexpr uint32_t kLboA = 128;                  // gathered A: bytes between K-adjacent core matrices
     constexpr int TPI = W < kItemK ? kItemK / W : 1;  // most taps per item
     constexpr int CPR = W / 16;                      // 16-byte chunks of one tap row in an item
@@ -94,14 +94,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        const uint32_t full_count = KIND == DENSE ? 1 : (RES ? kProducers : kProducers + 1);
+        // producer stages: one arrival per producer warp (lane 0 after __syncwarp) plus thread 0's TMA expect_tx
+        const uint32_t full_count = KIND == DENSE ? 1 : (RES ? kProducers / 32 : kProducers / 32 + 1);
         for (int s = 0; s < NST; ++s) {
             mbar_init(&full[s], full_count);
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 32 * kEpiWarps);
+            mbar_init(&acc_empty[b], kEpiWarps);
             mbar_init(&idx_full[b], kProducers + 1);
             mbar_init(&rec_full[b], 1);
             mbar_init(&rec_free[b], kProducers);
@@ -195,6 +196,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             // previous unit.
             const int r = threadIdx.x;
             const int my_c = lane % CPR, my_sub = lane / CPR;
+            const int my_row = 32 * warp + my_sub;                 // first row this lane copies (then + p * RPP)
+            // this lane's part of every copy: row group / row-in-group / 16-byte K chunk offsets in a stage
+            const uint32_t dst_lane = (uint32_t)((my_row >> 3) * kSboA + (my_row & 7) * 16 + my_c * kLboA);
+            const int8_t* in_lane = in + my_c * 16;
+            const uint32_t rows32 = (uint32_t)in_rows;             // in_rows < 2^31 and in_rows * Ci < 2^32
             uint32_t pend_first = 0;
             int pending = 0;
             const uint32_t idx_base = smem_u32(idx);
@@ -243,7 +249,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive(&rec_free[cb]);
                 const int mc = ra.y;
                 const int n0 = (int)(u % nblk) * NT;
-                const int32_t* cidx = idx + cb * 27 * kM;
+                const uint32_t cidx_base = idx_base + (uint32_t)(cb * 27 * kM + my_row) * 4u;
+                uint32_t row_live = 0;                      // bit p: row my_row + p * RPP is inside the tile
+#pragma unroll
+                for (int p = 0; p < CPR; ++p) row_live |= (my_row + p * RPP < mc ? 1u : 0u) << p;
                 bool prefetched = false;
                 uint32_t mk = (uint32_t)ra.z;
                 while (mk && ok) {
@@ -260,27 +269,43 @@ __global__ void __launch_bounds__(kThreads, 1)
                             for (int g = 0; g < TPI; ++g)
                                 if (g < nt) tma_tile2d(sa + C::kA + g * NT * W, &tmB, kb * W, tv[g] * Co + n0, &full[s]);
                         }
-                        const int koff = kb * W + my_c * 16;
+                        // all of the item's source rows first (independent shared loads), then the copies: the
+                        // copies' asm is a compiler memory barrier, so interleaving them would serialise the loads.
+                        // Row r of pass p is my_row + p * RPP; an index is valid when 0 <= id < in_rows (one unsigned
+                        // compare) and its row is inside the tile.
+                        uint32_t id[TPI][CPR];
+#pragma unroll
+                        for (int g = 0; g < TPI; ++g) {
+                            const uint32_t ia = cidx_base + (uint32_t)(tv[g] * kM) * 4u;
+#pragma unroll
+                            for (int p = 0; p < CPR; ++p) {
+                                const bool use = g < nt && ((row_live >> p) & 1u);
+                                id[g][p] = use ? (uint32_t)ld_shared_s32(ia + (uint32_t)(p * RPP) * 4u) : 0xFFFFFFFFu;
+                            }
+                        }
+                        const uint32_t koff = (uint32_t)(kb * W);
 #pragma unroll
                         for (int g = 0; g < TPI; ++g) {
                             if (g >= nt) break;
-                            const int v = tv[g];
-                            const int kc = g * CPR + my_c;                          // 16-byte K chunk in the item
 #pragma unroll
                             for (int p = 0; p < CPR; ++p) {
-                                const int rr = 32 * warp + p * RPP + my_sub;          // row within the tile
-                                int32_t id = rr < mc ? cidx[v * kM + rr] : -1;
-                                if (id >= in_rows) id = -1;
-                                const uint32_t dst = sa + (uint32_t)((rr >> 3) * kSboA + kc * kLboA + (rr & 7) * 16);
-                                cp_async16(dst, in + (int64_t)(id >= 0 ? id : 0) * Ci + koff, id >= 0);
+                                const bool valid = id[g][p] < rows32;
+                                // row my_row + p * RPP: whole 8-row groups plus a row offset that never carries
+                                // (my_row & 7 < RPP when RPP < 8)
+                                const uint32_t dst = sa + dst_lane +
+                                                     (uint32_t)(((p * RPP) >> 3) * kSboA + ((p * RPP) & 7) * 16 +
+                                                                g * CPR * kLboA);
+                                cp_async16(dst, in_lane + (valid ? id[g][p] * (uint32_t)Ci + koff : 0u), valid);
                             }
                         }
                         cp_async_commit();
                         ++pending;
                         if (pending > LAG) {
+                            // every lane's copies of the oldest pending item have landed: one arrival per warp
                             cp_async_wait<LAG>();
                             fence_proxy_async();
-                            mbar_arrive(&full[pend_first % NST]);
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(&full[pend_first % NST]);
                             ++pend_first;
                             --pending;
                         }
@@ -300,8 +325,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             cp_async_wait_all();
             fence_proxy_async();
+            __syncwarp();
             while (pending > 0) {
-                mbar_arrive(&full[pend_first % NST]);
+                if (lane == 0) mbar_arrive(&full[pend_first % NST]);
                 ++pend_first;
                 --pending;
             }
@@ -389,14 +415,23 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!mbar_wait(&acc_full[b], (t >> 1) & 1u, &s_abort)) { ok = false; break; }
             tc_fence_after();
             const int rr = 32 * q + lane;
+            const bool live = rr < mc;
+            const float* rrow = (e.mode == PMG_EPI_F32_RESID && live) ? e.resid + (m0 + rr) * Co + n0 : nullptr;
+            float4 rcur[4], rnext[4];
+            if (rrow) load_resid16(rrow, rcur);
 #pragma unroll 1
             for (int j = 0; j < NT / 16; ++j) {
+                // the next chunk's residual loads are in flight while this chunk is read from TMEM and stored
+                if (rrow && j + 1 < NT / 16) load_resid16(rrow + (j + 1) * 16, rnext);
                 uint32_t acc[16];
                 tmem_ld16(tmem + b * NCOLS + ((uint32_t)(32 * q) << 16) + (uint32_t)(j * 16), acc);
-                if (rr < mc) epi_store16(e, s_ws, s_bias, m0 + rr, n0 + j * 16, Co, acc);
+                if (live) epi_store16(e, s_ws, s_bias, m0 + rr, n0 + j * 16, Co, acc, rcur);
+#pragma unroll
+                for (int t4 = 0; t4 < 4; ++t4) rcur[t4] = rnext[t4];
             }
             tc_fence_before();
-            mbar_arrive(&acc_empty[b]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[b]);
         }
         if (!ok) {
             s_abort = 1;
@@ -531,6 +566,7 @@ int gemm_i8_tc(const int8_t* in, int64_t in_rows, const int32_t* nmap, int64_t l
                cudaStream_t s) {
     if (!tc_supported(Ci, Co) || (taps != 1 && taps != 27)) return PMG_ERR_UNSUPPORTED;
     if (in_rows <= 0 || in_rows >= INT32_MAX) return PMG_ERR_BAD_ARG;
+    if (taps == 27 && (uint64_t)in_rows * (uint64_t)Ci >= (1ull << 32)) return PMG_ERR_UNSUPPORTED;   // 32-bit offsets
     TcArgs a{in, in_rows, nmap, ld, tile_mask, count, max_rows, Ci, Co, taps, w};
     if (taps == 1) return dispatch<tc::DENSE>(a, e, s);
     return dispatch<tc::GATHER>(a, e, s);

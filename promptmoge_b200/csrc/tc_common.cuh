@@ -78,6 +78,11 @@ __device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
 }
+__device__ __forceinline__ int32_t ld_shared_s32(uint32_t addr) {
+    int32_t v;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+    return v;
+}
 __device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
 }
@@ -177,10 +182,16 @@ constexpr int tmem_cols() {
     return N <= 32 ? 32 : (N <= 64 ? 64 : (N <= 128 ? 128 : 256));
 }
 
+__device__ __forceinline__ void load_resid16(const float* p, float4 (&r)[4]) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) r[q] = reinterpret_cast<const float4*>(p)[q];
+}
+
 // Fused epilogue for 16 consecutive output channels n0.. of row m (ld = row pitch of the output in elements); ws and
-// bias are the per-channel weight scales and biases (shared-memory copies of e.ws / e.bias).
+// bias are the per-channel weight scales and biases (shared-memory copies of e.ws / e.bias); res holds the residual
+// of these 16 channels in F32_RESID mode (loaded ahead by the caller).
 __device__ __forceinline__ void epi_store16(const Epi& e, const float* ws, const float* bias, int64_t m, int n0,
-                                            int ld, const uint32_t (&r)[16]) {
+                                            int ld, const uint32_t (&r)[16], const float4 (&res)[4]) {
     const int64_t o = m * ld + n0;
     if (e.mode == PMG_EPI_ACC32) {
         int4* d = reinterpret_cast<int4*>(reinterpret_cast<int32_t*>(e.out) + o);
@@ -203,15 +214,13 @@ __device__ __forceinline__ void epi_store16(const Epi& e, const float* ws, const
             make_int4((int)packed[0], (int)packed[1], (int)packed[2], (int)packed[3]);
     } else {
         float* d = reinterpret_cast<float*>(e.out) + o;
-        const float* rs = e.mode == PMG_EPI_F32_RESID ? e.resid + o : nullptr;
+        const bool rs = e.mode == PMG_EPI_F32_RESID;
         uint32_t packed[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             float4 v;
             float* pv = reinterpret_cast<float*>(&v);
-            float4 rr = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (rs) rr = *reinterpret_cast<const float4*>(rs + 4 * q);
-            const float* prr = reinterpret_cast<const float*>(&rr);
+            const float* prr = reinterpret_cast<const float*>(&res[q]);
             uint32_t w = 0;
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
