@@ -66,6 +66,14 @@ int pmg_voxelize_l0(const float* point_coord, int32_t B, int32_t H, int32_t W, f
 int pmg_l0_coords(const int32_t* zq, const int32_t* zmin, int32_t B, int32_t H, int32_t W, int32_t* coords,
                   void* stream);
 
+/* Column CSR of a voxel set given as coords [M,4] int32 (b, i, j, z) sorted by (column, z), column = (b*H+i)*W+j,
+ * over a B x H x W x Z sparse shape: col_start [B*H*W+1] and z [M].  This is the order the refiner's levels have
+ * (pixel order at level 0, unique sorted keys after each pool, _core.py:339-392), so a caller holding only
+ * coordinates can hand a level to pmg_pool_frames / pmg_nmap_frames.  Coordinates out of range or out of order set
+ * PMG_ERR_RANGE in `status`.  coords 16-byte aligned.  No counterpart in the reference. */
+int pmg_frame_csr(const int32_t* coords, int64_t M, int32_t B, int32_t H, int32_t W, int64_t Z, int32_t* col_start,
+                  int32_t* z, int32_t* status, void* stream);
+
 /* Workspace for pmg_pool_frames. */
 size_t pmg_pool_frames_workspace_bytes(int32_t B, int32_t Hc, int32_t Wc);
 
@@ -171,6 +179,11 @@ int pmg_pool_mean_q8(const float* x, const int32_t* seg_indices, const int32_t* 
 /* Mean pool over CSR children in fp32 (the float sparse_pool of the reference, _core.py:444-481). */
 int pmg_pool_mean_f32(const float* x, const int32_t* seg_indices, const int32_t* seg_offsets,
                       const int32_t* coarse_count, int64_t max_rows, int32_t C, float* out, void* stream);
+
+/* Sum pool over CSR children in fp32 (sparse_pool reduce="sum", _core.py:444-481): children added in ascending
+ * fine index, one fp32 rounding per add. */
+int pmg_pool_sum_f32(const float* x, const int32_t* seg_indices, const int32_t* seg_offsets,
+                     const int32_t* coarse_count, int64_t max_rows, int32_t C, float* out, void* stream);
 
 /* Nearest upsample by parent (sparse_upsample, _core.py:484-505): out[m] = x[parent[m]]. */
 int pmg_gather_rows_f32(const float* x, const int32_t* parent, const int32_t* count, int64_t max_rows, int32_t C,

@@ -82,7 +82,7 @@ __global__ void k_ln_silu_q8(const float* __restrict__ x, const float* __restric
 template <bool QUANT>
 __global__ void k_pool_mean(const float* __restrict__ x, const int32_t* __restrict__ seg_idx,
                             const int32_t* __restrict__ seg_off, const int32_t* __restrict__ count, int64_t max_rows,
-                            int C, float scale, int8_t* __restrict__ q, float* __restrict__ out) {
+                            int C, float scale, int8_t* __restrict__ q, float* __restrict__ out, bool mean) {
     const int64_t M = rows_of(count, max_rows);
     const int64_t total = M * C;
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
@@ -91,9 +91,9 @@ __global__ void k_pool_mean(const float* __restrict__ x, const int32_t* __restri
         const int lo = seg_off[o], hi = seg_off[o + 1];
         float acc = 0.f;
         for (int k = lo; k < hi; ++k) acc = __fadd_rn(acc, x[(int64_t)seg_idx[k] * C + c]);
-        const float mean = __fdiv_rn(acc, (float)max(hi - lo, 1));
-        if (QUANT) q[e] = (int8_t)quant8(mean, scale);
-        else out[e] = mean;
+        const float r = mean ? __fdiv_rn(acc, (float)max(hi - lo, 1)) : acc;
+        if (QUANT) q[e] = (int8_t)quant8(r, scale);
+        else out[e] = r;
     }
 }
 
@@ -305,7 +305,7 @@ template <int C, bool QUANT>
 __device__ __forceinline__ void pool_mean_rows(const float* __restrict__ x, const int32_t* __restrict__ seg_idx,
                                                const int32_t* __restrict__ seg_off, const int32_t* __restrict__ count,
                                                int64_t max_rows, float scale, int8_t* __restrict__ q,
-                                               float* __restrict__ out) {
+                                               float* __restrict__ out, bool mean) {
     constexpr int G = RowMap<C>::G, RPB = RowMap<C>::RPB;
     const int64_t M = rows_of(count, max_rows);
     const int sub = threadIdx.x % G;
@@ -321,8 +321,9 @@ __device__ __forceinline__ void pool_mean_rows(const float* __restrict__ x, cons
             for (int k = 0; k < 8; ++k) acc[k] = __fadd_rn(acc[k], v[k]);
         }
         const float n = (float)max(hi - lo, 1);
+        if (mean)
 #pragma unroll
-        for (int k = 0; k < 8; ++k) acc[k] = __fdiv_rn(acc[k], n);
+            for (int k = 0; k < 8; ++k) acc[k] = __fdiv_rn(acc[k], n);
         if (QUANT) {
             int qv[8];
 #pragma unroll
@@ -338,16 +339,18 @@ template <int C>
 __global__ void __launch_bounds__(256) k_pool_mean_rows_q(const float* __restrict__ x, const int32_t* __restrict__ seg_idx,
                                                           const int32_t* __restrict__ seg_off,
                                                           const int32_t* __restrict__ count, int64_t max_rows,
-                                                          float scale, int8_t* __restrict__ q, float* __restrict__ out) {
-    pool_mean_rows<C, true>(x, seg_idx, seg_off, count, max_rows, scale, q, out);
+                                                          float scale, int8_t* __restrict__ q, float* __restrict__ out,
+                                                          bool mean) {
+    pool_mean_rows<C, true>(x, seg_idx, seg_off, count, max_rows, scale, q, out, mean);
 }
 
 template <int C>
 __global__ void __launch_bounds__(256) k_pool_mean_rows_f(const float* __restrict__ x, const int32_t* __restrict__ seg_idx,
                                                           const int32_t* __restrict__ seg_off,
                                                           const int32_t* __restrict__ count, int64_t max_rows,
-                                                          float scale, int8_t* __restrict__ q, float* __restrict__ out) {
-    pool_mean_rows<C, false>(x, seg_idx, seg_off, count, max_rows, scale, q, out);
+                                                          float scale, int8_t* __restrict__ q, float* __restrict__ out,
+                                                          bool mean) {
+    pool_mean_rows<C, false>(x, seg_idx, seg_off, count, max_rows, scale, q, out, mean);
 }
 
 template <int C>
@@ -484,19 +487,19 @@ int ln_silu_q8(const float* x, const float* up_src, const int32_t* parent, const
 }
 
 int pool_mean(const float* x, const int32_t* seg_idx, const int32_t* seg_off, const int32_t* count, int64_t max_rows,
-              int C, float scale, int8_t* q, float* out, cudaStream_t st) {
+              int C, float scale, int8_t* q, float* out, cudaStream_t st, bool mean) {
     if (max_rows == 0) return PMG_OK;
     if (rows_ok(C, {x, q, out})) {
         if (q) {
-            PMG_ROWS_DISPATCH(C, k_pool_mean_rows_q, max_rows, x, seg_idx, seg_off, count, max_rows, scale, q, out)
+            PMG_ROWS_DISPATCH(C, k_pool_mean_rows_q, max_rows, x, seg_idx, seg_off, count, max_rows, scale, q, out, mean)
         } else {
-            PMG_ROWS_DISPATCH(C, k_pool_mean_rows_f, max_rows, x, seg_idx, seg_off, count, max_rows, scale, q, out)
+            PMG_ROWS_DISPATCH(C, k_pool_mean_rows_f, max_rows, x, seg_idx, seg_off, count, max_rows, scale, q, out, mean)
         }
         PMG_LAUNCH_CHECK();
         return PMG_OK;
     }
-    if (q) k_pool_mean<true><<<grid_for(max_rows * C, 256), 256, 0, st>>>(x, seg_idx, seg_off, count, max_rows, C, scale, q, nullptr);
-    else k_pool_mean<false><<<grid_for(max_rows * C, 256), 256, 0, st>>>(x, seg_idx, seg_off, count, max_rows, C, scale, nullptr, out);
+    if (q) k_pool_mean<true><<<grid_for(max_rows * C, 256), 256, 0, st>>>(x, seg_idx, seg_off, count, max_rows, C, scale, q, nullptr, mean);
+    else k_pool_mean<false><<<grid_for(max_rows * C, 256), 256, 0, st>>>(x, seg_idx, seg_off, count, max_rows, C, scale, nullptr, out, mean);
     PMG_LAUNCH_CHECK();
     return PMG_OK;
 }
@@ -584,6 +587,13 @@ extern "C" int pmg_pool_mean_f32(const float* x, const int32_t* seg_indices, con
                                  const int32_t* coarse_count, int64_t max_rows, int32_t C, float* out, void* stream) {
     if (!x || !seg_indices || !seg_offsets || !out || C <= 0 || max_rows < 0) return PMG_ERR_BAD_ARG;
     return pool_mean(x, seg_indices, seg_offsets, coarse_count, max_rows, C, 0.f, nullptr, out, as_stream(stream));
+}
+
+extern "C" int pmg_pool_sum_f32(const float* x, const int32_t* seg_indices, const int32_t* seg_offsets,
+                                const int32_t* coarse_count, int64_t max_rows, int32_t C, float* out, void* stream) {
+    if (!x || !seg_indices || !seg_offsets || !out || C <= 0 || max_rows < 0) return PMG_ERR_BAD_ARG;
+    return pool_mean(x, seg_indices, seg_offsets, coarse_count, max_rows, C, 0.f, nullptr, out, as_stream(stream),
+                     false);
 }
 
 extern "C" int pmg_gather_rows_f32(const float* x, const int32_t* parent, const int32_t* count, int64_t max_rows,

@@ -37,7 +37,7 @@ int ln_silu_q8(const float* x, const float* up_src, const int32_t* parent, const
                const int32_t* count, int64_t max_rows, int C, const float* gamma, const float* beta, double eps,
                float scale, int8_t* q, cudaStream_t st);
 int pool_mean(const float* x, const int32_t* seg_idx, const int32_t* seg_off, const int32_t* count, int64_t max_rows,
-              int C, float scale, int8_t* q, float* out, cudaStream_t st);
+              int C, float scale, int8_t* q, float* out, cudaStream_t st, bool mean = true);
 int gather_rows(const float* x, const int32_t* parent, const int32_t* count, int64_t max_rows, int C, float* out,
                 cudaStream_t st);
 int concat_q8(const float* x, const float* enc_tok, const int32_t* col, const int32_t* count, int64_t max_rows, int C,

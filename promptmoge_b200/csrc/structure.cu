@@ -478,6 +478,50 @@ extern "C" int pmg_pool_frames(int32_t B, int32_t Hf, int32_t Wf, const int32_t*
     return PMG_OK;
 }
 
+// Column CSR of a voxel set sorted by (column, z) over a B x H x W column grid.  Thread m (0..M) writes
+// col_start[c] = m for every column c in (column(m-1), column(m)], the tail thread m = M closing the array, so each
+// entry is written exactly once.  Out-of-range or out-of-order voxels set PMG_ERR_RANGE and write nothing.
+__global__ void k_frame_csr(const int32_t* __restrict__ coords, int64_t M, int B, int H, int W, int64_t Z,
+                            int32_t* __restrict__ col_start, int32_t* __restrict__ z_out, int32_t* __restrict__ status) {
+    const int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (m > M) return;
+    const int64_t ncol = (int64_t)B * H * W;
+    auto column = [&](int64_t k, int64_t& c, int32_t& zz) -> bool {
+        const int4 v = reinterpret_cast<const int4*>(coords)[k];
+        zz = v.w;
+        if (v.x < 0 || v.x >= B || v.y < 0 || v.y >= H || v.z < 0 || v.z >= W || v.w < 0 || v.w >= Z) return false;
+        c = ((int64_t)v.x * H + v.y) * W + v.z;
+        return true;
+    };
+    int64_t c_cur = ncol, c_prev = -1;
+    int32_t z_cur = 0, z_prev = 0;
+    if (m < M) {
+        if (!column(m, c_cur, z_cur)) {
+            flag(status, PMG_ERR_RANGE);
+            return;
+        }
+        z_out[m] = z_cur;
+    }
+    if (m > 0) {
+        if (!column(m - 1, c_prev, z_prev)) return;      // reported by thread m - 1
+        if (m < M && (c_prev > c_cur || (c_prev == c_cur && z_prev >= z_cur))) {
+            flag(status, PMG_ERR_RANGE);
+            return;
+        }
+    }
+    for (int64_t c = c_prev + 1; c <= c_cur; ++c) col_start[c] = (int32_t)m;
+}
+
+extern "C" int pmg_frame_csr(const int32_t* coords, int64_t M, int32_t B, int32_t H, int32_t W, int64_t Z,
+                             int32_t* col_start, int32_t* z, int32_t* status, void* stream) {
+    if ((M > 0 && (!coords || !z)) || !col_start || M < 0 || M >= INT32_MAX || B <= 0 || H <= 0 || W <= 0 || Z <= 0)
+        return PMG_ERR_BAD_ARG;
+    if ((int64_t)B * H * W >= INT32_MAX || (reinterpret_cast<uintptr_t>(coords) & 15)) return PMG_ERR_BAD_ARG;
+    k_frame_csr<<<ceil_div(M + 1, 256), 256, 0, as_stream(stream)>>>(coords, M, B, H, W, Z, col_start, z, status);
+    PMG_LAUNCH_CHECK();
+    return PMG_OK;
+}
+
 extern "C" int pmg_nmap_frames(int32_t B, int32_t H, int32_t W, const int32_t* count, const int32_t* z,
                                const int32_t* col, const int32_t* col_start, int32_t* nmap, int64_t ld,
                                uint32_t* tile_mask, void* stream) {

@@ -173,6 +173,25 @@ def ln_silu_q8(x, gamma, beta, scale, eps=1e-6, up_src=None, parent=None, skip=N
     return (q, x_out) if up_src is not None else q
 
 
+def frame_csr(coords, B, H, W, Z, status=None):
+    """Column CSR (col_start [B*H*W+1], z [M]) of coords [M,4] sorted by (column, z)."""
+    _dev(coords, torch.int32, "coords")
+    M = coords.shape[0]
+    dev = coords.device
+    col_start = torch.empty(B * H * W + 1, dtype=torch.int32, device=dev)
+    z = torch.empty(max(M, 1), dtype=torch.int32, device=dev)
+    st = status if status is not None else torch.zeros(1, dtype=torch.int32, device=dev)
+    call("pmg_frame_csr", _p(coords), M, B, H, W, int(Z), _p(col_start), _p(z), _p(st), _stream())
+    return col_start, z[:M], st
+
+
+def pool_sum(x, seg_indices, seg_offsets, rows, count=None):
+    C_ = x.shape[1]
+    out = torch.empty((rows, C_), dtype=torch.float32, device=x.device)
+    call("pmg_pool_sum_f32", _p(x), _p(seg_indices), _p(seg_offsets), _p(count), rows, C_, _p(out), _stream())
+    return out
+
+
 def pool_mean(x, seg_indices, seg_offsets, rows, scale=None, count=None):
     C_ = x.shape[1]
     if scale is None:
