@@ -158,6 +158,26 @@ int pmg_dense_i8(const int8_t* a_q8, const int32_t* count, int64_t max_rows, int
 
 
 /* --------------------------------------------------------------------------------------------------------------
+ * Polynomial prompt gauge
+ * ------------------------------------------------------------------------------------------------------------ */
+
+/* Workspace for pmg_gauge_poly over B frames with an h x w sensor grid. */
+size_t pmg_gauge_workspace_bytes(int32_t B, int32_t h, int32_t w);
+
+/* Per-frame polynomial gauge (MoGeModel.prompt_gauge_poly, moge/model/v3.py:151-183; applied by infer,
+ * v3.py:841-846): the prediction `depth` [B,H,W] is area-averaged onto the sensor grid over finite positive pixels,
+ * log(max(lidar,1e-3)) - log(max(z,1e-3)) on confident pixels (conf >= 2, lidar > 0, z > 0; conf NULL = all) is
+ * fitted by a degree-1 or degree-2 polynomial in (u, v) = linspace(-1, 1) of the sensor grid with `iters`
+ * reweighted least-squares solves (weights min(2 * (1.4826 * lower-median|r| + 1e-4) / max(|r|, 1e-6), 1)); frames
+ * with fewer than 200 confident pixels or a singular / non-finite solve get no correction.  Outputs (each may be
+ * NULL): corr [B,H,W] = exp(poly) on the image grid, depth_out [B,H,W] = depth * corr (may alias depth), points
+ * [B,H,W,3] multiplied by corr in place, coef_out [B][8] = 6 coefficients (3 used at degree 1), ok, confident
+ * count.  The reference solves each system with LAPACK in fp32; here fp64 normal equations (~1e-6 relative). */
+int pmg_gauge_poly(const float* depth, const float* lidar, const float* conf, int32_t B, int32_t H, int32_t W,
+                   int32_t h, int32_t w, int32_t degree, int32_t iters, float* corr, float* depth_out, float* points,
+                   float* coef_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* --------------------------------------------------------------------------------------------------------------
  * Refiner glue
  * ------------------------------------------------------------------------------------------------------------ */
 

@@ -46,6 +46,8 @@ SIGNATURES = {
     "pmg_nmap_hash": (I32, [P, I64, C.POINTER(I64), P, I64, I32, P, P, SZ, P, P]),
     "pmg_nmap_hash_noalloc": (I32, [P, I64, C.POINTER(I64), P, I64, I32, P, P, P]),
     "pmg_frame_csr": (I32, [P, I64, I32, I32, I32, I64, P, P, P, P]),
+    "pmg_gauge_workspace_bytes": (SZ, [I32, I32, I32]),
+    "pmg_gauge_poly": (I32, [P, P, P, I32, I32, I32, I32, I32, I32, I32, P, P, P, P, P, SZ, P]),
     "pmg_spconv_i8": (I32, [P, I64, P, I64, P, P, I64, I32, I32, P, P, P, F32, I32, F32, P, P, I32, P, P]),
     "pmg_dense_i8": (I32, [P, P, I64, I32, I32, P, P, P, F32, I32, F32, P, P, I32, P, P]),
     "pmg_quantize": (I32, [P, I64, F32, P, P]),

@@ -296,3 +296,25 @@ def apply_affine(depth, state):
     B = depth.shape[0]
     call("pmg_apply_affine", _p(depth), _p(state), B, depth[0].numel(), _stream())
     return depth
+
+
+# ----------------------------------------------------------------------------------------------------------------- #
+# Polynomial prompt gauge
+# ----------------------------------------------------------------------------------------------------------------- #
+def gauge_poly(depth, lidar, conf=None, degree: int = 2, iters: int = 3, points=None, in_place: bool = False):
+    """Per-frame gauge of depth [B,H,W] to lidar [B,h,w] (conf [B,h,w] or None).  Returns (corr [B,H,W],
+    corrected depth [B,H,W] (depth itself when in_place), coef [B,8] = 6 coefficients, ok, count); points
+    [B,H,W,3], when given, is multiplied by corr in place."""
+    _dev(depth, torch.float32, "depth")
+    _dev(lidar, torch.float32, "lidar")
+    B, H, W = depth.shape
+    h, w = lidar.shape[-2:]
+    dev = depth.device
+    corr = torch.empty((B, H, W), dtype=torch.float32, device=dev)
+    out = depth if in_place else torch.empty_like(depth)
+    coef = torch.empty((B, 8), dtype=torch.float32, device=dev)
+    nbytes = _lib.load().pmg_gauge_workspace_bytes(B, h, w)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    call("pmg_gauge_poly", _p(depth), _p(lidar.contiguous()), _p(conf.contiguous() if conf is not None else None), B,
+         H, W, h, w, degree, iters, _p(corr), _p(out), _p(points), _p(coef), _p(ws), nbytes, _stream())
+    return corr, out, coef
