@@ -23,8 +23,8 @@
 // width W = min(Ci, 128)); a conv whose whole 27-tap weight fits (Co = NT, Ci < 128) keeps it resident in shared
 // memory for the kernel's lifetime.  Gathered A operands use the K-major no-swizzle core-matrix layout with the 8-row
 // groups outermost ([16 row groups][8 K chunks][8 rows][16 bytes]), so a warp's 16-byte writes hit distinct banks.
-// No multicast anywhere.  Every wait is bounded: on timeout the CTA records PMG_ERR_TIMEOUT in the status word, lets
-// issued MMAs retire, frees its TMEM and returns.
+// Every TMA copy lands in this CTA's own shared memory.  Every wait is bounded: on timeout the CTA records
+// PMG_ERR_TIMEOUT in the status word, lets issued MMAs retire, frees its TMEM and returns.
 #include <algorithm>
 #include <mutex>
 
