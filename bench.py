@@ -28,6 +28,10 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "refine steps/s (Model A, 480x640, K=1)"
+METRIC_B = "refine steps/s (Model B, 240x320, K=1)"
+# the only published numbers for this path (int8 Metal, iPad Pro 11" M5, warm, K = 1)
+PUBLISHED_MS = {"A": 27.3, "B": 10.4}
+PUBLISHED_STEPS_S = {k: 1000.0 / v for k, v in PUBLISHED_MS.items()}
 UNIT = "steps/s"
 
 
@@ -168,10 +172,12 @@ def run_ours(args, ws, rank, local):
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    weights, clips = synthetic_model("A", 0)
+    mdl = synth.MODELS[args.model]
+    weights, clips = synthetic_model(args.model, 0)
     batch = args.batch
-    ref = Refiner(weights, clips, "A", batch=batch, device=dev)
-    sc = synth.make_scene(1000 * rank, 480, 640, 16, 256, batch=batch)
+    ref = Refiner(weights, clips, args.model, batch=batch, device=dev)
+    sc = synth.make_scene(1000 * rank, mdl["H"], mdl["W"], mdl["encoder_downsample"], mdl["model_channels"][-1],
+                          batch=batch)
     h_pc, h_ld, h_lc = pinned(sc.point_coord), pinned(sc.lidar_depth), pinned(sc.lidar_conf)
     h_enc, h_uv = pinned(sc.encoder_feature), pinned(sc.uv_bias)
     # first call sizes the plan: run once, shrink level capacities to the measured counts (+25 %), recapture
@@ -250,32 +256,50 @@ def run_ours(args, ws, rank, local):
     line = None
     if rank == 0:
         launches = eng.launches_per_step() * args.K
-        # roofline of the dominant kernel
+        # roofline of the dominant kernel: the conv level with the largest per-step time.  Convs with C <= 64 are
+        # bandwidth-bound (minimum traffic M*Ci + M*Co + 27*4*M + 27*Ci*Co bytes), wider ones tensor-bound (2 * occupied
+        # taps * Ci * Co ops); the int8 peak is measured in this run (MEASURED_PEAKS.json holds bf16 only).
         convs = dominant_conv(torch, eng)
         dom = max(convs, key=lambda r: r["per_step"])
-        peak = int8_peak_tops(torch)
-        achieved = dom["ops"] / (dom["ms"] * 1e-3) / 1e12
+        tops = dom["ops"] / (dom["ms"] * 1e-3) / 1e12
+        peak_i8 = int8_peak_tops(torch)
         traffic = None
-        tfile = ROOT / "profiles" / "traffic.json"
-        if tfile.exists():
-            tj = json.loads(tfile.read_text())
-            traffic = tj.get(f"conv_L{dom['level']}")
-        roof = {"bound": "tensor", "achieved": round(achieved, 3), "peak": round(peak, 1), "unit": "TOP/s",
-                "frac": round(achieved / peak, 5), "traffic": traffic,
-                "kernel": f"int8 submanifold conv level {dom['level']} (M={dom['M']}, C={dom['C']})",
-                "peak_source": "measured in this run: cuBLASLt int8 GEMM (torch._int_mm 8192^3, best of 10); "
-                               "MEASURED_PEAKS.json has no int8 figure",
-                "per_level_ms": {f"L{r['level']}": round(r["ms"], 4) for r in convs}}
+        prof = ROOT / "profiles" / f"conv_i8_L{dom['level']}_A480x640_ncu.md"
+        if prof.exists():
+            for ln in prof.read_text().splitlines():
+                if ln.startswith("dram_bytes_per_launch:"):
+                    traffic = int(ln.split(":")[1])
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+        hbm = float(peaks.get("hbm_gbs", 6650.0))
+        if dom["C"] <= 64:
+            gbs = dom["bytes"] / (dom["ms"] * 1e-3) / 1e9
+            roof = {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s", "frac": round(gbs / hbm, 5),
+                    "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if peaks else "fallback 6650 GB/s"}
+        else:
+            roof = {"bound": "tensor", "achieved": round(tops, 3), "peak": round(peak_i8, 1), "unit": "TOP/s",
+                    "frac": round(tops / peak_i8, 5),
+                    "peak_source": "measured in this run: cuBLASLt int8 GEMM (torch._int_mm 8192^3, best of 10)"}
+        roof.update({"traffic": traffic, "algorithmic_bytes": dom["bytes"],
+                     "kernel": f"int8 submanifold conv level {dom['level']} (M={dom['M']}, C={dom['C']}), k_gemm_tc",
+                     "int8_tops": round(tops, 3), "int8_peak_tops": round(peak_i8, 1),
+                     "traffic_source": f"profiles/{prof.name} (ncu dram bytes read + written, one launch)",
+                     "per_level_ms": {f"L{r['level']}": round(r["ms"], 4) for r in convs}})
         cpu = None
-        if ws == 1 and not args.no_cpu_baseline:
+        if ws == 1 and not args.no_cpu_baseline and args.model == "A":
             cpu = cpu_baseline(batch=1, steps=1)
         line = {
-            "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+            "metric": METRIC if args.model == "A" else METRIC_B, "value": round(value, 3), "unit": UNIT, "n_gpus": ws,
+            "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": "C2: Model A refiner (widths 32-64-128-256-256), 1 refine step, 480x640, "
-                                   f"batch {batch} per GPU, synthetic room (seed = 1000*rank)",
-                       "model": "PromptMoGe Model A sparse refiner (random-init int8 QAT weights)",
+            "scaling": "weak", "vs_baseline": round(value / PUBLISHED_STEPS_S[args.model], 3),
+            "vs_baseline_basis": f"the reference's published int8 Metal time for one refine step of Model "
+                                 f"{args.model} on an iPad Pro M5 ({PUBLISHED_MS[args.model]} ms, docs/index.html:453)",
+            "dtype": "int8", "data": "synthetic",
+            "config": {"workload": (f"C2: Model A refiner (widths 32-64-128-256-256), 1 refine step, 480x640, "
+                                    if args.model == "A" else
+                                    "C1: Model B refiner (widths 32-64-128-256), 1 refine step, 240x320, ")
+                                   + f"batch {batch} per GPU, synthetic room (seed = 1000*rank)",
+                       "model": f"PromptMoGe Model {args.model} sparse refiner (random-init int8 QAT weights)",
                        "K": args.K, "global_batch": ws * batch, "parallelism": f"frame-batch x{ws}",
                        "levels_voxels": counts, "l2": "flushed by a 256 MiB write before every timed step",
                        "timing": "CUDA events around each graph replay, max over ranks"},
@@ -339,6 +363,51 @@ def profile_conv(args):
     return {"profile_conv": k, "M": M, "C": C_, "occupied_taps": nnz, "path": "tcgen05" if tc_path else "simt"}
 
 
+def conv_sweep(args):
+    """the isolated int8 submanifold conv on surface-shell voxel sets (about 9 occupied taps per
+    voxel) of N in {1e5, 5e5, 2e6, 8e6} voxels, C in {16, 32, 64, 128}: neighbour map by the hash builder, then the
+    conv (tcgen05 where the width allows, SIMT dp4a at C = 16) with the SiLU + requantise epilogue, timed alone with
+    CUDA events (median of --steps, inputs 2-128 MB, L2 flushed before each launch).  One JSON line per (N, C) with
+    voxel*GOPS = 2 * occupied taps * C * C / t."""
+    import torch
+    from promptmoge_b200 import ops, synth
+    torch.cuda.set_device(0)
+    flush = torch.empty(256 << 18, dtype=torch.float32, device="cuda")
+    sizes = [int(x) for x in args.sweep_n.split(",")]
+    for N in sizes:
+        coords = torch.from_numpy(synth.make_surface_voxels(N, seed=N % 97)).cuda()
+        M = coords.shape[0]
+        nmap, mask, st = ops.nmap_hash(coords, [1, 1 << 21, 1 << 21, 1 << 21])
+        if int(st.item()) != 0:
+            raise RuntimeError("hash neighbour map failed")
+        nnz = int((nmap >= 0).sum().item())
+        for C in (16, 32, 64, 128):
+            g = torch.Generator(device="cuda").manual_seed(C)
+            q = torch.randint(-127, 127, (M, C), dtype=torch.int8, device="cuda", generator=g)
+            w = torch.randint(-127, 127, (27, C, C), dtype=torch.int8, device="cuda", generator=g)
+            ws_ = torch.full((C,), 1e-3, device="cuda")
+            b = torch.zeros(C, device="cuda")
+            run = lambda: ops.spconv_i8(q, nmap, mask, w, ws_, b, 0.01, ops.EPI_SILU_Q8, 0.02)
+            for _ in range(3):
+                run()
+            torch.cuda.synchronize()
+            ts = []
+            for _ in range(max(3, args.steps)):
+                flush.zero_()
+                s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s0.record()
+                run()
+                e0.record()
+                torch.cuda.synchronize()
+                ts.append(s0.elapsed_time(e0))
+            t = float(np.median(ts))
+            print(json.dumps({"metric": "int8 sparse-conv voxel*GOPS (C3)", "value": round(2.0 * nnz * C * C / (t * 1e-3) / 1e9, 1),
+                              "unit": "GOPS", "N": M, "C": C, "ms": round(t, 4), "occupied_taps_per_voxel":
+                              round(nnz / M, 2), "path": "tcgen05" if ops.tc_supported(C, C) else "simt",
+                              "data": "synthetic surface shells", "l2": "flushed before each launch"}), flush=True)
+        del nmap, mask
+
+
 def run_reference(args, ws, rank):
     """Reference arm: the reference's CPU algorithm (the oracle port) on the host cores, rank 0 only."""
     if rank != 0:
@@ -383,9 +452,16 @@ def main():
     ap.add_argument("--profile-conv", type=int, default=None, metavar="LEVEL",
                     help="profiling driver: launch one level's conv --steps times on the benchmark frame's structure")
     ap.add_argument("--simt", action="store_true", help="with --profile-conv: the SIMT kernel instead of tcgen05")
+    ap.add_argument("--model", choices=["A", "B"], default="A",
+                    help="A: the headline config (480x640); B: config 1 (Model B, 240x320)")
+    ap.add_argument("--conv-sweep", action="store_true", help="config 3: isolated int8 conv sweep (one line per N, C)")
+    ap.add_argument("--sweep-n", default="100000,500000,2000000,8000000")
     args = ap.parse_args()
     if args.profile_conv is not None:
         print(json.dumps(profile_conv(args)), flush=True)
+        return
+    if args.conv_sweep:
+        conv_sweep(args)
         return
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
