@@ -140,8 +140,15 @@ def dominant_conv(torch, eng, reps: int = 20):
         b = torch.zeros(C_, device="cuda")
         nnz = int((nmap[:, :M] >= 0).sum().item())
         tc = bool(eng.tensor_cores) and ops.tc_supported(C_, C_)
-        run = lambda: ops.spconv_i8(q1, nmap, mask, w, ws, b, 0.01, ops.EPI_SILU_Q8, 0.02, count=cnt,
-                                    tensor_cores=tc)
+        if k == 0 and bool(eng.tensor_cores) and ops.grid0_supported(C_, C_):
+            # level 0 runs the neighbour-map-free frame-grid kernel in the plan
+            g = eng.geo
+            zq = eng.debug_tensor("zq", 0, (g.batch * g.height * g.width,), torch.int32)
+            run = lambda: ops.spconv_i8_grid0(q1, zq, g.batch, g.height, g.width, w, ws, b, 0.01, ops.EPI_SILU_Q8,
+                                              0.02)
+        else:
+            run = lambda: ops.spconv_i8(q1, nmap, mask, w, ws, b, 0.01, ops.EPI_SILU_Q8, 0.02, count=cnt,
+                                        tensor_cores=tc)
 
         def timed(fn):
             fn()
@@ -280,7 +287,8 @@ def run_ours(args, ws, rank, local):
                     "frac": round(tops / peak_i8, 5),
                     "peak_source": "measured in this run: cuBLASLt int8 GEMM (torch._int_mm 8192^3, best of 10)"}
         roof.update({"traffic": traffic, "algorithmic_bytes": dom["bytes"],
-                     "kernel": f"int8 submanifold conv level {dom['level']} (M={dom['M']}, C={dom['C']}), k_gemm_tc",
+                     "kernel": f"int8 submanifold conv level {dom['level']} (M={dom['M']}, C={dom['C']}), "
+                               + ("k_conv_grid0" if dom["level"] == 0 and eng.tensor_cores else "k_gemm_tc"),
                      "int8_tops": round(tops, 3), "int8_peak_tops": round(peak_i8, 1),
                      "traffic_source": f"profiles/{prof.name} (ncu dram bytes read + written, one launch)",
                      "per_level_ms": {f"L{r['level']}": round(r["ms"], 4) for r in convs}})

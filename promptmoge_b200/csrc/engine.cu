@@ -295,10 +295,14 @@ int check_weights(pmg_refiner* r) {
 
 int flags_of(const pmg_refiner* r) { return r->cfg.use_tensor_cores ? 0 : PMG_FLAG_SIMT; }
 
-int conv(const pmg_refiner* r, const LevelBuf& l, const int8_t* in, const QL& q, int mode, float out_scale,
+// Level 0 (one voxel per pixel) runs the neighbour-map-free frame-grid conv on the tensor-core path; the other
+// levels gather through their neighbour maps.
+int conv(const pmg_refiner* r, int k, const LevelBuf& l, const int8_t* in, const QL& q, int mode, float out_scale,
          const float* resid, void* out, const int32_t* count, cudaStream_t s, int8_t* q2 = nullptr,
          float q2_scale = 0.f) {
     Epi e{mode, q.sa, out_scale, q.ws, q.b, resid, out, r->status, q2, q2_scale};
+    if (k == 0 && r->cfg.use_tensor_cores && grid0_supported(l.C, l.C))
+        return conv_grid0_tc(in, r->zq, r->cfg.batch, r->cfg.height, r->cfg.width, l.C, l.C, q.w, e, s);
     return gemm_i8(in, l.cap, l.nmap, l.cap, l.mask, count, l.cap, l.C, l.C, 27, q.w, flags_of(r), e, s);
 }
 
@@ -316,8 +320,8 @@ int resblock(pmg_refiner* r, int k, const RB& b, const float* up_src, const int3
     LevelBuf& l = r->lv[k];
     const int32_t* cnt = r->counts + 2 * k;
     LAUNCH(ln_silu_q8(l.X, up_src, parent, l.S, l.X, cnt, l.cap, l.C, b.norm.g, b.norm.b, 1e-6, b.c1.sa, l.q1, s));
-    LAUNCH(conv(r, l, l.q1, b.c1, PMG_EPI_SILU_Q8, b.c2.sa, nullptr, l.q2, cnt, s));
-    LAUNCH(conv(r, l, l.q2, b.c2, PMG_EPI_F32_RESID, 0.f, l.X, l.S, cnt, s, uq, uq_scale));
+    LAUNCH(conv(r, k, l, l.q1, b.c1, PMG_EPI_SILU_Q8, b.c2.sa, nullptr, l.q2, cnt, s));
+    LAUNCH(conv(r, k, l, l.q2, b.c2, PMG_EPI_F32_RESID, 0.f, l.X, l.S, cnt, s, uq, uq_scale));
     return PMG_OK;
 }
 

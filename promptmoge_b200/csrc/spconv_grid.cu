@@ -1,0 +1,354 @@
+// Level-0 submanifold conv on a frame grid: shifted TMA slabs + lane-masked tcgen05 MMAs (no gather).
+//
+// Level 0 of the refiner holds exactly one voxel per pixel, stored in pixel order (m = (b*H + i)*W + j), and the
+// neighbour of voxel m at tap (di, dj, dz) is pixel q = m + di*W + dj whenever that pixel is inside the frame and
+// zq[q] - zq[m] == dz (_core.py:269-295; the 27-tap order is v = (di+1)*9 + (dj+1)*3 + (dz+1), _core.py:65-82).
+// So for a tile of 128 consecutive output rows the A operand of every tap with spatial offset (di, dj) is the
+// CONTIGUOUS input slab rows [m0 + di*W + dj, +128): one 2-D TMA tile load, no per-row gather.  What differs between
+// the three taps of one spatial offset, and between rows, is only WHICH output rows the tap applies to; that is
+// exactly tcgen05.mma's disable-output-lane mask (one bit per accumulator row / TMEM lane).  Per tile:
+//   9 slab loads (rows past either end of the input read as zero), 27 MMAs (M = 128, N = Co, K = Ci) each with its
+//   tap's 128-bit row mask; the centre tap (0, 0, 0) is present for every voxel, so it runs first, unmasked, and
+//   initialises the accumulator.  A tap no row of the tile uses is skipped.
+// int32 accumulation is exact, so the accumulators equal the gather kernel's (and the reference's) bit for bit.
+//
+// Warp roles (256 threads, one persistent CTA per SM, tiles round-robin):
+//   warp 0       lane 0 issues the TMA loads: the 27-tap weight once (resident in shared memory), then per tile the
+//                9 slabs into an NS-stage ring.
+//   warp 1       lane 0 issues the MMAs into one of two TMEM accumulators and commits stages / accumulators.
+//   warps 2-3    build each tile's 27 x 128-bit masks from zq (bounds of the frame + the z difference), one ballot
+//                per (tap, 32-row group), into a ring of NR mask records.
+//   warps 4-7    epilogue (TMEM lane quarter warp & 3), the same fused dequant / SiLU / requantise / residual as the
+//                gather kernel.
+// Every wait is bounded; on expiry the CTA records PMG_ERR_TIMEOUT, lets issued MMAs retire, frees TMEM, returns.
+// No TMA multicast: every copy lands in this CTA's own shared memory.
+#include <algorithm>
+
+#include "tc_common.cuh"
+
+namespace pmg {
+namespace tcg {
+
+using namespace tc;
+
+constexpr int kThreads = 256;
+constexpr int kNR = 8;                  // mask records in flight
+constexpr int kRec = 27 * 4 * 4;        // one record: enable words [27 taps][4 row groups]
+constexpr int kBudget = 200 * 1024;    // resident weights + slab ring
+
+template <int NT, int W>
+struct GCfg {
+    static constexpr int kRes = 27 * NT * W;
+    static constexpr int kSlab = kM * W;
+    static constexpr int kStagesRaw = (kBudget - kRes) / kSlab;
+    static constexpr int kStages = kStagesRaw > 36 ? 36 : kStagesRaw;   // up to 4 tiles of 9 slabs in flight
+    static_assert(kStagesRaw >= 9, "shared memory budget");
+    static constexpr int kSmem = kRes + kStages * kSlab + kNR * kRec + 1024 + 1024;
+};
+
+__device__ __forceinline__ void mma_i8_lanes(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t acc, const uint4& off) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(off.x), "r"(off.y), "r"(off.z), "r"(off.w)
+        : "memory");
+}
+
+// Slab order: the centre offset (di, dj) = (0, 0) first, so its dz = 0 tap can initialise the accumulator.
+__device__ __forceinline__ int slab_of(int k) { return k == 0 ? 4 : (k <= 4 ? k - 1 : k); }
+
+template <int NT, int W>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_conv_grid0(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const int32_t* __restrict__ zq, int B, int H, int Wd, Epi e) {
+    using C = GCfg<NT, W>;
+    constexpr int NS = C::kStages;
+    constexpr int NCOLS = tmem_cols<NT>();
+    constexpr uint32_t IDESC = instr_desc(kM, NT);
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* res = smem;                                   // [27][NT][W] weights (swizzled)
+    uint8_t* ring = res + C::kRes;                         // [NS][128][W] slabs (swizzled)
+    uint32_t* recs = reinterpret_cast<uint32_t*>(ring + NS * C::kSlab);   // [NR][27][4]
+    uint64_t* full = reinterpret_cast<uint64_t*>(recs + kNR * 27 * 4);
+    uint64_t* empty = full + NS;
+    uint64_t* rec_full = empty + NS;        // [NR]
+    uint64_t* rec_empty = rec_full + kNR;   // [NR]
+    uint64_t* acc_full = rec_empty + kNR;   // [2]
+    uint64_t* acc_empty = acc_full + 2;     // [2]
+    uint64_t* wres = acc_empty + 2;
+    uint64_t* drain = wres + 1;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    __shared__ volatile int s_abort;
+    __shared__ float s_ws[256], s_bias[256];
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int r = 0; r < kNR; ++r) {
+            mbar_init(&rec_full[r], 2);
+            mbar_init(&rec_empty[r], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);
+        }
+        mbar_init(wres, 1);
+        mbar_init(drain, 1);
+        s_abort = 0;
+        fence_mbar_init();
+    }
+    if (e.ws && e.bias)
+        for (int n = threadIdx.x; n < NT; n += blockDim.x) {
+            s_ws[n] = e.ws[n];
+            s_bias[n] = e.bias[n];
+        }
+    if (warp == 1) tmem_alloc(tmem_slot, 2 * NCOLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    const int64_t HW = (int64_t)H * Wd;
+    const int64_t N = (int64_t)B * HW;
+    const int64_t ntile = (N + kM - 1) / kM;
+    const uint32_t ring_base = smem_u32(ring), res_base = smem_u32(res);
+
+    if (warp == 0) {
+        // ============================================ TMA loads ============================================ //
+        if (lane == 0) {
+            bool ok = true;
+            if (ntile > (int64_t)blockIdx.x) {
+                mbar_arrive_expect_tx(wres, (uint32_t)C::kRes);
+                for (int v = 0; v < 27; ++v) tma_tile2d(res_base + v * NT * W, &tmB, 0, v * NT, wres);
+            }
+            uint32_t it = 0;
+            for (int64_t t = blockIdx.x; t < ntile && ok; t += gridDim.x) {
+                const int64_t m0 = t * kM;
+                for (int k = 0; k < 9; ++k) {
+                    const int s9 = slab_of(k);
+                    const int di = s9 / 3 - 1, dj = s9 % 3 - 1;
+                    const uint32_t st = it % NS, ph = (it / NS) & 1u;
+                    if (!mbar_wait(&empty[st], ph ^ 1u, &s_abort)) { ok = false; break; }
+                    mbar_arrive_expect_tx(&full[st], (uint32_t)C::kSlab);
+                    // the row coordinate may be negative or past the end: TMA zero-fills those rows
+                    tma_tile2d(ring_base + st * C::kSlab, &tmA, 0, (int)(m0 + (int64_t)di * Wd + dj), &full[st]);
+                    ++it;
+                }
+            }
+            if (!ok) {
+                s_abort = 1;
+                flag(e.status, PMG_ERR_TIMEOUT);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ============================================ MMA issuer ============================================ //
+        if (lane == 0) {
+            bool ok = true, issued = false;
+            if (ntile > (int64_t)blockIdx.x) ok = mbar_wait(wres, 0, &s_abort);
+            uint32_t it = 0, k = 0;
+            for (int64_t t = blockIdx.x; t < ntile && ok; t += gridDim.x, ++k) {
+                const uint32_t b = k & 1u, rs = k % kNR;
+                if (!mbar_wait(&acc_empty[b], ((k >> 1) & 1u) ^ 1u, &s_abort)) { ok = false; break; }
+                if (!mbar_wait(&rec_full[rs], (k / kNR) & 1u, &s_abort)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d = tmem + b * NCOLS;
+                const uint4* rec = reinterpret_cast<const uint4*>(recs + rs * 27 * 4);
+                for (int kk9 = 0; kk9 < 9 && ok; ++kk9) {
+                    const int s9 = slab_of(kk9);
+                    const uint32_t st = it % NS, ph = (it / NS) & 1u;
+                    if (!mbar_wait(&full[st], ph, &s_abort)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t sa = ring_base + st * C::kSlab;
+#pragma unroll
+                    for (int g = 0; g < 3; ++g) {
+                        // centre slab: dz = 0 (tap 13) first, unmasked, starting the accumulation
+                        const int dzi = kk9 == 0 ? (g == 0 ? 1 : (g == 1 ? 0 : 2)) : g;
+                        const int v = s9 * 3 + dzi;
+                        const bool first = kk9 == 0 && g == 0;
+                        uint4 en = rec[v];
+                        if (!first && (en.x | en.y | en.z | en.w) == 0u) continue;
+                        const uint4 off = first ? make_uint4(0u, 0u, 0u, 0u)
+                                                : make_uint4(~en.x, ~en.y, ~en.z, ~en.w);
+#pragma unroll
+                        for (int kq = 0; kq < W / 32; ++kq) {
+                            mma_i8_lanes(d, desc_sw<W>(sa + 32 * kq), desc_sw<W>(res_base + v * NT * W + 32 * kq),
+                                         IDESC, (first && kq == 0) ? 0u : 1u, off);
+                        }
+                        issued = true;
+                    }
+                    mma_commit(&empty[st]);
+                    ++it;
+                }
+                if (!ok) break;
+                mbar_arrive(&rec_empty[rs]);     // the masks were read into registers at issue
+                mma_commit(&acc_full[b]);
+            }
+            if (!ok) {
+                s_abort = 1;
+                flag(e.status, PMG_ERR_TIMEOUT);
+                if (issued) {
+                    mma_commit(drain);
+                    const uint64_t t0 = global_ns();
+                    while (!mbar_try_wait_sleep(drain, 0, 4000) && global_ns() - t0 < kWaitNs) {
+                    }
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp < 4) {
+        // ============================================ row masks ============================================ //
+        const int mw = warp - 2;                 // row groups 2*mw, 2*mw + 1
+        bool ok = true;
+        uint32_t k = 0;
+        for (int64_t t = blockIdx.x; t < ntile && ok; t += gridDim.x, ++k) {
+            const uint32_t rs = k % kNR;
+            ok = __all_sync(0xffffffffu, mbar_wait(&rec_empty[rs], ((k / kNR) & 1u) ^ 1u, &s_abort));
+            if (!ok) break;
+            uint32_t* rec = recs + rs * 27 * 4;
+#pragma unroll
+            for (int gg = 0; gg < 2; ++gg) {
+                const int g = 2 * mw + gg;
+                const int64_t o = t * kM + 32 * g + lane;
+                const bool valid = o < N;
+                int i = 0, j = 0, z0 = 0;
+                if (valid) {
+                    const int64_t rem = o % HW;
+                    i = (int)(rem / Wd);
+                    j = (int)(rem - (int64_t)i * Wd);
+                    z0 = zq[o];
+                }
+                int zn[9];
+#pragma unroll
+                for (int s9 = 0; s9 < 9; ++s9) {
+                    const int di = s9 / 3 - 1, dj = s9 % 3 - 1;
+                    const bool in = valid && i + di >= 0 && i + di < H && j + dj >= 0 && j + dj < Wd;
+                    zn[s9] = in ? zq[o + (int64_t)di * Wd + dj] : INT32_MIN;
+                }
+                uint32_t mine = 0;
+#pragma unroll
+                for (int s9 = 0; s9 < 9; ++s9) {
+                    // INT32_MIN marks "outside the frame": its difference never lands in [-1, 1]
+                    const int dz = zn[s9] == INT32_MIN ? 2 : zn[s9] - z0;
+#pragma unroll
+                    for (int dzi = 0; dzi < 3; ++dzi) {
+                        const uint32_t bal = __ballot_sync(0xffffffffu, dz == dzi - 1);
+                        if (lane == s9 * 3 + dzi) mine = bal;
+                    }
+                }
+                if (lane < 27) rec[lane * 4 + g] = mine;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&rec_full[rs]);
+        }
+        if (!ok) {
+            s_abort = 1;
+            flag(e.status, PMG_ERR_TIMEOUT);
+        }
+    } else {
+        // ============================================ epilogue ============================================ //
+        const int q = warp & 3;
+        uint32_t k = 0;
+        bool ok = true;
+        for (int64_t t = blockIdx.x; t < ntile && ok; t += gridDim.x, ++k) {
+            const int64_t m0 = t * kM;
+            const uint32_t b = k & 1u;
+            if (!mbar_wait(&acc_full[b], (k >> 1) & 1u, &s_abort)) { ok = false; break; }
+            tc_fence_after();
+            const int rr = 32 * q + lane;
+            const bool live = m0 + rr < N;
+            const float* rrow = (e.mode == PMG_EPI_F32_RESID && live) ? e.resid + (m0 + rr) * NT : nullptr;
+            float4 rcur[4], rnext[4];
+            if (rrow) load_resid16(rrow, rcur);
+#pragma unroll 1
+            for (int j = 0; j < NT / 16; ++j) {
+                if (rrow && j + 1 < NT / 16) load_resid16(rrow + (j + 1) * 16, rnext);
+                uint32_t acc[16];
+                tmem_ld16(tmem + b * NCOLS + ((uint32_t)(32 * q) << 16) + (uint32_t)(j * 16), acc);
+                if (live) epi_store16(e, s_ws, s_bias, m0 + rr, j * 16, NT, acc, rcur);
+#pragma unroll
+                for (int t4 = 0; t4 < 4; ++t4) rcur[t4] = rnext[t4];
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[b]);
+        }
+        if (!ok) {
+            s_abort = 1;
+            flag(e.status, PMG_ERR_TIMEOUT);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 2 * NCOLS);
+    }
+}
+
+}  // namespace tcg
+
+namespace {
+
+template <int NT, int W>
+int launch_grid0(const int8_t* in, const int32_t* zq, int B, int H, int Wd, const int8_t* w, const Epi& e,
+                 cudaStream_t s) {
+    using C = tcg::GCfg<NT, W>;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    PMG_CUDA_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return PMG_ERR_UNSUPPORTED;
+    if (!attr_set[dev]) {
+        PMG_CUDA_TRY(cudaFuncSetAttribute(tcg::k_conv_grid0<NT, W>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          C::kSmem));
+        attr_set[dev] = true;
+    }
+    const int64_t N = (int64_t)B * H * Wd;
+    const int64_t tiles = (N + tc::kM - 1) / tc::kM;
+    const int grid = (int)std::min<int64_t>(tiles, (int64_t)kNumSMs);
+    if (grid <= 0) return PMG_OK;
+    CUtensorMap ma, mb;
+    int rc = make_tensor_map(&ma, in, (uint64_t)N, (uint64_t)W, W, tc::kM);
+    if (rc != PMG_OK) return rc;
+    rc = make_tensor_map(&mb, w, (uint64_t)27 * NT, (uint64_t)W, W, NT);
+    if (rc != PMG_OK) return rc;
+    tcg::k_conv_grid0<NT, W><<<grid, tcg::kThreads, C::kSmem, s>>>(ma, mb, zq, B, H, Wd, e);
+    PMG_LAUNCH_CHECK();
+    return PMG_OK;
+}
+
+}  // namespace
+
+bool grid0_supported(int Ci, int Co) { return Ci == Co && (Ci == 32 || Ci == 64); }
+
+int conv_grid0_tc(const int8_t* in, const int32_t* zq, int B, int H, int W, int Ci, int Co, const int8_t* w,
+                  const Epi& e, cudaStream_t s) {
+    if (!grid0_supported(Ci, Co)) return PMG_ERR_UNSUPPORTED;
+    if (B <= 0 || H <= 0 || W <= 0) return PMG_ERR_BAD_ARG;
+    const int64_t N = (int64_t)B * H * W;
+    if (N >= INT32_MAX - 2 * (int64_t)W - 256) return PMG_ERR_UNSUPPORTED;   // TMA row coordinates are int32
+    if (Ci == 32) return launch_grid0<32, 32>(in, zq, B, H, W, w, e, s);
+    return launch_grid0<64, 64>(in, zq, B, H, W, w, e, s);
+}
+
+}  // namespace pmg
+
+using namespace pmg;
+
+extern "C" int pmg_spconv_i8_grid0(const int8_t* in_q8, const int32_t* zq, int32_t B, int32_t H, int32_t W,
+                                   int32_t Ci, int32_t Co, const int8_t* weight, const float* w_scale,
+                                   const float* bias, float act_scale, int32_t epilogue, float out_scale,
+                                   const float* resid, void* out, int32_t* status, void* stream) {
+    if (!in_q8 || !zq || !weight || !out) return PMG_ERR_BAD_ARG;
+    if (epilogue < PMG_EPI_ACC32 || epilogue > PMG_EPI_SILU_Q8) return PMG_ERR_BAD_ARG;
+    if (epilogue != PMG_EPI_ACC32 && (!w_scale || !bias)) return PMG_ERR_BAD_ARG;
+    if (epilogue == PMG_EPI_F32_RESID && !resid) return PMG_ERR_BAD_ARG;
+    if (!grid0_supported(Ci, Co)) return PMG_ERR_UNSUPPORTED;
+    Epi e{epilogue, act_scale, out_scale, w_scale, bias, resid, out, status};
+    return conv_grid0_tc(in_q8, zq, B, H, W, Ci, Co, weight, e, as_stream(stream));
+}

@@ -126,6 +126,11 @@ def tc_supported(Ci: int, Co: int) -> bool:
     return Co in (32, 64, 128, 256) and (Ci in (32, 64) or (Ci >= 128 and Ci % 128 == 0))
 
 
+def grid0_supported(Ci: int, Co: int) -> bool:
+    """Widths the level-0 frame-grid tensor-core conv covers."""
+    return Ci == Co and Ci in (32, 64)
+
+
 def spconv_i8(q_in, nmap, tile_mask, weight_tap_major, w_scale=None, bias=None, act_scale=1.0, mode=EPI_ACC32,
               out_scale=1.0, resid=None, count=None, rows=None, tensor_cores=True, status=None):
     """Submanifold conv: q_in [M_in, Ci] int8, nmap [27, ld] int32, weight [27, Co, Ci] int8.  The tcgen05 kernel
@@ -139,6 +144,21 @@ def spconv_i8(q_in, nmap, tile_mask, weight_tap_major, w_scale=None, bias=None, 
     call("pmg_spconv_i8", _p(q_in), q_in.shape[0], _p(nmap), ld, _p(tile_mask), _p(count), rows, Ci, Co,
          _p(weight_tap_major), _p(w_scale), _p(bias), float(act_scale), mode, float(out_scale), _p(resid), _p(out),
          0 if tensor_cores else FLAG_SIMT, _p(status), _stream())
+    return out
+
+
+def spconv_i8_grid0(q_in, zq, B, H, W, weight_tap_major, w_scale=None, bias=None, act_scale=1.0, mode=EPI_ACC32,
+                    out_scale=1.0, resid=None, status=None):
+    """Level-0 submanifold conv of a B x H x W frame grid (one voxel per pixel, z = zq) without a neighbour map:
+    q_in [B*H*W, C] int8, zq [B*H*W] int32, weight [27, C, C] int8, C in {32, 64}."""
+    _dev(q_in, torch.int8, "q_in")
+    _dev(zq, torch.int32, "zq")
+    _dev(weight_tap_major, torch.int8, "weight")
+    rows = B * H * W
+    Co, Ci = weight_tap_major.shape[1], weight_tap_major.shape[2]
+    out = _epi_out(mode, rows, Co, q_in.device)
+    call("pmg_spconv_i8_grid0", _p(q_in), _p(zq), B, H, W, Ci, Co, _p(weight_tap_major), _p(w_scale), _p(bias),
+         float(act_scale), mode, float(out_scale), _p(resid), _p(out), _p(status), _stream())
     return out
 
 
