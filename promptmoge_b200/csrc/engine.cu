@@ -117,6 +117,10 @@ struct pmg_refiner {
     const float* conf = nullptr;
     // graph
     cudaStream_t cap_stream = nullptr;
+    // The voxel structure of a step (voxelise, pools, neighbour maps) depends only on the point map, not on the
+    // LiDAR fit: it runs on `side`, forked from the step's stream and joined before the U-Net needs it.
+    cudaStream_t side = nullptr;
+    cudaEvent_t ev_fork = nullptr, ev_vox = nullptr, ev_struct = nullptr;
     cudaGraphExec_t exec = nullptr;
     std::vector<void*> allocs;
     int launches = 0;
@@ -329,6 +333,8 @@ int enqueue_step(pmg_refiner* r, cudaStream_t s) {
     const auto& c = r->cfg;
     const int B = c.batch, H = c.height, W = c.width, L = r->L;
     int nl = 0;
+    PMG_CUDA_TRY(cudaEventRecord(r->ev_fork, s));
+    PMG_CUDA_TRY(cudaStreamWaitEvent(r->side, r->ev_fork, 0));
     // --- per-step LiDAR fit + prompt features (v3.py:552-555) --------------------------------------------------- //
     if (c.use_prompt) {
         LAUNCH(fit_prep_prompt(r->pc + 2, 3, r->lidar, r->conf, B, H, W, c.lidar_h, c.lidar_w, r->fz, r->fy,
@@ -342,31 +348,36 @@ int enqueue_step(pmg_refiner* r, cudaStream_t s) {
         LAUNCH(prompt_feats(r->pc + 2, 3, r->lidar, r->conf, r->fst, B, H, W, c.lidar_h, c.lidar_w, c.soft_gate,
                             r->prompt, s));
     }
-    // --- structure ------------------------------------------------------------------------------------------------ //
-    PMG_CUDA_TRY(cudaMemsetAsync(r->zext, 0x7f, B * sizeof(int32_t), s));
-    PMG_CUDA_TRY(cudaMemsetAsync(r->zext + B, 0x80, B * sizeof(int32_t), s));
+    // --- structure (side stream) ----------------------------------------------------------------------------------- //
+    cudaStream_t ss = r->side;
+    PMG_CUDA_TRY(cudaMemsetAsync(r->zext, 0x7f, B * sizeof(int32_t), ss));
+    PMG_CUDA_TRY(cudaMemsetAsync(r->zext + B, 0x80, B * sizeof(int32_t), ss));
     LevelBuf& l0 = r->lv[0];
     LAUNCH(pmg_voxelize_l0(r->pc, B, H, W, c.depth_resolution, r->zq, r->zext, r->zext + B, l0.nmap, l0.cap, l0.mask,
-                           s));
+                           ss));
+    PMG_CUDA_TRY(cudaEventRecord(r->ev_vox, ss));
     for (int k = 0; k + 1 < L; ++k) {
         LevelBuf& f = r->lv[k];
         LevelBuf& n = r->lv[k + 1];
         PMG_TRY(pmg_pool_frames(B, f.H, f.W, r->counts + 2 * k, k == 0 ? nullptr : f.col_start, k == 0 ? r->zq : f.z,
                                 k == 0 ? r->zext : nullptr, r->counts + 2 * (k + 1), n.z, n.col, n.col_start, nullptr,
-                                n.cap, f.parent, f.seg_idx, f.seg_off, f.pool_ws, f.pool_ws_bytes, r->status, s));
+                                n.cap, f.parent, f.seg_idx, f.seg_off, f.pool_ws, f.pool_ws_bytes, r->status, ss));
         nl += 3;
         LAUNCH(pmg_nmap_frames(B, n.H, n.W, r->counts + 2 * (k + 1), n.z, n.col, n.col_start, n.nmap, n.cap, n.mask,
-                               s));
+                               ss));
     }
+    PMG_CUDA_TRY(cudaEventRecord(r->ev_struct, ss));
     // --- U-Net ---------------------------------------------------------------------------------------------------- //
     LAUNCH(input_proj(r->pc, c.use_prompt ? r->prompt : nullptr, r->N, l0.C, r->in_proj.w, r->in_proj.b,
                       r->pr_proj.w, r->pr_proj.b, l0.X, s));
+    PMG_CUDA_TRY(cudaStreamWaitEvent(s, r->ev_vox, 0));      // level 0: zq / neighbour map
     for (int k = 0; k < L; ++k) {
         PMG_TRY(resblock(r, k, r->down[k], nullptr, nullptr, s, nl));
         if (k + 1 < L) {
             LevelBuf& f = r->lv[k];
             LevelBuf& n = r->lv[k + 1];
             const int32_t* ncnt = r->counts + 2 * (k + 1);
+            if (k == 0) PMG_CUDA_TRY(cudaStreamWaitEvent(s, r->ev_struct, 0));   // pools and coarser levels
             LAUNCH(pool_mean(f.S, f.seg_idx, f.seg_off, ncnt, n.cap, f.C, r->pool[k].sa, f.pq, nullptr, s));
             LAUNCH(dense(r, f.pq, ncnt, n.cap, f.C, n.C, r->pool[k], PMG_EPI_F32, 0.f, nullptr, n.X, s));
         }
@@ -408,6 +419,23 @@ int enqueue_run(pmg_refiner* r, int K, float* pc_out, pmg_fit_state* fit_out, cu
 
 }  // namespace
 
+namespace {
+void destroy_streams(pmg_refiner* r) {
+    if (r->exec) cudaGraphExecDestroy(r->exec);
+    r->exec = nullptr;
+    for (cudaEvent_t* e : {&r->ev_fork, &r->ev_vox, &r->ev_struct})
+        if (*e) {
+            cudaEventDestroy(*e);
+            *e = nullptr;
+        }
+    for (cudaStream_t* st : {&r->cap_stream, &r->side})
+        if (*st) {
+            cudaStreamDestroy(*st);
+            *st = nullptr;
+        }
+}
+}  // namespace
+
 extern "C" int pmg_refiner_create(const pmg_refiner_config* cfg, pmg_refiner** out) {
     if (!cfg || !out) return PMG_ERR_BAD_ARG;
     const int L = cfg->levels;
@@ -421,6 +449,10 @@ extern "C" int pmg_refiner_create(const pmg_refiner_config* cfg, pmg_refiner** o
     int rc = allocate(r);
     if (rc == PMG_OK) {
         cudaError_t e = cudaStreamCreateWithFlags(&r->cap_stream, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&r->side, cudaStreamNonBlocking);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&r->ev_fork, cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&r->ev_vox, cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&r->ev_struct, cudaEventDisableTiming);
         if (e != cudaSuccess) {
             set_cuda_error(e);
             rc = PMG_ERR_CUDA;
@@ -428,6 +460,7 @@ extern "C" int pmg_refiner_create(const pmg_refiner_config* cfg, pmg_refiner** o
     }
     if (rc != PMG_OK) {
         free_all(r);
+        destroy_streams(r);
         delete r;
         return rc;
     }
@@ -439,7 +472,7 @@ extern "C" void pmg_refiner_destroy(pmg_refiner* r) {
     if (!r) return;
     cudaDeviceSynchronize();
     free_all(r);
-    if (r->cap_stream) cudaStreamDestroy(r->cap_stream);
+    destroy_streams(r);
     delete r;
 }
 

@@ -36,14 +36,18 @@ constexpr int kNR = 8;                  // mask records in flight
 constexpr int kRec = 27 * 4 * 4;        // one record: enable words [27 taps][4 row groups]
 constexpr int kBudget = 200 * 1024;    // resident weights + slab ring
 
+// A ring stage holds SPS consecutive slabs of a tile (all 9 when they fit), so the issuing threads wait and commit
+// once per stage rather than once per slab.
 template <int NT, int W>
 struct GCfg {
     static constexpr int kRes = 27 * NT * W;
     static constexpr int kSlab = kM * W;
-    static constexpr int kStagesRaw = (kBudget - kRes) / kSlab;
-    static constexpr int kStages = kStagesRaw > 36 ? 36 : kStagesRaw;   // up to 4 tiles of 9 slabs in flight
-    static_assert(kStagesRaw >= 9, "shared memory budget");
-    static constexpr int kSmem = kRes + kStages * kSlab + kNR * kRec + 1024 + 1024;
+    static constexpr int SPS = (kBudget - kRes) / (9 * kSlab) >= 3 ? 9 : ((kBudget - kRes) / (3 * kSlab) >= 3 ? 3 : 1);
+    static constexpr int kStage = SPS * kSlab;
+    static constexpr int kStagesRaw = (kBudget - kRes) / kStage;
+    static constexpr int kStages = kStagesRaw > 6 * (9 / SPS) ? 6 * (9 / SPS) : kStagesRaw;
+    static_assert(kStagesRaw >= 2, "shared memory budget");
+    static constexpr int kSmem = kRes + kStages * kStage + kNR * kRec + 1024 + 1024;
 };
 
 __device__ __forceinline__ void mma_i8_lanes(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -69,8 +73,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* res = smem;                                   // [27][NT][W] weights (swizzled)
-    uint8_t* ring = res + C::kRes;                         // [NS][128][W] slabs (swizzled)
-    uint32_t* recs = reinterpret_cast<uint32_t*>(ring + NS * C::kSlab);   // [NR][27][4]
+    uint8_t* ring = res + C::kRes;                         // [NS][SPS][128][W] slabs (swizzled)
+    uint32_t* recs = reinterpret_cast<uint32_t*>(ring + NS * C::kStage);  // [NR][27][4]
     uint64_t* full = reinterpret_cast<uint64_t*>(recs + kNR * 27 * 4);
     uint64_t* empty = full + NS;
     uint64_t* rec_full = empty + NS;        // [NR]
@@ -120,24 +124,30 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == 0) {
         // ============================================ TMA loads ============================================ //
+        // The issuing threads keep their loops lean: every instruction of a single-thread loop costs its full
+        // latency, so offsets, descriptors and ring positions are precomputed or advanced incrementally.
         if (lane == 0) {
             bool ok = true;
+            int yoff[9];
+#pragma unroll
+            for (int k = 0; k < 9; ++k) yoff[k] = (slab_of(k) / 3 - 1) * Wd + (slab_of(k) % 3 - 1);
             if (ntile > (int64_t)blockIdx.x) {
                 mbar_arrive_expect_tx(wres, (uint32_t)C::kRes);
                 for (int v = 0; v < 27; ++v) tma_tile2d(res_base + v * NT * W, &tmB, 0, v * NT, wres);
             }
-            uint32_t it = 0;
+            uint32_t st = 0, ph = 0;
             for (int64_t t = blockIdx.x; t < ntile && ok; t += gridDim.x) {
-                const int64_t m0 = t * kM;
+                const int m0 = (int)(t * kM);
+#pragma unroll
                 for (int k = 0; k < 9; ++k) {
-                    const int s9 = slab_of(k);
-                    const int di = s9 / 3 - 1, dj = s9 % 3 - 1;
-                    const uint32_t st = it % NS, ph = (it / NS) & 1u;
-                    if (!mbar_wait(&empty[st], ph ^ 1u, &s_abort)) { ok = false; break; }
-                    mbar_arrive_expect_tx(&full[st], (uint32_t)C::kSlab);
+                    constexpr int SPS = C::SPS;
+                    if (k % SPS == 0) {
+                        if (!mbar_wait(&empty[st], ph ^ 1u, &s_abort)) { ok = false; break; }
+                        mbar_arrive_expect_tx(&full[st], (uint32_t)C::kStage);
+                    }
                     // the row coordinate may be negative or past the end: TMA zero-fills those rows
-                    tma_tile2d(ring_base + st * C::kSlab, &tmA, 0, (int)(m0 + (int64_t)di * Wd + dj), &full[st]);
-                    ++it;
+                    tma_tile2d(ring_base + st * C::kStage + (k % SPS) * C::kSlab, &tmA, 0, m0 + yoff[k], &full[st]);
+                    if (k % SPS == SPS - 1 && ++st == (uint32_t)NS) { st = 0; ph ^= 1u; }
                 }
             }
             if (!ok) {
@@ -151,39 +161,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             bool ok = true, issued = false;
             if (ntile > (int64_t)blockIdx.x) ok = mbar_wait(wres, 0, &s_abort);
-            uint32_t it = 0, k = 0;
+            const uint64_t a_base = desc_sw<W>(ring_base), b_base = desc_sw<W>(res_base);
+            constexpr uint64_t A_STEP = C::kStage >> 4, A_SLAB = C::kSlab >> 4;  // descriptor address units
+            constexpr uint64_t B_STEP = (NT * W) >> 4;
+            const uint4 none = make_uint4(0u, 0u, 0u, 0u);
+            uint32_t st = 0, ph = 0, k = 0;
             for (int64_t t = blockIdx.x; t < ntile && ok; t += gridDim.x, ++k) {
-                const uint32_t b = k & 1u, rs = k % kNR;
+                const uint32_t b = k & 1u, rs = k & (kNR - 1);
                 if (!mbar_wait(&acc_empty[b], ((k >> 1) & 1u) ^ 1u, &s_abort)) { ok = false; break; }
                 if (!mbar_wait(&rec_full[rs], (k / kNR) & 1u, &s_abort)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t d = tmem + b * NCOLS;
                 const uint4* rec = reinterpret_cast<const uint4*>(recs + rs * 27 * 4);
-                for (int kk9 = 0; kk9 < 9 && ok; ++kk9) {
+#pragma unroll
+                for (int kk9 = 0; kk9 < 9; ++kk9) {
                     const int s9 = slab_of(kk9);
-                    const uint32_t st = it % NS, ph = (it / NS) & 1u;
-                    if (!mbar_wait(&full[st], ph, &s_abort)) { ok = false; break; }
-                    tc_fence_after();
-                    const uint32_t sa = ring_base + st * C::kSlab;
+                    constexpr int SPS = C::SPS;
+                    const uint4 e0 = rec[s9 * 3], e1 = rec[s9 * 3 + 1], e2 = rec[s9 * 3 + 2];
+                    if (kk9 % SPS == 0) {
+                        if (!mbar_wait(&full[st], ph, &s_abort)) { ok = false; break; }
+                        tc_fence_after();
+                    }
+                    const uint64_t ad = a_base + st * A_STEP + (kk9 % SPS) * A_SLAB;
 #pragma unroll
                     for (int g = 0; g < 3; ++g) {
                         // centre slab: dz = 0 (tap 13) first, unmasked, starting the accumulation
                         const int dzi = kk9 == 0 ? (g == 0 ? 1 : (g == 1 ? 0 : 2)) : g;
-                        const int v = s9 * 3 + dzi;
                         const bool first = kk9 == 0 && g == 0;
-                        uint4 en = rec[v];
+                        const uint4 en = dzi == 0 ? e0 : (dzi == 1 ? e1 : e2);
                         if (!first && (en.x | en.y | en.z | en.w) == 0u) continue;
-                        const uint4 off = first ? make_uint4(0u, 0u, 0u, 0u)
-                                                : make_uint4(~en.x, ~en.y, ~en.z, ~en.w);
+                        const uint4 off = first ? none : make_uint4(~en.x, ~en.y, ~en.z, ~en.w);
+                        const uint64_t bd = b_base + (uint64_t)(s9 * 3 + dzi) * B_STEP;
 #pragma unroll
-                        for (int kq = 0; kq < W / 32; ++kq) {
-                            mma_i8_lanes(d, desc_sw<W>(sa + 32 * kq), desc_sw<W>(res_base + v * NT * W + 32 * kq),
-                                         IDESC, (first && kq == 0) ? 0u : 1u, off);
-                        }
-                        issued = true;
+                        for (int kq = 0; kq < W / 32; ++kq)
+                            mma_i8_lanes(d, ad + 2 * kq, bd + 2 * kq, IDESC, (first && kq == 0) ? 0u : 1u, off);
                     }
-                    mma_commit(&empty[st]);
-                    ++it;
+                    issued = true;
+                    if (kk9 % SPS == SPS - 1) {
+                        mma_commit(&empty[st]);
+                        if (++st == (uint32_t)NS) { st = 0; ph ^= 1u; }
+                    }
                 }
                 if (!ok) break;
                 mbar_arrive(&rec_empty[rs]);     // the masks were read into registers at issue
@@ -203,45 +220,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
     } else if (warp < 4) {
         // ============================================ row masks ============================================ //
-        const int mw = warp - 2;                 // row groups 2*mw, 2*mw + 1
+        // Warp 2 + mw builds row groups 2 mw and 2 mw + 1 of each tile: bit `lane` of word [tap][group] is set when
+        // row 32 group + lane has that neighbour.  All 20 z loads of both groups are issued before the ballots.
+        const int mw = warp - 2;
+        const uint32_t n32 = (uint32_t)N, hw32 = (uint32_t)HW, w32 = (uint32_t)Wd;
         bool ok = true;
         uint32_t k = 0;
         for (int64_t t = blockIdx.x; t < ntile && ok; t += gridDim.x, ++k) {
-            const uint32_t rs = k % kNR;
+            const uint32_t rs = k & (kNR - 1);
             ok = __all_sync(0xffffffffu, mbar_wait(&rec_empty[rs], ((k / kNR) & 1u) ^ 1u, &s_abort));
             if (!ok) break;
             uint32_t* rec = recs + rs * 27 * 4;
+            int z0[2], zn[2][9];
 #pragma unroll
             for (int gg = 0; gg < 2; ++gg) {
-                const int g = 2 * mw + gg;
-                const int64_t o = t * kM + 32 * g + lane;
-                const bool valid = o < N;
-                int i = 0, j = 0, z0 = 0;
-                if (valid) {
-                    const int64_t rem = o % HW;
-                    i = (int)(rem / Wd);
-                    j = (int)(rem - (int64_t)i * Wd);
-                    z0 = zq[o];
-                }
-                int zn[9];
+                const uint32_t o = (uint32_t)t * kM + 32u * (2 * mw + gg) + lane;
+                const bool valid = o < n32;
+                const uint32_t rem = valid ? o % hw32 : 0u;
+                const int i = (int)(rem / w32), j = (int)(rem - (rem / w32) * w32);
+                z0[gg] = valid ? zq[o] : 0;
 #pragma unroll
                 for (int s9 = 0; s9 < 9; ++s9) {
                     const int di = s9 / 3 - 1, dj = s9 % 3 - 1;
                     const bool in = valid && i + di >= 0 && i + di < H && j + dj >= 0 && j + dj < Wd;
-                    zn[s9] = in ? zq[o + (int64_t)di * Wd + dj] : INT32_MIN;
+                    zn[gg][s9] = in ? zq[(int)o + di * Wd + dj] : INT32_MIN;
                 }
+            }
+#pragma unroll
+            for (int gg = 0; gg < 2; ++gg) {
                 uint32_t mine = 0;
 #pragma unroll
                 for (int s9 = 0; s9 < 9; ++s9) {
                     // INT32_MIN marks "outside the frame": its difference never lands in [-1, 1]
-                    const int dz = zn[s9] == INT32_MIN ? 2 : zn[s9] - z0;
+                    const int dz = zn[gg][s9] == INT32_MIN ? 2 : zn[gg][s9] - z0[gg];
 #pragma unroll
                     for (int dzi = 0; dzi < 3; ++dzi) {
                         const uint32_t bal = __ballot_sync(0xffffffffu, dz == dzi - 1);
                         if (lane == s9 * 3 + dzi) mine = bal;
                     }
                 }
-                if (lane < 27) rec[lane * 4 + g] = mine;
+                if (lane < 27) rec[lane * 4 + 2 * mw + gg] = mine;
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&rec_full[rs]);

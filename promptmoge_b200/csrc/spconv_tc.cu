@@ -339,9 +339,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 4) {
         // =========================================== MMA issuer =========================================== //
         if (lane == 0) {
-            uint32_t it = 0, t = 0;
+            // A lean loop: every instruction of this single thread costs its full latency, so descriptors are
+            // precomputed and advanced in descriptor address units (16 bytes), ring positions incrementally.
+            uint32_t t = 0, s = 0, ph = 0;
             bool ok = true, issued = false;
             if (RES && nunits > (int64_t)blockIdx.x) ok = mbar_wait(wres, 0, &s_abort);
+            const uint64_t a_desc0 = KIND == DENSE ? desc_sw<W>(ring_base) : desc_plain(ring_base, kLboA, kSboA);
+            const uint64_t b_desc0 = RES ? desc_sw<W>(res_base) : desc_sw<W>(ring_base + C::kA);
+            constexpr uint64_t STAGE = C::kStage >> 4;
+            constexpr uint64_t A_G = (CPR * kLboA) >> 4;                        // next tap of a gathered item
+            constexpr uint64_t A_KK = KIND == DENSE ? 2 : (2 * kLboA) >> 4;     // next 32 bytes of K
+            constexpr uint64_t B_G = (NT * W) >> 4;                              // next tap's weights
             int64_t xm0;
             int xmc;
             uint32_t xmk = 1;
@@ -358,29 +366,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                     int tv[TPI];
                     const int nt = take(mk, tv);
                     for (int kb = 0; kb < nkb; ++kb) {
-                        const uint32_t s = it % NST, ph = (it / NST) & 1u;
                         if (!mbar_wait(&full[s], ph, &s_abort)) { ok = false; break; }
                         tc_fence_after();
-                        const uint32_t sa = ring_base + s * C::kStage;
-                        const uint32_t sb = sa + C::kA;
+                        const uint64_t ad0 = a_desc0 + s * STAGE;
+                        const uint64_t bd0 = RES ? b_desc0 : b_desc0 + s * STAGE;
 #pragma unroll
                         for (int g = 0; g < TPI; ++g) {
                             if (g >= nt) break;
+                            const uint64_t bdg = RES ? bd0 + (uint64_t)tv[g] * B_G : bd0 + g * B_G;
 #pragma unroll
                             for (int kk = 0; kk < W / 32; ++kk) {
-                                const uint64_t ad = KIND == DENSE
-                                                        ? desc_sw<W>(sa + 32 * kk)
-                                                        : desc_plain(sa + (uint32_t)(g * CPR + 2 * kk) * kLboA, kLboA,
-                                                                     kSboA);
-                                const uint64_t bd = RES ? desc_sw<W>(res_base + tv[g] * NT * W + 32 * kk)
-                                                        : desc_sw<W>(sb + g * NT * W + 32 * kk);
-                                mma_i8(d, ad, bd, IDESC, accumulate);
+                                mma_i8(d, ad0 + g * A_G + kk * A_KK, bdg + 2 * kk, IDESC, accumulate);
                                 accumulate = 1;
-                                issued = true;
                             }
                         }
+                        issued = true;
                         mma_commit(&empty[s]);
-                        ++it;
+                        if (++s == (uint32_t)NST) { s = 0; ph ^= 1u; }
                     }
                 }
                 if (!ok) break;
