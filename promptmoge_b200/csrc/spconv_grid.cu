@@ -18,8 +18,9 @@
 //   warp 1       lane 0 issues the MMAs into one of two TMEM accumulators and commits stages / accumulators.
 //   warps 2-3    build each tile's 27 x 128-bit masks from zq (bounds of the frame + the z difference), one ballot
 //                per (tap, 32-row group), into a ring of NR mask records.
-//   warps 4-7    epilogue (TMEM lane quarter warp & 3), the same fused dequant / SiLU / requantise / residual as the
-//                gather kernel.
+//   warps 4-11   epilogue: two warps per TMEM lane quarter (warp & 3), each on half of the output channels, the same
+//                fused dequant / SiLU / requantise / residual as the gather kernel (the SiLU + requantise arithmetic
+//                is issue-bound, so two warps per SM sub-partition hide each other's latency).
 // Every wait is bounded; on expiry the CTA records PMG_ERR_TIMEOUT, lets issued MMAs retire, frees TMEM, returns.
 // No TMA multicast: every copy lands in this CTA's own shared memory.
 #include <algorithm>
@@ -31,7 +32,8 @@ namespace tcg {
 
 using namespace tc;
 
-constexpr int kThreads = 256;
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 32 * (4 + kEpiWarps);
 constexpr int kNR = 8;                  // mask records in flight
 constexpr int kRec = 27 * 4 * 4;        // one record: enable words [27 taps][4 row groups]
 constexpr int kBudget = 200 * 1024;    // resident weights + slab ring
@@ -99,7 +101,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], 4);
+            mbar_init(&acc_empty[b], kEpiWarps);
         }
         mbar_init(wres, 1);
         mbar_init(drain, 1);
@@ -271,6 +273,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // ============================================ epilogue ============================================ //
         const int q = warp & 3;
+        constexpr int CH = NT / 32;                   // 16-column chunks per epilogue warp
+        const int j0 = ((warp - 4) >> 2) * CH;
         uint32_t k = 0;
         bool ok = true;
         for (int64_t t = blockIdx.x; t < ntile && ok; t += gridDim.x, ++k) {
@@ -280,12 +284,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int rr = 32 * q + lane;
             const bool live = m0 + rr < N;
-            const float* rrow = (e.mode == PMG_EPI_F32_RESID && live) ? e.resid + (m0 + rr) * NT : nullptr;
+            const float* rrow = (e.mode == PMG_EPI_F32_RESID && live) ? e.resid + (m0 + rr) * NT + j0 * 16 : nullptr;
             float4 rcur[4], rnext[4];
             if (rrow) load_resid16(rrow, rcur);
 #pragma unroll 1
-            for (int j = 0; j < NT / 16; ++j) {
-                if (rrow && j + 1 < NT / 16) load_resid16(rrow + (j + 1) * 16, rnext);
+            for (int jj = 0; jj < CH; ++jj) {
+                const int j = j0 + jj;
+                if (rrow && jj + 1 < CH) load_resid16(rrow + (jj + 1) * 16, rnext);
                 uint32_t acc[16];
                 tmem_ld16(tmem + b * NCOLS + ((uint32_t)(32 * q) << 16) + (uint32_t)(j * 16), acc);
                 if (live) epi_store16(e, s_ws, s_bias, m0 + rr, j * 16, NT, acc, rcur);

@@ -6,8 +6,9 @@
 //   warps 0-3   producers:
 //     DENSE   (dense layers) thread 0 issues a 2-D TMA tile load of the 128 A rows (swizzled) and of the weights;
 //     GATHER  (convs) per item the warps gather the tap rows' 16-byte chunks with cp.async, lanes spread along K
-//             (absent neighbours zero-filled by the copy); completion is tracked with a lag of half the ring
-//             (cp.async.wait_group + proxy fence + arrive), so the MMA always has finished items queued.  The
+//             (absent neighbours zero-filled by the copy); each thread's copies arrive on the stage's mbarrier
+//             asynchronously (cp.async.mbarrier.arrive.noinc), so producers never block on their own copies and
+//             the whole ring can be in flight; the MMA thread fences the proxies after its wait.  The
 //             neighbour indices of the next tile are copied into shared memory (4-byte cp.async per row and tap,
 //             completion tracked by an mbarrier) while the current tile's items run, and thread 0 publishes each
 //             tile's record (rows, tap mask) through shared memory, so no producer waits on a dependent global
@@ -52,7 +53,6 @@ struct Cfg {
     static constexpr int kStage = kA + kB;
     static constexpr int kStagesRaw = (kBudget - kRes) / kStage;
     static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
-    static constexpr int kLag = KIND == GATHER ? (kStages / 2 > 1 ? kStages / 2 : 1) : 0;
     static constexpr int kSmem = kRes + kIdx + kStages * kStage + 1024 + 512;
     static_assert(RES || kStagesRaw >= 2, "shared memory budget");
 };
@@ -65,7 +65,6 @@ __global__ void __launch_bounds__(kThreads, 1)
               int Co, int taps, Epi e) {
     using C = Cfg<KIND, NT, W, RES>;
     constexpr int NST = C::kStages;
-    constexpr int LAG = C::kLag;
     constexpr int NCOLS = tmem_cols<NT>();
     constexpr uint32_t IDESC = instr_desc(kM, NT);
     constexpr uint32_t kSboA = (kItemK / 16) * 128;  // gathered A: bytes between 8-row groups (K/16 chunks of 128 B)
@@ -94,8 +93,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        // producer stages: one arrival per producer warp (lane 0 after __syncwarp) plus thread 0's TMA expect_tx
-        const uint32_t full_count = KIND == DENSE ? 1 : (RES ? kProducers / 32 : kProducers / 32 + 1);
+        // producer stages: one asynchronous arrival per producer thread (when its copies have landed) plus thread 0's
+        // TMA expect_tx
+        const uint32_t full_count = KIND == DENSE ? 1 : (RES ? kProducers : kProducers + 1);
         for (int s = 0; s < NST; ++s) {
             mbar_init(&full[s], full_count);
             mbar_init(&empty[s], 1);
@@ -201,8 +201,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t dst_lane = (uint32_t)((my_row >> 3) * kSboA + (my_row & 7) * 16 + my_c * kLboA);
             const int8_t* in_lane = in + my_c * 16;
             const uint32_t rows32 = (uint32_t)in_rows;             // in_rows < 2^31 and in_rows * Ci < 2^32
-            uint32_t pend_first = 0;
-            int pending = 0;
             const uint32_t idx_base = smem_u32(idx);
             auto publish = [&](int64_t u, uint32_t k) -> bool {      // thread 0
                 const uint32_t b = k & 1u, use = k >> 1;
@@ -298,17 +296,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 cp_async16(dst, in_lane + (valid ? id[g][p] * (uint32_t)Ci + koff : 0u), valid);
                             }
                         }
-                        cp_async_commit();
-                        ++pending;
-                        if (pending > LAG) {
-                            // every lane's copies of the oldest pending item have landed: one arrival per warp
-                            cp_async_wait<LAG>();
-                            fence_proxy_async();
-                            __syncwarp();
-                            if (lane == 0) mbar_arrive(&full[pend_first % NST]);
-                            ++pend_first;
-                            --pending;
-                        }
+                        // arrives on the stage once every copy this thread issued so far has landed; the MMA
+                        // thread orders them before its tensor-core reads with a proxy fence after the wait
+                        cp_async_mbar_arrive(&full[it % NST]);
                         ++it;
                         if (!prefetched) {
                             // after the first item: publish the next unit and start its index copies
@@ -324,13 +314,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ok = __all_sync(0xffffffffu, ok);
             }
             cp_async_wait_all();
-            fence_proxy_async();
-            __syncwarp();
-            while (pending > 0) {
-                if (lane == 0) mbar_arrive(&full[pend_first % NST]);
-                ++pend_first;
-                --pending;
-            }
         }
         if (!ok) {
             s_abort = 1;
@@ -367,6 +350,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int nt = take(mk, tv);
                     for (int kb = 0; kb < nkb; ++kb) {
                         if (!mbar_wait(&full[s], ph, &s_abort)) { ok = false; break; }
+                        // the gathered rows were written by the producers' cp.async (generic proxy); order them
+                        // before this thread's tensor-core (async proxy) reads
+                        if (KIND == GATHER) fence_proxy_async();
                         tc_fence_after();
                         const uint64_t ad0 = a_desc0 + s * STAGE;
                         const uint64_t bd0 = RES ? b_desc0 : b_desc0 + s * STAGE;
