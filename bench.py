@@ -143,9 +143,9 @@ def dominant_conv(torch, eng, reps: int = 20):
         if k == 0 and bool(eng.tensor_cores) and ops.grid0_supported(C_, C_):
             # level 0 runs the neighbour-map-free frame-grid kernel in the plan
             g = eng.geo
-            zq = eng.debug_tensor("zq", 0, (g.batch * g.height * g.width,), torch.int32)
-            run = lambda: ops.spconv_i8_grid0(q1, zq, g.batch, g.height, g.width, w, ws, b, 0.01, ops.EPI_SILU_Q8,
-                                              0.02)
+            lanes = eng.debug_tensor("lanes0", 0, ((g.batch * g.height * g.width + 127) // 128, 27, 4), torch.int32)
+            run = lambda: ops.spconv_i8_grid0(q1, lanes, g.batch, g.height, g.width, w, ws, b, 0.01,
+                                              ops.EPI_SILU_Q8, 0.02)
         else:
             run = lambda: ops.spconv_i8(q1, nmap, mask, w, ws, b, 0.01, ops.EPI_SILU_Q8, 0.02, count=cnt,
                                         tensor_cores=tc)

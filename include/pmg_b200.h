@@ -149,15 +149,21 @@ int pmg_spconv_i8(const int8_t* in_q8, int64_t in_rows, const int32_t* nmap, int
                   const float* w_scale, const float* bias, float act_scale, int32_t epilogue, float out_scale,
                   const float* resid, void* out, int32_t flags, int32_t* status, void* stream);
 
+/* Tap masks of level 0 for pmg_spconv_i8_grid0, the "column" neighbour rule of the level-0 neighbour map
+ * (_core.py:269-295) in bit form: tap_lanes [ceil(B*H*W/128)][27][4] uint32, word [t][v][g] bit l set when voxel
+ * 128 t + 32 g + l has its tap-v neighbour (pixel m + di*W + dj inside the frame, zq differing by dz).  zq as written
+ * by pmg_voxelize_l0 (any per-frame offset of z gives the same masks).  pmg_l0_tap_lanes_bytes gives the size. */
+size_t pmg_l0_tap_lanes_bytes(int32_t B, int32_t H, int32_t W);
+int pmg_l0_tap_lanes(const int32_t* zq, int32_t B, int32_t H, int32_t W, uint32_t* tap_lanes, void* stream);
+
 /* Level-0 submanifold conv of a frame grid, int8 x int8 -> int32, without a neighbour map.  Replaces the same
  * submanifold_conv (_core.py:399-441) as pmg_spconv_i8 for level 0 of the refiner, whose voxels are the B*H*W pixels
- * in pixel order with z = zq (the "column" neighbour rule of _core.py:269-295: tap (di,dj,dz) of voxel m is pixel
- * m + di*W + dj when that pixel is inside the frame and zq differs by dz).  in_q8 [B*H*W, Ci], zq [B*H*W] as written
- * by pmg_voxelize_l0 (any per-frame offset of z gives the same result), weight/w_scale/bias/epilogue as
- * pmg_spconv_i8, resid/out pitch Co.  Ci == Co in {32, 64} (else PMG_ERR_UNSUPPORTED).  tcgen05 kernel: shifted
- * 2-D TMA slabs as the A operands and per-row tap masks as the MMA's disabled output lanes; accumulators equal
- * pmg_spconv_i8's with the level-0 neighbour map bit for bit.  Pointers 16-byte aligned. */
-int pmg_spconv_i8_grid0(const int8_t* in_q8, const int32_t* zq, int32_t B, int32_t H, int32_t W, int32_t Ci,
+ * in pixel order (tap (di,dj,dz) of voxel m is pixel m + di*W + dj when tap_lanes says it exists).  in_q8
+ * [B*H*W, Ci], tap_lanes from pmg_l0_tap_lanes, weight/w_scale/bias/epilogue as pmg_spconv_i8, resid/out pitch Co.
+ * Ci == Co in {32, 64} (else PMG_ERR_UNSUPPORTED).  tcgen05 kernel: shifted 2-D TMA slabs as the A operands and the
+ * per-row tap masks as the MMA's disabled output lanes; accumulators equal pmg_spconv_i8's with the level-0
+ * neighbour map bit for bit.  Pointers 16-byte aligned. */
+int pmg_spconv_i8_grid0(const int8_t* in_q8, const uint32_t* tap_lanes, int32_t B, int32_t H, int32_t W, int32_t Ci,
                         int32_t Co, const int8_t* weight, const float* w_scale, const float* bias, float act_scale,
                         int32_t epilogue, float out_scale, const float* resid, void* out, int32_t* status,
                         void* stream);

@@ -100,6 +100,7 @@ struct pmg_refiner {
     void* fit_ws = nullptr;
     size_t fit_ws_bytes = 0;
     int32_t* zq = nullptr;         // [N]
+    uint32_t* lanes0 = nullptr;    // level-0 tap masks of the frame-grid conv: [ceil(N / 128)][27][4]
     int32_t* zext = nullptr;       // [2B]: zmin[B], zmax[B]
     int32_t* counts = nullptr;     // [L][2]
     int32_t* status = nullptr;
@@ -207,6 +208,7 @@ int allocate(pmg_refiner* r) {
     PMG_TRY(alloc(r, reinterpret_cast<char**>(&r->fit_ws), r->fit_ws_bytes));
     PMG_CUDA_TRY(cudaMemset(r->fit_ws, 0, r->fit_ws_bytes));
     PMG_TRY(alloc(r, &r->zq, r->N));
+    PMG_TRY(alloc(r, &r->lanes0, (size_t)((r->N + 127) / 128) * 27 * 4));
     PMG_TRY(alloc(r, &r->zext, 2 * B));
     PMG_TRY(alloc(r, &r->counts, 2 * r->L));
     PMG_TRY(alloc(r, &r->status, 1));
@@ -298,6 +300,7 @@ int check_weights(pmg_refiner* r) {
     } while (0)
 
 int flags_of(const pmg_refiner* r) { return r->cfg.use_tensor_cores ? 0 : PMG_FLAG_SIMT; }
+bool grid0_used(const pmg_refiner* r) { return r->cfg.use_tensor_cores && grid0_supported(r->lv[0].C, r->lv[0].C); }
 
 // Level 0 (one voxel per pixel) runs the neighbour-map-free frame-grid conv on the tensor-core path; the other
 // levels gather through their neighbour maps.
@@ -305,8 +308,8 @@ int conv(const pmg_refiner* r, int k, const LevelBuf& l, const int8_t* in, const
          const float* resid, void* out, const int32_t* count, cudaStream_t s, int8_t* q2 = nullptr,
          float q2_scale = 0.f) {
     Epi e{mode, q.sa, out_scale, q.ws, q.b, resid, out, r->status, q2, q2_scale};
-    if (k == 0 && r->cfg.use_tensor_cores && grid0_supported(l.C, l.C))
-        return conv_grid0_tc(in, r->zq, r->cfg.batch, r->cfg.height, r->cfg.width, l.C, l.C, q.w, e, s);
+    if (k == 0 && grid0_used(r))
+        return conv_grid0_tc(in, r->lanes0, r->cfg.batch, r->cfg.height, r->cfg.width, l.C, l.C, q.w, e, s);
     return gemm_i8(in, l.cap, l.nmap, l.cap, l.mask, count, l.cap, l.C, l.C, 27, q.w, flags_of(r), e, s);
 }
 
@@ -355,6 +358,7 @@ int enqueue_step(pmg_refiner* r, cudaStream_t s) {
     LevelBuf& l0 = r->lv[0];
     LAUNCH(pmg_voxelize_l0(r->pc, B, H, W, c.depth_resolution, r->zq, r->zext, r->zext + B, l0.nmap, l0.cap, l0.mask,
                            ss));
+    if (grid0_used(r)) LAUNCH(l0_tap_lanes(r->zq, B, H, W, r->lanes0, ss));
     PMG_CUDA_TRY(cudaEventRecord(r->ev_vox, ss));
     for (int k = 0; k + 1 < L; ++k) {
         LevelBuf& f = r->lv[k];
@@ -633,6 +637,7 @@ extern "C" void* pmg_refiner_debug_ptr(pmg_refiner* r, const char* what, int32_t
     if (!r || !what) return nullptr;
     const std::string w(what);
     if (w == "zq") return r->zq;
+    if (w == "lanes0") return r->lanes0;
     if (w == "zext") return r->zext;
     if (w == "counts") return r->counts;
     if (w == "pc") return r->pc;

@@ -29,8 +29,10 @@ int gemm_i8_tc(const int8_t* in, int64_t in_rows, const int32_t* nmap, int64_t l
 bool tc_supported(int Ci, int Co);
 // Level-0 conv of a frame grid without a neighbour map (shifted TMA slabs + masked MMA lanes); Ci == Co in {32, 64}.
 bool grid0_supported(int Ci, int Co);
-int conv_grid0_tc(const int8_t* in, const int32_t* zq, int B, int H, int W, int Ci, int Co, const int8_t* w,
+int conv_grid0_tc(const int8_t* in, const uint32_t* lanes, int B, int H, int W, int Ci, int Co, const int8_t* w,
                   const Epi& e, cudaStream_t s);
+// Per-tile tap masks of level 0 for conv_grid0_tc: [ceil(B*H*W / 128)][27][4] uint32 from zq.
+int l0_tap_lanes(const int32_t* zq, int B, int H, int W, uint32_t* lanes, cudaStream_t s);
 // Dispatch: tcgen05 where the shape is covered (unless flags has PMG_FLAG_SIMT), SIMT otherwise.
 int gemm_i8(const int8_t* in, int64_t in_rows, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask,
             const int32_t* count, int64_t max_rows, int Ci, int Co, int taps, const int8_t* w, int flags,

@@ -12,13 +12,14 @@
 //   initialises the accumulator.  A tap no row of the tile uses is skipped.
 // int32 accumulation is exact, so the accumulators equal the gather kernel's (and the reference's) bit for bit.
 //
-// Warp roles (256 threads, one persistent CTA per SM, tiles round-robin):
-//   warp 0       lane 0 issues the TMA loads: the 27-tap weight once (resident in shared memory), then per tile the
-//                9 slabs into an NS-stage ring.
+// The masks come precomputed (k_l0_tap_lanes, one ballot per (tap, 32-row group) from zq: bounds of the frame + the z
+// difference) as one 432-byte record per tile, bulk-copied next to the slabs.
+//
+// Warp roles (320 threads, one persistent CTA per SM, tiles round-robin):
+//   warp 0       lane 0 issues the copies: the 27-tap weight once (resident in shared memory), then per tile its mask
+//                record into a ring of NR records and its 9 slabs into an NS-stage ring.
 //   warp 1       lane 0 issues the MMAs into one of two TMEM accumulators and commits stages / accumulators.
-//   warps 2-3    build each tile's 27 x 128-bit masks from zq (bounds of the frame + the z difference), one ballot
-//                per (tap, 32-row group), into a ring of NR mask records.
-//   warps 4-11   epilogue: two warps per TMEM lane quarter (warp & 3), each on half of the output channels, the same
+//   warps 2-9    epilogue: two warps per TMEM lane quarter (warp & 3), each on half of the output channels, the same
 //                fused dequant / SiLU / requantise / residual as the gather kernel (the SiLU + requantise arithmetic
 //                is issue-bound, so two warps per SM sub-partition hide each other's latency).
 // Every wait is bounded; on expiry the CTA records PMG_ERR_TIMEOUT, lets issued MMAs retire, frees TMEM, returns.
@@ -33,7 +34,7 @@ namespace tcg {
 using namespace tc;
 
 constexpr int kEpiWarps = 8;
-constexpr int kThreads = 32 * (4 + kEpiWarps);
+constexpr int kThreads = 32 * (2 + kEpiWarps);
 constexpr int kNR = 8;                  // mask records in flight
 constexpr int kRec = 27 * 4 * 4;        // one record: enable words [27 taps][4 row groups]
 constexpr int kBudget = 200 * 1024;    // resident weights + slab ring
@@ -67,7 +68,7 @@ __device__ __forceinline__ int slab_of(int k) { return k == 0 ? 4 : (k <= 4 ? k 
 template <int NT, int W>
 __global__ void __launch_bounds__(kThreads, 1)
     k_conv_grid0(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                 const int32_t* __restrict__ zq, int B, int H, int Wd, Epi e) {
+                 const uint32_t* __restrict__ lanes, int B, int H, int Wd, Epi e) {
     using C = GCfg<NT, W>;
     constexpr int NS = C::kStages;
     constexpr int NCOLS = tmem_cols<NT>();
@@ -96,7 +97,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&empty[s], 1);
         }
         for (int r = 0; r < kNR; ++r) {
-            mbar_init(&rec_full[r], 2);
+            mbar_init(&rec_full[r], 1);
             mbar_init(&rec_empty[r], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -137,9 +138,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive_expect_tx(wres, (uint32_t)C::kRes);
                 for (int v = 0; v < 27; ++v) tma_tile2d(res_base + v * NT * W, &tmB, 0, v * NT, wres);
             }
-            uint32_t st = 0, ph = 0;
-            for (int64_t t = blockIdx.x; t < ntile && ok; t += gridDim.x) {
+            uint32_t st = 0, ph = 0, kt = 0;
+            for (int64_t t = blockIdx.x; t < ntile && ok; t += gridDim.x, ++kt) {
                 const int m0 = (int)(t * kM);
+                const uint32_t rs = kt & (kNR - 1);
+                if (!mbar_wait(&rec_empty[rs], ((kt / kNR) & 1u) ^ 1u, &s_abort)) { ok = false; break; }
+                mbar_arrive_expect_tx(&rec_full[rs], (uint32_t)kRec);
+                bulk_g2s(smem_u32(recs + rs * 27 * 4), lanes + t * 27 * 4, (uint32_t)kRec, &rec_full[rs]);
 #pragma unroll
                 for (int k = 0; k < 9; ++k) {
                     constexpr int SPS = C::SPS;
@@ -175,11 +180,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_after();
                 const uint32_t d = tmem + b * NCOLS;
                 const uint4* rec = reinterpret_cast<const uint4*>(recs + rs * 27 * 4);
+                // the masks of the next slab are loaded before this slab's MMAs are issued
+                uint4 n0 = rec[slab_of(0) * 3], n1 = rec[slab_of(0) * 3 + 1], n2 = rec[slab_of(0) * 3 + 2];
 #pragma unroll
                 for (int kk9 = 0; kk9 < 9; ++kk9) {
                     const int s9 = slab_of(kk9);
                     constexpr int SPS = C::SPS;
-                    const uint4 e0 = rec[s9 * 3], e1 = rec[s9 * 3 + 1], e2 = rec[s9 * 3 + 2];
+                    const uint4 e0 = n0, e1 = n1, e2 = n2;
+                    if (kk9 + 1 < 9) {
+                        n0 = rec[slab_of(kk9 + 1) * 3];
+                        n1 = rec[slab_of(kk9 + 1) * 3 + 1];
+                        n2 = rec[slab_of(kk9 + 1) * 3 + 2];
+                    }
                     if (kk9 % SPS == 0) {
                         if (!mbar_wait(&full[st], ph, &s_abort)) { ok = false; break; }
                         tc_fence_after();
@@ -220,61 +232,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
         __syncwarp();
-    } else if (warp < 4) {
-        // ============================================ row masks ============================================ //
-        // Warp 2 + mw builds row groups 2 mw and 2 mw + 1 of each tile: bit `lane` of word [tap][group] is set when
-        // row 32 group + lane has that neighbour.  All 20 z loads of both groups are issued before the ballots.
-        const int mw = warp - 2;
-        const uint32_t n32 = (uint32_t)N, hw32 = (uint32_t)HW, w32 = (uint32_t)Wd;
-        bool ok = true;
-        uint32_t k = 0;
-        for (int64_t t = blockIdx.x; t < ntile && ok; t += gridDim.x, ++k) {
-            const uint32_t rs = k & (kNR - 1);
-            ok = __all_sync(0xffffffffu, mbar_wait(&rec_empty[rs], ((k / kNR) & 1u) ^ 1u, &s_abort));
-            if (!ok) break;
-            uint32_t* rec = recs + rs * 27 * 4;
-            int z0[2], zn[2][9];
-#pragma unroll
-            for (int gg = 0; gg < 2; ++gg) {
-                const uint32_t o = (uint32_t)t * kM + 32u * (2 * mw + gg) + lane;
-                const bool valid = o < n32;
-                const uint32_t rem = valid ? o % hw32 : 0u;
-                const int i = (int)(rem / w32), j = (int)(rem - (rem / w32) * w32);
-                z0[gg] = valid ? zq[o] : 0;
-#pragma unroll
-                for (int s9 = 0; s9 < 9; ++s9) {
-                    const int di = s9 / 3 - 1, dj = s9 % 3 - 1;
-                    const bool in = valid && i + di >= 0 && i + di < H && j + dj >= 0 && j + dj < Wd;
-                    zn[gg][s9] = in ? zq[(int)o + di * Wd + dj] : INT32_MIN;
-                }
-            }
-#pragma unroll
-            for (int gg = 0; gg < 2; ++gg) {
-                uint32_t mine = 0;
-#pragma unroll
-                for (int s9 = 0; s9 < 9; ++s9) {
-                    // INT32_MIN marks "outside the frame": its difference never lands in [-1, 1]
-                    const int dz = zn[gg][s9] == INT32_MIN ? 2 : zn[gg][s9] - z0[gg];
-#pragma unroll
-                    for (int dzi = 0; dzi < 3; ++dzi) {
-                        const uint32_t bal = __ballot_sync(0xffffffffu, dz == dzi - 1);
-                        if (lane == s9 * 3 + dzi) mine = bal;
-                    }
-                }
-                if (lane < 27) rec[lane * 4 + 2 * mw + gg] = mine;
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&rec_full[rs]);
-        }
-        if (!ok) {
-            s_abort = 1;
-            flag(e.status, PMG_ERR_TIMEOUT);
-        }
     } else {
         // ============================================ epilogue ============================================ //
         const int q = warp & 3;
         constexpr int CH = NT / 32;                   // 16-column chunks per epilogue warp
-        const int j0 = ((warp - 4) >> 2) * CH;
+        const int j0 = ((warp - 2) >> 2) * CH;
         uint32_t k = 0;
         bool ok = true;
         for (int64_t t = blockIdx.x; t < ntile && ok; t += gridDim.x, ++k) {
@@ -319,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 namespace {
 
 template <int NT, int W>
-int launch_grid0(const int8_t* in, const int32_t* zq, int B, int H, int Wd, const int8_t* w, const Epi& e,
+int launch_grid0(const int8_t* in, const uint32_t* lanes, int B, int H, int Wd, const int8_t* w, const Epi& e,
                  cudaStream_t s) {
     using C = tcg::GCfg<NT, W>;
     static bool attr_set[64] = {};
@@ -340,7 +302,7 @@ int launch_grid0(const int8_t* in, const int32_t* zq, int B, int H, int Wd, cons
     if (rc != PMG_OK) return rc;
     rc = make_tensor_map(&mb, w, (uint64_t)27 * NT, (uint64_t)W, W, NT);
     if (rc != PMG_OK) return rc;
-    tcg::k_conv_grid0<NT, W><<<grid, tcg::kThreads, C::kSmem, s>>>(ma, mb, zq, B, H, Wd, e);
+    tcg::k_conv_grid0<NT, W><<<grid, tcg::kThreads, C::kSmem, s>>>(ma, mb, lanes, B, H, Wd, e);
     PMG_LAUNCH_CHECK();
     return PMG_OK;
 }
@@ -349,29 +311,88 @@ int launch_grid0(const int8_t* in, const int32_t* zq, int B, int H, int Wd, cons
 
 bool grid0_supported(int Ci, int Co) { return Ci == Co && (Ci == 32 || Ci == 64); }
 
-int conv_grid0_tc(const int8_t* in, const int32_t* zq, int B, int H, int W, int Ci, int Co, const int8_t* w,
+int conv_grid0_tc(const int8_t* in, const uint32_t* lanes, int B, int H, int W, int Ci, int Co, const int8_t* w,
                   const Epi& e, cudaStream_t s) {
     if (!grid0_supported(Ci, Co)) return PMG_ERR_UNSUPPORTED;
     if (B <= 0 || H <= 0 || W <= 0) return PMG_ERR_BAD_ARG;
     const int64_t N = (int64_t)B * H * W;
     if (N >= INT32_MAX - 2 * (int64_t)W - 256) return PMG_ERR_UNSUPPORTED;   // TMA row coordinates are int32
-    if (Ci == 32) return launch_grid0<32, 32>(in, zq, B, H, W, w, e, s);
-    return launch_grid0<64, 64>(in, zq, B, H, W, w, e, s);
+    if (reinterpret_cast<uintptr_t>(lanes) & 15) return PMG_ERR_BAD_ARG;      // bulk copies of 16-byte multiples
+    if (Ci == 32) return launch_grid0<32, 32>(in, lanes, B, H, W, w, e, s);
+    return launch_grid0<64, 64>(in, lanes, B, H, W, w, e, s);
+}
+
+// ------------------------------------------------------------------------------------------------------------- //
+// Tap masks of level 0: word [tile][tap][group] has bit `lane` set when row 128 tile + 32 group + lane has the tap's
+// neighbour (inside the frame, z difference dz).  One warp per 32-row group; all 10 z loads are issued first.
+// ------------------------------------------------------------------------------------------------------------- //
+
+__global__ void __launch_bounds__(256) k_l0_tap_lanes(const int32_t* __restrict__ zq, int B, int H, int W,
+                                                      uint32_t* __restrict__ lanes) {
+    const int64_t N = (int64_t)B * H * W;
+    const int64_t groups = (N + 127) / 128 * 4;
+    const int lane = threadIdx.x & 31;
+    const int64_t g = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (g >= groups) return;
+    const int64_t o = g * 32 + lane;
+    const bool valid = o < N;
+    int i = 0, j = 0, z0 = 0;
+    if (valid) {
+        const int64_t rem = o % ((int64_t)H * W);
+        i = (int)(rem / W);
+        j = (int)(rem - (int64_t)i * W);
+        z0 = zq[o];
+    }
+    int dz[9];
+#pragma unroll
+    for (int s9 = 0; s9 < 9; ++s9) {
+        const int di = s9 / 3 - 1, dj = s9 % 3 - 1;
+        const bool in = valid && i + di >= 0 && i + di < H && j + dj >= 0 && j + dj < W;
+        dz[s9] = in ? zq[o + (int64_t)di * W + dj] : 0;
+        dz[s9] = in ? dz[s9] - z0 : 2;                  // 2: no neighbour at any dz
+    }
+    uint32_t mine = 0;
+#pragma unroll
+    for (int s9 = 0; s9 < 9; ++s9)
+#pragma unroll
+        for (int d = 0; d < 3; ++d) {
+            const uint32_t bal = __ballot_sync(0xffffffffu, dz[s9] == d - 1);
+            if (lane == s9 * 3 + d) mine = bal;
+        }
+    if (lane < 27) lanes[(g >> 2) * 108 + lane * 4 + (g & 3)] = mine;
+}
+
+int l0_tap_lanes(const int32_t* zq, int B, int H, int W, uint32_t* lanes, cudaStream_t s) {
+    if (!zq || !lanes || B <= 0 || H <= 0 || W <= 0) return PMG_ERR_BAD_ARG;
+    const int64_t N = (int64_t)B * H * W;
+    const int64_t groups = (N + 127) / 128 * 4;
+    k_l0_tap_lanes<<<ceil_div(groups * 32, 256), 256, 0, s>>>(zq, B, H, W, lanes);
+    PMG_LAUNCH_CHECK();
+    return PMG_OK;
 }
 
 }  // namespace pmg
 
 using namespace pmg;
 
-extern "C" int pmg_spconv_i8_grid0(const int8_t* in_q8, const int32_t* zq, int32_t B, int32_t H, int32_t W,
+extern "C" size_t pmg_l0_tap_lanes_bytes(int32_t B, int32_t H, int32_t W) {
+    if (B <= 0 || H <= 0 || W <= 0) return 0;
+    return (size_t)(((int64_t)B * H * W + 127) / 128) * tcg::kRec;
+}
+
+extern "C" int pmg_l0_tap_lanes(const int32_t* zq, int32_t B, int32_t H, int32_t W, uint32_t* lanes, void* stream) {
+    return l0_tap_lanes(zq, B, H, W, lanes, as_stream(stream));
+}
+
+extern "C" int pmg_spconv_i8_grid0(const int8_t* in_q8, const uint32_t* tap_lanes, int32_t B, int32_t H, int32_t W,
                                    int32_t Ci, int32_t Co, const int8_t* weight, const float* w_scale,
                                    const float* bias, float act_scale, int32_t epilogue, float out_scale,
                                    const float* resid, void* out, int32_t* status, void* stream) {
-    if (!in_q8 || !zq || !weight || !out) return PMG_ERR_BAD_ARG;
+    if (!in_q8 || !tap_lanes || !weight || !out) return PMG_ERR_BAD_ARG;
     if (epilogue < PMG_EPI_ACC32 || epilogue > PMG_EPI_SILU_Q8) return PMG_ERR_BAD_ARG;
     if (epilogue != PMG_EPI_ACC32 && (!w_scale || !bias)) return PMG_ERR_BAD_ARG;
     if (epilogue == PMG_EPI_F32_RESID && !resid) return PMG_ERR_BAD_ARG;
     if (!grid0_supported(Ci, Co)) return PMG_ERR_UNSUPPORTED;
     Epi e{epilogue, act_scale, out_scale, w_scale, bias, resid, out, status};
-    return conv_grid0_tc(in_q8, zq, B, H, W, Ci, Co, weight, e, as_stream(stream));
+    return conv_grid0_tc(in_q8, tap_lanes, B, H, W, Ci, Co, weight, e, as_stream(stream));
 }

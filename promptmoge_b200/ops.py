@@ -147,17 +147,26 @@ def spconv_i8(q_in, nmap, tile_mask, weight_tap_major, w_scale=None, bias=None, 
     return out
 
 
-def spconv_i8_grid0(q_in, zq, B, H, W, weight_tap_major, w_scale=None, bias=None, act_scale=1.0, mode=EPI_ACC32,
-                    out_scale=1.0, resid=None, status=None):
-    """Level-0 submanifold conv of a B x H x W frame grid (one voxel per pixel, z = zq) without a neighbour map:
-    q_in [B*H*W, C] int8, zq [B*H*W] int32, weight [27, C, C] int8, C in {32, 64}."""
-    _dev(q_in, torch.int8, "q_in")
+def l0_tap_lanes(zq, B, H, W):
+    """Per-tile tap masks of level 0 ([ceil(B*H*W/128), 27, 4] int32 view of the uint32 words) from zq."""
     _dev(zq, torch.int32, "zq")
+    n = (B * H * W + 127) // 128
+    lanes = torch.empty((n, 27, 4), dtype=torch.int32, device=zq.device)
+    call("pmg_l0_tap_lanes", _p(zq), B, H, W, _p(lanes), _stream())
+    return lanes
+
+
+def spconv_i8_grid0(q_in, lanes, B, H, W, weight_tap_major, w_scale=None, bias=None, act_scale=1.0, mode=EPI_ACC32,
+                    out_scale=1.0, resid=None, status=None):
+    """Level-0 submanifold conv of a B x H x W frame grid (one voxel per pixel) without a neighbour map:
+    q_in [B*H*W, C] int8, lanes from l0_tap_lanes, weight [27, C, C] int8, C in {32, 64}."""
+    _dev(q_in, torch.int8, "q_in")
+    _dev(lanes, torch.int32, "lanes")
     _dev(weight_tap_major, torch.int8, "weight")
     rows = B * H * W
     Co, Ci = weight_tap_major.shape[1], weight_tap_major.shape[2]
     out = _epi_out(mode, rows, Co, q_in.device)
-    call("pmg_spconv_i8_grid0", _p(q_in), _p(zq), B, H, W, Ci, Co, _p(weight_tap_major), _p(w_scale), _p(bias),
+    call("pmg_spconv_i8_grid0", _p(q_in), _p(lanes), B, H, W, Ci, Co, _p(weight_tap_major), _p(w_scale), _p(bias),
          float(act_scale), mode, float(out_scale), _p(resid), _p(out), _p(status), _stream())
     return out
 

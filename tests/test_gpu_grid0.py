@@ -36,6 +36,7 @@ def test_grid0_reference_accumulators(golden, name):
     coords = g["s0_L0_coords"]
     assert coords.shape[0] == H * W
     zq = torch.from_numpy(np.ascontiguousarray(coords[:, 3]).astype(np.int32)).cuda()
+    lanes = ops.l0_tap_lanes(zq, 1, H, W)
     w = g.weights()
     names = _level0_convs(g)
     assert len(names) == 4, names
@@ -45,9 +46,9 @@ def test_grid0_reference_accumulators(golden, name):
         q = torch.from_numpy(g[key + "_q"]).cuda()
         qw, sw = quantise_weight(w[n + ".weight"])
         wt = _tap_major_weight(qw)
-        acc = ops.spconv_i8_grid0(q, zq, 1, H, W, wt, status=status)
+        acc = ops.spconv_i8_grid0(q, lanes, 1, H, W, wt, status=status)
         sa = act_scale(g.clips[n])
-        f32 = ops.spconv_i8_grid0(q, zq, 1, H, W, wt, torch.from_numpy(sw).cuda(),
+        f32 = ops.spconv_i8_grid0(q, lanes, 1, H, W, wt, torch.from_numpy(sw).cuda(),
                                   torch.from_numpy(w[n + ".bias"]).cuda(), sa, ops.EPI_F32, status=status)
         torch.cuda.synchronize()
         acc_np = acc.cpu().numpy()
@@ -87,7 +88,14 @@ def test_grid0_equals_gather_every_epilogue(B, H, W, C, kind):
     else:
         pc = _rough_point_map(B, H, W, seed=H * W + C)
     zq, _, _, nmap, mask = ops.voxelize_l0(torch.from_numpy(np.ascontiguousarray(pc)).cuda())
+    lanes = ops.l0_tap_lanes(zq, B, H, W)
     N = B * H * W
+    # the masks are the level-0 neighbour map in bit form
+    nm = nmap.cpu().numpy()[:, :N]
+    ln = lanes.cpu().numpy().view(np.uint32)
+    rows = np.arange(N)
+    bits = (ln[rows // 128, :, (rows // 32) % 4] >> (rows % 32)[:, None].astype(np.uint32)) & 1
+    np.testing.assert_array_equal(bits.astype(bool), (nm >= 0).T)
     rng = np.random.default_rng(C + N)
     q = torch.from_numpy(rng.integers(-127, 128, (N, C)).astype(np.int8)).cuda()
     wt = torch.from_numpy(rng.integers(-127, 128, (27, C, C)).astype(np.int8)).cuda()
@@ -97,15 +105,15 @@ def test_grid0_equals_gather_every_epilogue(B, H, W, C, kind):
     status = torch.zeros(1, dtype=torch.int32).cuda()
     for mode in (ops.EPI_ACC32, ops.EPI_F32, ops.EPI_F32_RESID, ops.EPI_SILU_Q8):
         want = ops.spconv_i8(q, nmap, mask, wt, ws, b, 0.03, mode, 0.05, resid, status=status)
-        got = ops.spconv_i8_grid0(q, zq, B, H, W, wt, ws, b, 0.03, mode, 0.05, resid, status=status)
-        again = ops.spconv_i8_grid0(q, zq, B, H, W, wt, ws, b, 0.03, mode, 0.05, resid, status=status)
+        got = ops.spconv_i8_grid0(q, lanes, B, H, W, wt, ws, b, 0.03, mode, 0.05, resid, status=status)
+        again = ops.spconv_i8_grid0(q, lanes, B, H, W, wt, ws, b, 0.03, mode, 0.05, resid, status=status)
         assert torch.equal(got, want), mode
         assert torch.equal(again, got), mode
     if kind == "rough":
         # the oracle's exact int64 accumulators over the level-0 neighbour map
         nm = nmap.cpu().numpy()[:, :N].T
         wnp = wt.cpu().numpy().transpose(1, 0, 2).reshape(C, 3, 3, 3, C)
-        acc = ops.spconv_i8_grid0(q, zq, B, H, W, wt).cpu().numpy()
+        acc = ops.spconv_i8_grid0(q, lanes, B, H, W, wt).cpu().numpy()
         np.testing.assert_array_equal(acc.astype(np.int64), oref.conv_acc(q.cpu().numpy(), nm, wnp))
     assert int(status.item()) == 0
 
@@ -113,7 +121,7 @@ def test_grid0_equals_gather_every_epilogue(B, H, W, C, kind):
 def test_grid0_rejects_unsupported_widths():
     from promptmoge_b200 import ops
     q = torch.zeros((64, 128), dtype=torch.int8).cuda()
-    zq = torch.zeros(64, dtype=torch.int32).cuda()
+    lanes = ops.l0_tap_lanes(torch.zeros(64, dtype=torch.int32).cuda(), 1, 8, 8)
     wt = torch.zeros((27, 128, 128), dtype=torch.int8).cuda()
     with pytest.raises(Exception):
-        ops.spconv_i8_grid0(q, zq, 1, 8, 8, wt)
+        ops.spconv_i8_grid0(q, lanes, 1, 8, 8, wt)
