@@ -36,8 +36,10 @@ namespace pmg {
 namespace tc {
 
 constexpr int kProducers = 128;                   // warps 0-3
-constexpr int kEpiWarps = 4;                      // warps 5-8
-constexpr int kThreads = 32 * (5 + kEpiWarps);
+constexpr int kMmaWarps = 2;                      // warps 4-5
+constexpr int kEpiWarps = 8;                      // warps 6-13
+constexpr int kEpi0 = 4 + kMmaWarps;              // first epilogue warp
+constexpr int kThreads = 32 * (4 + kMmaWarps + kEpiWarps);
 constexpr int kItemK = 128;
 constexpr int kBudget = 196 * 1024;               // shared memory for resident weights + ring
 constexpr int kResMax = 110592;                   // 27-tap weights kept resident up to this size (64 x 64 x 27)
@@ -54,7 +56,8 @@ struct Cfg {
     static constexpr int kStagesRaw = (kBudget - kRes) / kStage;
     static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
     static constexpr int kSmem = kRes + kIdx + kStages * kStage + 1024 + 512;
-    static_assert(RES || kStagesRaw >= 2, "shared memory budget");
+    static_assert(RES || kStagesRaw >= 3, "shared memory budget");
+    static_assert(kStages >= 3, "two MMA warps need >= 3 ring stages for sound parity waits");
 };
 
 template <int KIND, int NT, int W, bool RES>
@@ -67,8 +70,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int NST = C::kStages;
     constexpr int NCOLS = tmem_cols<NT>();
     constexpr uint32_t IDESC = instr_desc(kM, NT);
-    constexpr uint32_t kSboA = (kItemK / 16) * 128;  // gathered A: bytes between 8-row groups (K/16 chunks of 128 B)
-    constexpr uint32_t kLboA = 128;                  // gathered A: bytes between K-adjacent core matrices
     constexpr int TPI = W < kItemK ? kItemK / W : 1;  // most taps per item
     constexpr int CPR = W / 16;                      // 16-byte chunks of one tap row in an item
     constexpr int RPP = 32 / CPR;                    // rows a warp covers per pass
@@ -79,13 +80,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* ring = res + C::kRes + C::kIdx;
     uint64_t* full = reinterpret_cast<uint64_t*>(ring + NST * C::kStage);
     uint64_t* empty = full + NST;
-    uint64_t* acc_full = empty + NST;       // [2]
-    uint64_t* acc_empty = acc_full + 2;     // [2]
-    uint64_t* idx_full = acc_empty + 2;     // [2] indices of a tile landed
+    uint64_t* acc_full = empty + NST;       // [4] (two used) accumulator buffer k & 1 of unit k: both warps' partials
+    uint64_t* acc_empty = acc_full + 4;     // [4]
+    uint64_t* idx_full = acc_empty + 4;     // [2] indices of a tile landed
     uint64_t* rec_full = idx_full + 2;      // [2] record of a tile published
     uint64_t* rec_free = rec_full + 2;      // [2] record read by every producer
-    uint64_t* drain = rec_free + 2;
-    uint64_t* wres = drain + 1;
+    uint64_t* drain = rec_free + 2;         // [2] one per MMA warp
+    uint64_t* wres = drain + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(wres + 1);
     __shared__ volatile int s_abort;
     __shared__ float s_ws[256], s_bias[256];           // epilogue per-channel weight scale and bias
@@ -100,14 +101,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&full[s], full_count);
             mbar_init(&empty[s], 1);
         }
+        for (int a = 0; a < 4; ++a) {
+            mbar_init(&acc_full[a], kMmaWarps);
+            mbar_init(&acc_empty[a], kEpiWarps);
+        }
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&acc_full[b], 1);
-            mbar_init(&acc_empty[b], kEpiWarps);
             mbar_init(&idx_full[b], kProducers + 1);
             mbar_init(&rec_full[b], 1);
             mbar_init(&rec_free[b], kProducers);
+            mbar_init(&drain[b], 1);
         }
-        mbar_init(drain, 1);
         mbar_init(wres, 1);
         s_abort = 0;
         fence_mbar_init();
@@ -117,7 +120,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             s_ws[n] = e.ws[n];
             s_bias[n] = e.bias[n];
         }
-    if (warp == 4) tmem_alloc(tmem_slot, 2 * NCOLS);
+    if (warp == 4) tmem_alloc(tmem_slot, 4 * NCOLS);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -198,7 +201,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int my_c = lane % CPR, my_sub = lane / CPR;
             const int my_row = 32 * warp + my_sub;                 // first row this lane copies (then + p * RPP)
             // this lane's part of every copy: row group / row-in-group / 16-byte K chunk offsets in a stage
-            const uint32_t dst_lane = (uint32_t)((my_row >> 3) * kSboA + (my_row & 7) * 16 + my_c * kLboA);
             const int8_t* in_lane = in + my_c * 16;
             const uint32_t rows32 = (uint32_t)in_rows;             // in_rows < 2^31 and in_rows * Ci < 2^32
             const uint32_t idx_base = smem_u32(idx);
@@ -288,11 +290,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                             for (int p = 0; p < CPR; ++p) {
                                 const bool valid = id[g][p] < rows32;
-                                // row my_row + p * RPP: whole 8-row groups plus a row offset that never carries
-                                // (my_row & 7 < RPP when RPP < 8)
-                                const uint32_t dst = sa + dst_lane +
-                                                     (uint32_t)(((p * RPP) >> 3) * kSboA + ((p * RPP) & 7) * 16 +
-                                                                g * CPR * kLboA);
+                                // row r = my_row + p * RPP of the item, 16-byte chunk c = g * CPR + my_c of its
+                                // 128-byte K row, in the 128-byte-swizzled K-major layout: rows 128 bytes apart,
+                                // chunk c stored at c ^ (r & 7) (bank-conflict-free across the warp's 8 rows)
+                                const uint32_t row = (uint32_t)(my_row + p * RPP);
+                                const uint32_t dst = sa + row * 128u + ((((uint32_t)(g * CPR + my_c)) ^ (row & 7u)) << 4);
                                 cp_async16(dst, in_lane + (valid ? id[g][p] * (uint32_t)Ci + koff : 0u), valid);
                             }
                         }
@@ -319,68 +321,95 @@ __global__ void __launch_bounds__(kThreads, 1)
             s_abort = 1;
             flag(e.status, PMG_ERR_TIMEOUT);
         }
-    } else if (warp == 4) {
-        // =========================================== MMA issuer =========================================== //
+    } else if (warp < kEpi0) {
+        // ========================================== MMA issuers ========================================== //
+        // Two issuing warps split every unit's items: warp 4 + w takes the unit's items w, w + 2, w + 4, ... into its
+        // own TMEM accumulator (the epilogue adds the two; integer sums are exact in any order), so one thread's wait
+        // and issue latency overlaps the other's MMAs.  Each warp waits for its next two items at once (a wait issued
+        // after MMAs costs a few hundred cycles).  A parity wait is only sound when the stage's previous phase has
+        // completed: a warp's previous item is at most 3 positions back (across a unit boundary), so single waits need
+        // >= 3 stages and the batched wait on item i + 2 needs >= 5.
+        const int mw = warp - 4;
         if (lane == 0) {
-            // A lean loop: every instruction of this single thread costs its full latency, so descriptors are
-            // precomputed and advanced in descriptor address units (16 bytes), ring positions incrementally.
-            uint32_t t = 0, s = 0, ph = 0;
+            // A lean loop: descriptors are precomputed and advanced in descriptor address units (16 bytes).
+            constexpr bool BATCH = NST >= 5;
+            uint32_t us = 0, uph = 0;             // ring position (stage, phase parity) of the unit's first item
             bool ok = true, issued = false;
             if (RES && nunits > (int64_t)blockIdx.x) ok = mbar_wait(wres, 0, &s_abort);
-            const uint64_t a_desc0 = KIND == DENSE ? desc_sw<W>(ring_base) : desc_plain(ring_base, kLboA, kSboA);
+            const uint64_t a_desc0 = KIND == DENSE ? desc_sw<W>(ring_base) : desc_sw<128>(ring_base);
             const uint64_t b_desc0 = RES ? desc_sw<W>(res_base) : desc_sw<W>(ring_base + C::kA);
             constexpr uint64_t STAGE = C::kStage >> 4;
-            constexpr uint64_t A_G = (CPR * kLboA) >> 4;                        // next tap of a gathered item
-            constexpr uint64_t A_KK = KIND == DENSE ? 2 : (2 * kLboA) >> 4;     // next 32 bytes of K
+            constexpr uint64_t A_G = W >> 4;                                     // next tap of a gathered item
+            constexpr uint64_t A_KK = 2;                                         // next 32 bytes of K
             constexpr uint64_t B_G = (NT * W) >> 4;                              // next tap's weights
-            int64_t xm0;
-            int xmc;
-            uint32_t xmk = 1;
-            if ((int64_t)blockIdx.x < nunits) tile_of(blockIdx.x / nblk, xm0, xmc, xmk);
-            for (int64_t u = blockIdx.x; u < nunits && ok; u += gridDim.x, ++t) {
-                uint32_t mk = xmk;
-                if (u + gridDim.x < nunits) tile_of((u + gridDim.x) / nblk, xm0, xmc, xmk);
-                const uint32_t b = t & 1u;
-                if (!mbar_wait(&acc_empty[b], ((t >> 1) & 1u) ^ 1u, &s_abort)) { ok = false; break; }
+            uint32_t k = 0;
+            for (int64_t u = blockIdx.x; u < nunits && ok; u += gridDim.x, ++k) {
+                int64_t m0;
+                int mc;
+                uint32_t mk;
+                tile_of(u / nblk, m0, mc, mk);
+                const int nitems = ((__popc(mk) + tpi - 1) / tpi) * nkb;
+                const uint32_t b = k & 1u;
+                if (!mbar_wait(&acc_empty[b], ((k >> 1) & 1u) ^ 1u, &s_abort)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t d = tmem + b * NCOLS;
+                const uint32_t d = tmem + (2 * b + (uint32_t)mw) * NCOLS;
                 uint32_t accumulate = 0;
-                while (mk && ok) {
-                    int tv[TPI];
-                    const int nt = take(mk, tv);
-                    for (int kb = 0; kb < nkb; ++kb) {
+                int tv[TPI];
+#pragma unroll
+                for (int g = 0; g < TPI; ++g) tv[g] = 0;
+                int nt = 0, kb = 0, ready = 0;
+                // walk the unit's item sequence; this warp issues items mw, mw + 2, ...
+                for (int i = 0; i < nitems; ++i) {
+                    if (kb == 0) nt = take(mk, tv);
+                    if (++kb == nkb) kb = 0;
+                    if ((i & 1) != mw) continue;
+                    const uint32_t pos = us + (uint32_t)i;
+                    const uint32_t s = pos % NST, ph = uph ^ ((pos / NST) & 1u);
+                    if (ready == 0) {
                         if (!mbar_wait(&full[s], ph, &s_abort)) { ok = false; break; }
+                        ready = 1;
+                        if (BATCH && i + 2 < nitems) {
+                            const uint32_t p2 = pos + 2;
+                            if (!mbar_wait(&full[p2 % NST], uph ^ ((p2 / NST) & 1u), &s_abort)) { ok = false; break; }
+                            ready = 2;
+                        }
                         // the gathered rows were written by the producers' cp.async (generic proxy); order them
                         // before this thread's tensor-core (async proxy) reads
                         if (KIND == GATHER) fence_proxy_async();
                         tc_fence_after();
-                        const uint64_t ad0 = a_desc0 + s * STAGE;
-                        const uint64_t bd0 = RES ? b_desc0 : b_desc0 + s * STAGE;
-#pragma unroll
-                        for (int g = 0; g < TPI; ++g) {
-                            if (g >= nt) break;
-                            const uint64_t bdg = RES ? bd0 + (uint64_t)tv[g] * B_G : bd0 + g * B_G;
-#pragma unroll
-                            for (int kk = 0; kk < W / 32; ++kk) {
-                                mma_i8(d, ad0 + g * A_G + kk * A_KK, bdg + 2 * kk, IDESC, accumulate);
-                                accumulate = 1;
-                            }
-                        }
-                        issued = true;
-                        mma_commit(&empty[s]);
-                        if (++s == (uint32_t)NST) { s = 0; ph ^= 1u; }
                     }
+                    const uint64_t ad0 = a_desc0 + s * STAGE;
+                    const uint64_t bd0 = RES ? b_desc0 : b_desc0 + s * STAGE;
+#pragma unroll
+                    for (int g = 0; g < TPI; ++g) {
+                        if (g >= nt) break;
+                        const uint64_t bdg = RES ? bd0 + (uint64_t)tv[g] * B_G : bd0 + g * B_G;
+#pragma unroll
+                        for (int kk = 0; kk < W / 32; ++kk) {
+                            mma_i8(d, ad0 + (KIND == GATHER ? g * A_G : 0) + kk * A_KK, bdg + 2 * kk, IDESC,
+                                   accumulate);
+                            accumulate = 1;
+                        }
+                    }
+                    issued = true;
+                    mma_commit(&empty[s]);
+                    --ready;
                 }
                 if (!ok) break;
-                mma_commit(&acc_full[b]);
+                {
+                    const uint32_t pos = us + (uint32_t)nitems;
+                    uph ^= (pos / NST) & 1u;
+                    us = pos % NST;
+                }
+                mma_commit(&acc_full[b]);     // both warps commit: the unit is done when both partial sums are
             }
             if (!ok) {
                 s_abort = 1;
                 flag(e.status, PMG_ERR_TIMEOUT);
                 if (issued) {
-                    mma_commit(drain);
+                    mma_commit(&drain[mw]);
                     const uint64_t t0 = global_ns();
-                    while (!mbar_try_wait_sleep(drain, 0, 4000) && global_ns() - t0 < kWaitNs) {
+                    while (!mbar_try_wait_sleep(&drain[mw], 0, 4000) && global_ns() - t0 < kWaitNs) {
                     }
                 }
             }
@@ -388,31 +417,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
     } else {
         // ============================================ epilogue ============================================ //
-        const int q = warp & 3;                         // TMEM lane quarter this warp may access
-        uint32_t t = 0;
+        // Two warps per TMEM lane quarter (warp & 3), each on half of the unit's NT columns; units in order.  The
+        // accumulator is the sum of the two MMA warps' partials (the second is empty when the unit has one item).
+        const int q = warp & 3;
+        constexpr int CH = NT / 32;                     // 16-column chunks per epilogue warp
+        const int j0 = ((warp - kEpi0) >> 2) * CH;
+        uint32_t k = 0;
         bool ok = true;
-        int64_t xm0 = 0;
-        int xmc = 0;
-        uint32_t xmk;
-        if ((int64_t)blockIdx.x < nunits) tile_of(blockIdx.x / nblk, xm0, xmc, xmk);
-        for (int64_t u = blockIdx.x; u < nunits && ok; u += gridDim.x, ++t) {
-            const int64_t m0 = xm0;
-            const int mc = xmc, n0 = (int)(u % nblk) * NT;
-            if (u + gridDim.x < nunits) tile_of((u + gridDim.x) / nblk, xm0, xmc, xmk);
-            const uint32_t b = t & 1u;
-            if (!mbar_wait(&acc_full[b], (t >> 1) & 1u, &s_abort)) { ok = false; break; }
+        for (int64_t u = blockIdx.x; u < nunits && ok; u += gridDim.x, ++k) {
+            int64_t m0;
+            int mc;
+            uint32_t mk;
+            tile_of(u / nblk, m0, mc, mk);
+            const bool two = ((__popc(mk) + tpi - 1) / tpi) * nkb > 1;
+            const int n0 = (int)(u % nblk) * NT;
+            const uint32_t b = k & 1u;
+            if (!mbar_wait(&acc_full[b], (k >> 1) & 1u, &s_abort)) { ok = false; break; }
             tc_fence_after();
             const int rr = 32 * q + lane;
             const bool live = rr < mc;
-            const float* rrow = (e.mode == PMG_EPI_F32_RESID && live) ? e.resid + (m0 + rr) * Co + n0 : nullptr;
+            const float* rrow =
+                (e.mode == PMG_EPI_F32_RESID && live) ? e.resid + (m0 + rr) * Co + n0 + j0 * 16 : nullptr;
             float4 rcur[4], rnext[4];
             if (rrow) load_resid16(rrow, rcur);
+            const uint32_t t0 = tmem + 2 * b * NCOLS + ((uint32_t)(32 * q) << 16);
 #pragma unroll 1
-            for (int j = 0; j < NT / 16; ++j) {
+            for (int jj = 0; jj < CH; ++jj) {
+                const int j = j0 + jj;
                 // the next chunk's residual loads are in flight while this chunk is read from TMEM and stored
-                if (rrow && j + 1 < NT / 16) load_resid16(rrow + (j + 1) * 16, rnext);
+                if (rrow && jj + 1 < CH) load_resid16(rrow + (jj + 1) * 16, rnext);
                 uint32_t acc[16];
-                tmem_ld16(tmem + b * NCOLS + ((uint32_t)(32 * q) << 16) + (uint32_t)(j * 16), acc);
+                tmem_ld16(t0 + (uint32_t)(j * 16), acc);
+                if (two) {
+                    uint32_t acc1[16];
+                    tmem_ld16(t0 + NCOLS + (uint32_t)(j * 16), acc1);
+#pragma unroll
+                    for (int t = 0; t < 16; ++t) acc[t] += acc1[t];
+                }
                 if (live) epi_store16(e, s_ws, s_bias, m0 + rr, n0 + j * 16, Co, acc, rcur);
 #pragma unroll
                 for (int t4 = 0; t4 < 4; ++t4) rcur[t4] = rnext[t4];
@@ -430,7 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (warp == 4) {
         tc_fence_after();
-        tmem_dealloc(tmem, 2 * NCOLS);
+        tmem_dealloc(tmem, 4 * NCOLS);
     }
 }
 
