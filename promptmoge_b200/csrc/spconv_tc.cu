@@ -35,11 +35,14 @@ namespace pmg {
 
 namespace tc {
 
-constexpr int kProducers = 128;                   // warps 0-3
-constexpr int kMmaWarps = 2;                      // warps 4-5
-constexpr int kEpiWarps = 8;                      // warps 6-13
-constexpr int kEpi0 = 4 + kMmaWarps;              // first epilogue warp
-constexpr int kThreads = 32 * (4 + kMmaWarps + kEpiWarps);
+constexpr int kProdWarps = 8;                     // warps 0-7
+constexpr int kProducers = 32 * kProdWarps;
+constexpr int kMmaWarps = 2;                      // warps 8-9
+constexpr int kMma0 = kProdWarps;                 // first MMA warp
+constexpr int kEpiWarps = 8;                      // warps 10-17
+constexpr int kEpi0 = kMma0 + kMmaWarps;          // first epilogue warp
+constexpr int kThreads = 32 * (kProdWarps + kMmaWarps + kEpiWarps);
+constexpr int kRowsPerWarp = 128 / kProdWarps;    // tile rows a producer warp copies
 constexpr int kItemK = 128;
 constexpr int kBudget = 196 * 1024;               // shared memory for resident weights + ring
 constexpr int kResMax = 110592;                   // 27-tap weights kept resident up to this size (64 x 64 x 27)
@@ -73,6 +76,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int TPI = W < kItemK ? kItemK / W : 1;  // most taps per item
     constexpr int CPR = W / 16;                      // 16-byte chunks of one tap row in an item
     constexpr int RPP = 32 / CPR;                    // rows a warp covers per pass
+    constexpr int NP = kRowsPerWarp / RPP;           // passes per producer warp and item
+    static_assert(NP >= 1 && NP * RPP == kRowsPerWarp, "producer row split");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* res = smem;                             // resident weights [27][NT][W] (RES)
@@ -85,7 +90,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* idx_full = acc_empty + 4;     // [2] indices of a tile landed
     uint64_t* rec_full = idx_full + 2;      // [2] record of a tile published
     uint64_t* rec_free = rec_full + 2;      // [2] record read by every producer
-    uint64_t* drain = rec_free + 2;         // [2] one per MMA warp
+    uint64_t* idx_free = rec_free + 2;      // [2] every producer is done with the indices of the buffer's last unit
+    uint64_t* drain = idx_free + 2;         // [2] one per MMA warp
     uint64_t* wres = drain + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(wres + 1);
     __shared__ volatile int s_abort;
@@ -109,6 +115,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&idx_full[b], kProducers + 1);
             mbar_init(&rec_full[b], 1);
             mbar_init(&rec_free[b], kProducers);
+            mbar_init(&idx_free[b], kProducers);
             mbar_init(&drain[b], 1);
         }
         mbar_init(wres, 1);
@@ -120,7 +127,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             s_ws[n] = e.ws[n];
             s_bias[n] = e.bias[n];
         }
-    if (warp == 4) tmem_alloc(tmem_slot, 4 * NCOLS);
+    if (warp == kMma0) tmem_alloc(tmem_slot, 4 * NCOLS);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -165,7 +172,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t ring_base = smem_u32(ring);
     const uint32_t res_base = smem_u32(res);
 
-    if (warp < 4) {
+    if (warp < kProdWarps) {
         // =========================================== producers =========================================== //
         uint32_t it = 0;
         bool ok = true;
@@ -197,9 +204,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             // every producer then copies its row's neighbour indices of the unit's taps into idx[k & 1] with 4-byte
             // cp.async (idx_full tracks their completion).  Both happen one unit ahead, after the first item of the
             // previous unit.
-            const int r = threadIdx.x;
+            const int r = threadIdx.x & (kM - 1), r_half = threadIdx.x / kM;   // index copies: row, tap parity
             const int my_c = lane % CPR, my_sub = lane / CPR;
-            const int my_row = 32 * warp + my_sub;                 // first row this lane copies (then + p * RPP)
+            const int my_row = kRowsPerWarp * warp + my_sub;       // first row this lane copies (then + p * RPP)
             // this lane's part of every copy: row group / row-in-group / 16-byte K chunk offsets in a stage
             const int8_t* in_lane = in + my_c * 16;
             const uint32_t rows32 = (uint32_t)in_rows;             // in_rows < 2^31 and in_rows * Ci < 2^32
@@ -215,21 +222,40 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive(&rec_full[b]);
                 return true;
             };
+            // Neighbour indices of a full tile are fetched with one 512-byte bulk copy per present tap (TMA, tracked
+            // by bytes on idx_full): keeping them out of the producers' cp.async groups matters because a stage's
+            // arrival waits for ALL earlier cp.async of the thread, and index rows come from HBM.  A partial tile or a
+            // neighbour map whose rows are not 16-byte aligned takes 4-byte cp.async per (row, tap) instead.
+            const bool ids_bulk_ok = (ld & 3) == 0 && (reinterpret_cast<uintptr_t>(nmap) & 15) == 0;
             auto issue_ids = [&](uint32_t k) -> bool {               // every producer
                 const uint32_t b = k & 1u;
                 if (!mbar_wait(&rec_full[b], (k >> 1) & 1u, &s_abort)) return false;
                 const int4 a = s_rec[b];
-                __syncwarp();        // the warp's lanes are done reading idx[b] (their rows) of unit k - 2
-                if (r < a.y) {
-                    const uint32_t mk = (uint32_t)a.z;
-                    const int32_t* src = nmap + a.x + r;
+                // idx[b] still holds unit k - 2's indices: every producer must be done with them (rows are written by
+                // other warps than the ones reading them)
+                if (k >= 2 && !mbar_wait(&idx_free[b], ((k - 2) >> 1) & 1u, &s_abort)) return false;
+                __syncwarp();
+                const uint32_t mk = (uint32_t)a.z;
+                if (ids_bulk_ok && a.y == kM) {
+                    if (warp == 0) {
+                        if (lane == 0) mbar_arrive_expect_tx(&idx_full[b], (uint32_t)__popc(mk) * kM * 4u);
+                        __syncwarp();
+                        if (lane < 27 && ((mk >> lane) & 1u))
+                            bulk_g2s(idx_base + (uint32_t)(((int)b * 27 + lane) * kM) * 4u,
+                                     nmap + (int64_t)lane * ld + a.x, kM * 4u, &idx_full[b]);
+                    }
+                    mbar_arrive(&idx_full[b]);
+                } else {
+                    if (r < a.y) {
+                        const int32_t* src = nmap + a.x + r;
 #pragma unroll
-                    for (int v = 0; v < 27; ++v)
-                        if ((mk >> v) & 1u)
-                            cp_async4(idx_base + (uint32_t)(((int)b * 27 + v) * kM + r) * 4u, src + (int64_t)v * ld);
+                        for (int v = 0; v < 27; ++v)
+                            if (((mk >> v) & 1u) && (v % (kProducers / kM)) == r_half)
+                                cp_async4(idx_base + (uint32_t)(((int)b * 27 + v) * kM + r) * 4u, src + (int64_t)v * ld);
+                    }
+                    cp_async_mbar_arrive(&idx_full[b]);
+                    if (threadIdx.x == 0) mbar_arrive(&idx_full[b]);
                 }
-                cp_async_mbar_arrive(&idx_full[b]);
-                if (threadIdx.x == 0) mbar_arrive(&idx_full[b]);
                 return true;
             };
 
@@ -252,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t cidx_base = idx_base + (uint32_t)(cb * 27 * kM + my_row) * 4u;
                 uint32_t row_live = 0;                      // bit p: row my_row + p * RPP is inside the tile
 #pragma unroll
-                for (int p = 0; p < CPR; ++p) row_live |= (my_row + p * RPP < mc ? 1u : 0u) << p;
+                for (int p = 0; p < NP; ++p) row_live |= (my_row + p * RPP < mc ? 1u : 0u) << p;
                 bool prefetched = false;
                 uint32_t mk = (uint32_t)ra.z;
                 while (mk && ok) {
@@ -273,12 +299,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         // copies' asm is a compiler memory barrier, so interleaving them would serialise the loads.
                         // Row r of pass p is my_row + p * RPP; an index is valid when 0 <= id < in_rows (one unsigned
                         // compare) and its row is inside the tile.
-                        uint32_t id[TPI][CPR];
+                        uint32_t id[TPI][NP];
 #pragma unroll
                         for (int g = 0; g < TPI; ++g) {
                             const uint32_t ia = cidx_base + (uint32_t)(tv[g] * kM) * 4u;
 #pragma unroll
-                            for (int p = 0; p < CPR; ++p) {
+                            for (int p = 0; p < NP; ++p) {
                                 const bool use = g < nt && ((row_live >> p) & 1u);
                                 id[g][p] = use ? (uint32_t)ld_shared_s32(ia + (uint32_t)(p * RPP) * 4u) : 0xFFFFFFFFu;
                             }
@@ -288,7 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int g = 0; g < TPI; ++g) {
                             if (g >= nt) break;
 #pragma unroll
-                            for (int p = 0; p < CPR; ++p) {
+                            for (int p = 0; p < NP; ++p) {
                                 const bool valid = id[g][p] < rows32;
                                 // row r = my_row + p * RPP of the item, 16-byte chunk c = g * CPR + my_c of its
                                 // 128-byte K row, in the 128-byte-swizzled K-major layout: rows 128 bytes apart,
@@ -313,6 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                 }
+                mbar_arrive(&idx_free[cb]);        // done with this unit's indices
                 ok = __all_sync(0xffffffffu, ok);
             }
             cp_async_wait_all();
@@ -329,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // after MMAs costs a few hundred cycles).  A parity wait is only sound when the stage's previous phase has
         // completed: a warp's previous item is at most 3 positions back (across a unit boundary), so single waits need
         // >= 3 stages and the batched wait on item i + 2 needs >= 5.
-        const int mw = warp - 4;
+        const int mw = warp - kMma0;
         if (lane == 0) {
             // A lean loop: descriptors are precomputed and advanced in descriptor address units (16 bytes).
             constexpr bool BATCH = NST >= 5;
@@ -469,7 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 4) {
+    if (warp == kMma0) {
         tc_fence_after();
         tmem_dealloc(tmem, 4 * NCOLS);
     }
