@@ -165,7 +165,10 @@ def dominant_conv(torch, eng, reps: int = 20):
             return float(np.median(tms))
         t = timed(run)
         ops_ = 2.0 * nnz * C_ * C_
-        byts = M * C_ + M * C_ + 27 * 4 * M + 27 * C_ * C_
+        if k == 0 and bool(eng.tensor_cores) and ops.grid0_supported(C_, C_):
+            byts = M * C_ + M * C_ + 27 * M // 8 + 27 * C_ * C_      # tap masks (3.4 B/row) instead of the map
+        else:
+            byts = M * C_ + M * C_ + 27 * 4 * M + 27 * C_ * C_
         # this level's convs per step: 2 down + 2 up (4 at L<L-1), 2 down + 2 bottleneck at the last level
         res.append(dict(level=k, M=M, C=C_, ms=t, ops=ops_, bytes=byts, per_step=4 * t))
     return res
@@ -361,14 +364,20 @@ def profile_conv(args):
     q = torch.randint(-127, 127, (M, C_), dtype=torch.int8, device="cuda", generator=g)
     w = torch.randint(-127, 127, (27, C_, C_), dtype=torch.int8, device="cuda", generator=g)
     tc_path = ops.tc_supported(C_, C_) and not args.simt
+    grid0 = k == 0 and not args.simt and ops.grid0_supported(C_, C_)
     ws_ = torch.full((C_,), 1e-3, device="cuda")
     b = torch.zeros(C_, device="cuda")
+    lanes = ops.l0_tap_lanes(l["z"], 1, 480, 640) if grid0 else None
     for _ in range(max(1, args.steps)):
-        ops.spconv_i8(q, l["nmap_tm"], l["mask"], w, ws_, b, 0.01, ops.EPI_SILU_Q8, 0.02, rows=M,
-                      tensor_cores=tc_path)
+        if grid0:   # level 0 runs the neighbour-map-free frame-grid kernel in the plan
+            ops.spconv_i8_grid0(q, lanes, 1, 480, 640, w, ws_, b, 0.01, ops.EPI_SILU_Q8, 0.02)
+        else:
+            ops.spconv_i8(q, l["nmap_tm"], l["mask"], w, ws_, b, 0.01, ops.EPI_SILU_Q8, 0.02, rows=M,
+                          tensor_cores=tc_path)
     torch.cuda.synchronize()
     nnz = int((l["nmap_tm"][:, :M] >= 0).sum().item())
-    return {"profile_conv": k, "M": M, "C": C_, "occupied_taps": nnz, "path": "tcgen05" if tc_path else "simt"}
+    return {"profile_conv": k, "M": M, "C": C_, "occupied_taps": nnz,
+            "path": "tcgen05 frame grid" if grid0 else ("tcgen05" if tc_path else "simt")}
 
 
 def conv_sweep(args):
