@@ -52,6 +52,28 @@ __device__ __forceinline__ int quant8(float x, float s) {
 // SiLU as x / (1 + exp(-x)) in fp32.
 __device__ __forceinline__ float silu(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
 
+// quant8(silu(x), s) for inv_s = 1 / s (IEEE), identical for every x.  The estimate t = fl(fl(x * rcp(d)) * inv_s),
+// d = 1 + exp(-x) formed exactly as silu() forms it and rcp with relative error <= 2^-22, differs from the exact
+// chain's quotient fl(fl(x / d) / s) by at most (2^-22 + 5 * 2^-24) |quotient| < 8.7e-5 for |quotient| < 160; when
+// t is more than 2^-12 from every half-integer both round to the same integer, and |t| >= 160 clamps either way.
+// Otherwise (about 5e-4 of values) the exact chain runs.  NaN takes the exact chain.  Used where the requantise is
+// issue-bound (the row kernels): one reciprocal estimate instead of two IEEE divides per value.
+__device__ __forceinline__ float rcp_approx(float x) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+__device__ __forceinline__ int silu_quant8_fast(float x, float s, float inv_s) {
+    const float d = __fadd_rn(1.0f, expf(-x));
+    const float t = __fmul_rn(__fmul_rn(x, rcp_approx(d)), inv_s);
+    const float a = fabsf(t);
+    const float f = a - truncf(a);
+    const bool sure = a >= 160.0f || fabsf(f - 0.5f) > (1.0f / 4096.0f);
+    if (__builtin_expect(sure, 1)) return static_cast<int>(fminf(fmaxf(rintf(t), -127.0f), 127.0f));
+    return quant8(__fdiv_rn(x, d), s);
+}
+
 // (acc * s_a) * s_w + b with round-to-nearest at every step (no contraction into FMA).
 __device__ __forceinline__ float dequant(int acc, float sa, float sw, float b) {
     return __fadd_rn(__fmul_rn(__fmul_rn(__int2float_rn(acc), sa), sw), b);

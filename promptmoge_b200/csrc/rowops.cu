@@ -249,6 +249,7 @@ __global__ void __launch_bounds__(256) k_ln_silu_rows(const float* __restrict__ 
                                                       const float* __restrict__ gamma, const float* __restrict__ beta,
                                                       double eps, float scale, int8_t* __restrict__ q) {
     constexpr int G = RowMap<C>::G, RPB = RowMap<C>::RPB;
+    const float inv_s = 1.0f / scale;
     __shared__ float sg[C], sb[C];
     for (int i = threadIdx.x; i < C; i += blockDim.x) {
         sg[i] = gamma[i];
@@ -295,7 +296,7 @@ __global__ void __launch_bounds__(256) k_ln_silu_rows(const float* __restrict__ 
         for (int k = 0; k < 8; ++k) {
             const int c = chan8<C>(sub, k);
             const float y = __fadd_rn(__fmul_rn(__fadd_rn(__fmul_rn(v[k], rstd), shift), sg[c]), sb[c]);
-            qv[k] = quant8(silu(y), scale);
+            qv[k] = silu_quant8_fast(y, scale, inv_s);
         }
         store8_q8<C>(q + m * C, sub, qv);
     }

@@ -65,3 +65,23 @@ def test_pool_mean_q8_exact(C):
     got = ops.pool_mean(torch.from_numpy(x).cuda(), torch.from_numpy(idx).cuda(), torch.from_numpy(off).cuda(),
                         M_out, scale=float(s)).cpu().numpy()
     np.testing.assert_array_equal(got, want)
+
+
+@pytest.mark.parametrize("C", [32, 64, 128, 256])
+def test_layernorm_silu_fast_requantise_equals_exact(C):
+    """The row-parallel LayerNorm + SiLU + requantise kernel uses the reciprocal-estimate quantiser; the warp-per-row
+    kernel (taken when a row pointer is not 16-byte aligned) uses the exact IEEE chain.  Same bits on the same rows."""
+    from promptmoge_b200 import ops
+    rng = np.random.default_rng(C)
+    M = 20000
+    base = torch.from_numpy((rng.standard_normal(M * C + 1) * 3).astype(np.float32)).cuda()
+    gamma = torch.from_numpy(rng.uniform(0.5, 2.0, C).astype(np.float32)).cuda()
+    beta = torch.from_numpy((rng.standard_normal(C) * 0.3).astype(np.float32)).cuda()
+    x_aligned = base[:M * C].clone().view(M, C)                    # 16-byte aligned: row-parallel kernel
+    x_odd = base[1:].view(M, C)                                     # 4-byte offset: warp-per-row kernel
+    x_odd.copy_(x_aligned)
+    for scale in (0.021, 0.0371, 0.11):
+        q_fast = ops.ln_silu_q8(x_aligned, gamma, beta, scale)
+        q_exact = ops.ln_silu_q8(x_odd, gamma, beta, scale)
+        torch.cuda.synchronize()
+        assert torch.equal(q_fast, q_exact), scale
