@@ -43,6 +43,7 @@ constexpr int kEpiWarps = 8;                      // warps 10-17
 constexpr int kEpi0 = kMma0 + kMmaWarps;          // first epilogue warp
 constexpr int kThreads = 32 * (kProdWarps + kMmaWarps + kEpiWarps);
 constexpr int kRowsPerWarp = 128 / kProdWarps;    // tile rows a producer warp copies
+constexpr int kRecs = 8;                          // unit records in flight (gather convs)
 constexpr int kItemK = 128;
 constexpr int kBudget = 196 * 1024;               // shared memory for resident weights + ring
 constexpr int kResMax = 110592;                   // 27-tap weights kept resident up to this size (64 x 64 x 27)
@@ -88,15 +89,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* acc_full = empty + NST;       // [4] (two used) accumulator buffer k & 1 of unit k: both warps' partials
     uint64_t* acc_empty = acc_full + 4;     // [4]
     uint64_t* idx_full = acc_empty + 4;     // [2] indices of a tile landed
-    uint64_t* rec_full = idx_full + 2;      // [2] record of a tile published
-    uint64_t* rec_free = rec_full + 2;      // [2] record read by every producer
-    uint64_t* idx_free = rec_free + 2;      // [2] every producer is done with the indices of the buffer's last unit
+    uint64_t* rec_full = idx_full + 2;      // [kRecs] record of a unit published
+    uint64_t* rec_free = rec_full + kRecs;  // [kRecs] record read by every epilogue warp (its last reader)
+    uint64_t* idx_free = rec_free + kRecs;  // [2] every producer is done with the indices of the buffer's last unit
     uint64_t* drain = idx_free + 2;         // [2] one per MMA warp
     uint64_t* wres = drain + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(wres + 1);
     __shared__ volatile int s_abort;
     __shared__ float s_ws[256], s_bias[256];           // epilogue per-channel weight scale and bias
-    __shared__ int4 s_rec[2];                          // producers: {m0, rows, tap mask} of the current / next unit
+    __shared__ int4 s_rec[kRecs];                      // {m0, rows, tap mask, items} of units k .. k + kRecs - 1
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -113,10 +114,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&idx_full[b], kProducers + 1);
-            mbar_init(&rec_full[b], 1);
-            mbar_init(&rec_free[b], kProducers);
             mbar_init(&idx_free[b], kProducers);
             mbar_init(&drain[b], 1);
+        }
+        for (int j = 0; j < kRecs; ++j) {
+            mbar_init(&rec_full[j], 1);
+            mbar_init(&rec_free[j], kEpiWarps);
         }
         mbar_init(wres, 1);
         s_abort = 0;
@@ -154,6 +157,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             mk &= 0x7ffffffu;
         }
         if (!mk) mk = 1u;       // an all-absent tile still runs one (zero) item so its accumulator is defined
+    };
+    // The same record in two halves, so the mask loads can be issued a unit before their words are used: the loads of
+    // the (at most 4) 32-row groups of tile t, then their OR.
+    auto mask_words = [&](int64_t t, uint32_t (&w)[4]) {
+        const int64_t m0 = t * kM;
+        const int mc = (int)min((int64_t)kM, M - m0);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) w[i] = (tile_mask && i * 32 < mc) ? tile_mask[(m0 >> 5) + i] : 0u;
+    };
+    auto record_of = [&](int64_t t, const uint32_t (&w)[4]) -> int4 {
+        const int64_t m0 = t * kM;
+        const int mc = (int)min((int64_t)kM, M - m0);
+        uint32_t mk = tile_mask ? ((w[0] | w[1] | w[2] | w[3]) & 0x7ffffffu) : 0x7ffffffu;
+        if (!mk) mk = 1u;
+        const int items = ((__popc(mk) + tpi - 1) / tpi) * nkb;
+        return make_int4((int)m0, mc, (int)mk, items);
     };
     // Next <= tpi taps of the unit's tap mask.  Fully unrolled so tv stays in registers (a dynamically indexed array
     // would live in local memory, and with most of the SM's unified L1 carved out as shared memory every access
@@ -211,16 +230,35 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int8_t* in_lane = in + my_c * 16;
             const uint32_t rows32 = (uint32_t)in_rows;             // in_rows < 2^31 and in_rows * Ci < 2^32
             const uint32_t idx_base = smem_u32(idx);
-            auto publish = [&](int64_t u, uint32_t k) -> bool {      // thread 0
-                const uint32_t b = k & 1u, use = k >> 1;
-                int64_t m0;
-                int mc;
-                uint32_t mk;
-                tile_of(u / nblk, m0, mc, mk);
-                if (use >= 1 && !mbar_wait(&rec_free[b], (use - 1) & 1u, &s_abort)) return false;
-                s_rec[b] = make_int4((int)m0, mc, (int)mk, 0);
-                mbar_arrive(&rec_full[b]);
+            // Thread 0 publishes unit records kRecs deep: record j (this CTA's j-th unit) goes to s_rec[j % kRecs] once
+            // every epilogue warp has read record j - kRecs.  Unit j's mask words are loaded two units before they
+            // are reduced, so no thread on the data path waits on a global load for a record.
+            uint32_t pf_w[4] = {0u, 0u, 0u, 0u};                     // mask words of unit `pf_j` in flight
+            uint32_t pf_j = 0xFFFFFFFFu;                               // none prefetched yet
+            auto publish_one = [&](uint32_t j, const int4& rec) -> bool {   // thread 0
+                const uint32_t slot = j % kRecs;
+                if (j >= kRecs && !mbar_wait(&rec_free[slot], ((j / kRecs) - 1) & 1u, &s_abort)) return false;
+                s_rec[slot] = rec;
+                mbar_arrive(&rec_full[slot]);
                 return true;
+            };
+            auto unit_tile = [&](uint32_t j) -> int64_t { return ((int64_t)blockIdx.x + (int64_t)j * gridDim.x) / nblk; };
+            auto unit_exists = [&](uint32_t j) -> bool { return (int64_t)blockIdx.x + (int64_t)j * gridDim.x < nunits; };
+            // publish unit j from the prefetched words (loaded earlier), then start the loads for unit j + 1
+            auto publish = [&](uint32_t j) -> bool {                 // thread 0; units in order
+                if (!unit_exists(j)) return true;
+                uint32_t w[4];
+                if (pf_j == j) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) w[i] = pf_w[i];
+                } else {
+                    mask_words(unit_tile(j), w);
+                }
+                if (unit_exists(j + 1)) {
+                    mask_words(unit_tile(j + 1), pf_w);
+                    pf_j = j + 1;
+                }
+                return publish_one(j, record_of(unit_tile(j), w));
             };
             // Neighbour indices of a full tile are fetched with one 512-byte bulk copy per present tap (TMA, tracked
             // by bytes on idx_full): keeping them out of the producers' cp.async groups matters because a stage's
@@ -229,8 +267,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool ids_bulk_ok = (ld & 3) == 0 && (reinterpret_cast<uintptr_t>(nmap) & 15) == 0;
             auto issue_ids = [&](uint32_t k) -> bool {               // every producer
                 const uint32_t b = k & 1u;
-                if (!mbar_wait(&rec_full[b], (k >> 1) & 1u, &s_abort)) return false;
-                const int4 a = s_rec[b];
+                if (!mbar_wait(&rec_full[k % kRecs], (k / kRecs) & 1u, &s_abort)) return false;
+                const int4 a = s_rec[k % kRecs];
                 // idx[b] still holds unit k - 2's indices: every producer must be done with them (rows are written by
                 // other warps than the ones reading them)
                 if (k >= 2 && !mbar_wait(&idx_free[b], ((k - 2) >> 1) & 1u, &s_abort)) return false;
@@ -262,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             int64_t u = blockIdx.x;
             uint32_t k = 0;
             if (u < nunits) {
-                if (threadIdx.x == 0) ok = publish(u, 0);
+                if (threadIdx.x == 0) ok = publish(0) && publish(1) && publish(2);
                 ok = __all_sync(0xffffffffu, ok);
                 ok = ok && issue_ids(0);
             }
@@ -271,8 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t cb = k & 1u;
                 ok = __all_sync(0xffffffffu, mbar_wait(&idx_full[cb], (k >> 1) & 1u, &s_abort));
                 if (!ok) break;
-                const int4 ra = s_rec[cb];
-                mbar_arrive(&rec_free[cb]);
+                const int4 ra = s_rec[k % kRecs];       // published (issue_ids(k) waited for it)
                 const int mc = ra.y;
                 const int n0 = (int)(u % nblk) * NT;
                 const uint32_t cidx_base = idx_base + (uint32_t)(cb * 27 * kM + my_row) * 4u;
@@ -332,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             // after the first item: publish the next unit and start its index copies
                             prefetched = true;
                             if (has_next) {
-                                if (threadIdx.x == 0) ok = publish(u + gridDim.x, k + 1);
+                                if (threadIdx.x == 0) ok = publish(k + 3);
                                 ok = __all_sync(0xffffffffu, ok);
                                 ok = ok && issue_ids(k + 1);
                             }
@@ -374,7 +411,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 int64_t m0;
                 int mc;
                 uint32_t mk;
-                tile_of(u / nblk, m0, mc, mk);
+                if (KIND == GATHER) {
+                    // the unit's record from the producers' ring (no global loads on this thread's path)
+                    if (!mbar_wait(&rec_full[k % kRecs], (k / kRecs) & 1u, &s_abort)) { ok = false; break; }
+                    const int4 rec = s_rec[k % kRecs];
+                    m0 = rec.x;
+                    mc = rec.y;
+                    mk = (uint32_t)rec.z;
+                } else {
+                    tile_of(u / nblk, m0, mc, mk);
+                }
                 const int nitems = ((__popc(mk) + tpi - 1) / tpi) * nkb;
                 const uint32_t b = k & 1u;
                 if (!mbar_wait(&acc_empty[b], ((k >> 1) & 1u) ^ 1u, &s_abort)) { ok = false; break; }
@@ -455,7 +501,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             int64_t m0;
             int mc;
             uint32_t mk;
-            tile_of(u / nblk, m0, mc, mk);
+            if (KIND == GATHER) {
+                if (!mbar_wait(&rec_full[k % kRecs], (k / kRecs) & 1u, &s_abort)) { ok = false; break; }
+                const int4 rec = s_rec[k % kRecs];
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&rec_free[k % kRecs]);    // every epilogue warp has read it: reusable
+                m0 = rec.x;
+                mc = rec.y;
+                mk = (uint32_t)rec.z;
+            } else {
+                tile_of(u / nblk, m0, mc, mk);
+            }
             const bool two = ((__popc(mk) + tpi - 1) / tpi) * nkb > 1;
             const int n0 = (int)(u % nblk) * NT;
             const uint32_t b = k & 1u;
