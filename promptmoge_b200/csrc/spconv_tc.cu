@@ -3,29 +3,29 @@
 // One persistent CTA per SM walks work units = (128-row output tile, N block of NT <= 128 output channels).  A unit's
 // reduction is a stream of items through an NST-stage shared-memory ring; an item is K = 128 bytes: 128 / Ci taps of
 // a narrow conv (4 taps at Ci = 32, 2 at Ci = 64), or one 128-byte K-block of a wide layer.  Warp roles:
-//   warps 0-3   producers:
+//   warps 0-7   producers:
 //     DENSE   (dense layers) thread 0 issues a 2-D TMA tile load of the 128 A rows (swizzled) and of the weights;
-//     GATHER  (convs) per item the warps gather the tap rows' 16-byte chunks with cp.async, lanes spread along K
-//             (absent neighbours zero-filled by the copy); each thread's copies arrive on the stage's mbarrier
-//             asynchronously (cp.async.mbarrier.arrive.noinc), so producers never block on their own copies and
-//             the whole ring can be in flight; the MMA thread fences the proxies after its wait.  The
-//             neighbour indices of the next tile are copied into shared memory (4-byte cp.async per row and tap,
-//             completion tracked by an mbarrier) while the current tile's items run, and thread 0 publishes each
-//             tile's record (rows, tap mask) through shared memory, so no producer waits on a dependent global
-//             load between tiles and no index is held in registers.
-//   warp 4      owns two TMEM accumulators (128 lanes x NT int32 columns); lane 0 issues
-//               tcgen05.mma.cta_group::1.kind::i8 (K = 32 bytes per instruction) and tcgen05.commit to release stages
-//               and to publish a finished accumulator.
-//   warps 5-8   epilogue, one warp per TMEM lane quarter: tcgen05.ld 32x32b.x16, then dequant -> +bias -> [SiLU ->
-//               requantise] or [+residual] with the reference's rounding, while the next unit accumulates into the
-//               other buffer.  (Nine warps leave each thread up to 168 registers; a thirteenth warp on an SM
-//               sub-partition would cap them at 128.)
+//     GATHER  (convs) per item each warp gathers 16 tile rows' 16-byte chunks with cp.async (absent neighbours
+//             zero-filled by the copy) into the 128-byte-swizzled K-major layout; each thread's copies arrive on the
+//             stage's mbarrier asynchronously (cp.async.mbarrier.arrive.noinc), so producers never block on their
+//             own copies and the whole ring can be in flight; the MMA threads fence the proxies after their wait.
+//             The neighbour indices of the next tile are copied into a double-buffered shared table while the
+//             current tile's items run (one 512-byte bulk copy per present tap of a full tile, else 4-byte cp.async
+//             per row and tap), so no producer waits on a dependent global load between tiles.
+//   thread 0    also publishes unit records {first row, rows, tap mask, items} three units ahead into an 8-deep ring
+//               (tap masks prefetched from the per-tile mask array), read by producers, MMA and epilogue warps.
+//   warps 8-9   MMA issue: each owns one partial accumulator per TMEM buffer (two buffers, 128 lanes x NT int32
+//               columns each) and issues alternate items of every unit (tcgen05.mma.cta_group::1.kind::i8, K = 32
+//               bytes per instruction), tcgen05.commit releasing stages and publishing its finished partial.  Two
+//               issuing threads halve the per-item issue latency that bounds a single thread.
+//   warps 10-17 epilogue, two warps per TMEM lane quarter (each half of the columns): tcgen05.ld 32x32b.x16 of both
+//               partials (exact int32 sum), then dequant -> +bias -> [SiLU -> requantise] or [+residual] with the
+//               reference's rounding, while the next unit accumulates into the other buffer.
 // Weights arrive by 2-D TMA tile loads from the plain tap-major [taps][Co][Ci] tensor (swizzle matching the row
-// width W = min(Ci, 128)); a conv whose whole 27-tap weight fits (Co = NT, Ci < 128) keeps it resident in shared
-// memory for the kernel's lifetime.  Gathered A operands use the K-major no-swizzle core-matrix layout with the 8-row
-// groups outermost ([16 row groups][8 K chunks][8 rows][16 bytes]), so a warp's 16-byte writes hit distinct banks.
-// Every TMA copy lands in this CTA's own shared memory.  Every wait is bounded: on timeout the CTA records
-// PMG_ERR_TIMEOUT in the status word, lets issued MMAs retire, frees its TMEM and returns.
+// width W = min(Ci, 128)); a conv whose whole 27-tap weight fits (Co = NT, Ci <= 64) keeps it resident in shared
+// memory for the kernel's lifetime.  Every TMA copy lands in this CTA's own shared memory (no multicast).  Every wait
+// is bounded: on timeout the CTA records PMG_ERR_TIMEOUT in the status word, lets issued MMAs retire, frees its TMEM
+// and returns.
 #include <algorithm>
 #include <mutex>
 
