@@ -298,6 +298,7 @@ def run_ours(args, ws, rank, local):
         cpu = None
         if ws == 1 and not args.no_cpu_baseline and args.model == "A":
             cpu = cpu_baseline(batch=1, steps=1)
+        prep = prompt_prep(torch, sc, dev, cpu=ws == 1 and not args.no_cpu_baseline)
         line = {
             "metric": METRIC if args.model == "A" else METRIC_B, "value": round(value, 3), "unit": UNIT, "n_gpus": ws,
             "steps": args.steps,
@@ -320,9 +321,55 @@ def run_ours(args, ws, rank, local):
             "roofline": roof,
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
+            "prompt_prep": prep,
         }
     ref.close()
     return line
+
+
+def prompt_prep(torch, sc, dev, cpu: bool, reps: int = 50):
+    """The per-frame LiDAR prompt preparation in front of the refiner (promptmoge.infer: nearest_fill of the
+    192x256 sensor frame, then build_prompt onto the 420x560 token grid of 1200 tokens): device time of the two
+    kernels pairs (CUDA events, mean of `reps`), and the CPU time of the same work through scipy's exact distance
+    transform (the reference's call) plus the numpy prompt oracle."""
+    from promptmoge_b200 import ops
+    ld = torch.from_numpy(sc.lidar_depth).to(dev)
+    lc = torch.from_numpy(sc.lidar_conf).to(dev)
+    fd, fc = torch.empty_like(ld), torch.empty_like(lc)
+    for _ in range(3):
+        ops.nearest_fill(ld, lc, out=(fd, fc))
+        ops.build_prompt(fd, fc, (420, 560))
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    ev[0].record()
+    for _ in range(reps):
+        ops.nearest_fill(ld, lc, out=(fd, fc))
+    ev[1].record()
+    for _ in range(reps):
+        ops.build_prompt(fd, fc, (420, 560))
+    ev[2].record()
+    ev[2].synchronize()
+    out = {"frames": int(ld.shape[0]), "sensor_hw": list(ld.shape[-2:]), "token_grid_hw": [420, 560],
+           "nearest_fill_us": round(ev[0].elapsed_time(ev[1]) * 1e3 / reps, 2),
+           "build_prompt_us": round(ev[1].elapsed_time(ev[2]) * 1e3 / reps, 2)}
+    if cpu:
+        import numpy as np
+        from scipy import ndimage
+        from oracle import prompt as oprompt
+        d = sc.lidar_depth.reshape(-1, *sc.lidar_depth.shape[-2:])
+        c = sc.lidar_conf.reshape(-1, *sc.lidar_conf.shape[-2:])
+        t0 = time.perf_counter()
+        filled = []
+        for b in range(d.shape[0]):
+            valid = d[b] > 0
+            idx = ndimage.distance_transform_edt(~valid, return_distances=False, return_indices=True)
+            filled.append((d[b][tuple(idx)], np.where(valid, c[b], 1).astype(np.float32)))
+        t1 = time.perf_counter()
+        oprompt.build_prompt(np.stack([f[0] for f in filled])[:, None], np.stack([f[1] for f in filled])[:, None],
+                             (420, 560))
+        t2 = time.perf_counter()
+        out["cpu"] = {"nearest_fill_us": round((t1 - t0) * 1e6, 1), "build_prompt_us": round((t2 - t1) * 1e6, 1),
+                      "kind": "scipy distance_transform_edt (the reference's call) + numpy prompt oracle, 1 thread"}
+    return out
 
 
 def cpu_baseline(batch=1, steps=1):

@@ -197,6 +197,30 @@ int pmg_gauge_poly(const float* depth, const float* lidar, const float* conf, in
                    float* coef_out, void* workspace, size_t workspace_bytes, void* stream);
 
 /* --------------------------------------------------------------------------------------------------------------
+ * LiDAR prompt preparation
+ * ------------------------------------------------------------------------------------------------------------ */
+
+/* Workspace for pmg_nearest_fill and pmg_build_prompt over B frames of h x w sensor pixels. */
+size_t pmg_prompt_workspace_bytes(int32_t B, int32_t h, int32_t w);
+
+/* promptmoge.nearest_fill (promptmoge/model.py:61-72) per frame of depth / conf [B,h,w]: every missing pixel
+ * (depth <= 0 or NaN) takes the depth of its Euclidean-nearest present pixel (ties: smallest column, then smallest
+ * row, as scipy's exact distance transform returns) and confidence 1; present pixels are copied; a frame with no
+ * missing or no present pixel is copied unchanged.  Outputs must not alias the inputs.  h, w <= 32767,
+ * w <= 12288.  Replaces the reference's host-side scipy.ndimage.distance_transform_edt call. */
+int pmg_nearest_fill(const float* depth, const float* conf, int32_t B, int32_t h, int32_t w, float* depth_out,
+                     float* conf_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* build_prompt (moge/model/modules/prompt_stem.py:45-105), the 4-channel prompt: depth / conf [B,h,w] ->
+ * prompt [B,4,H,W] fp32 (nearest-resampled as torch's F.interpolate 'nearest') with channels
+ * clamp(log d - mu, -4, 4) * valid, valid, c * valid, 1 - c * (1 - clamp((d - 3) / 2, 0, 1)) (1 where invalid),
+ * valid = finite and > 0, c = clamp(conf / conf_levels, 0, 1); mu [B] = the lower median of log d over the
+ * confident pixels (c >= 0.999), else over all valid pixels, else 0 (prompt_stem.py:33-40, 66). */
+int pmg_build_prompt(const float* depth, const float* conf, int32_t B, int32_t h, int32_t w, int32_t H, int32_t W,
+                     float conf_levels, float* prompt, float* mu, void* workspace, size_t workspace_bytes,
+                     void* stream);
+
+/* --------------------------------------------------------------------------------------------------------------
  * Refiner glue
  * ------------------------------------------------------------------------------------------------------------ */
 

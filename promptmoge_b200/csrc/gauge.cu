@@ -14,12 +14,13 @@
 // with it to ~1e-6 relative.  A second kernel multiplies depth (and points) by exp(poly) over the image grid.
 #include <algorithm>
 
+#include "block.cuh"
 #include "common.cuh"
 
 namespace pmg {
 
 constexpr int kGaugeThreads = 512;   // 27 fp64 accumulators per thread need more than 64 registers
-constexpr int kGaugeBins = 2048;
+constexpr int kGaugeBins = kSelectBins;
 constexpr int kGaugeOut = 8;    // per frame: coef[6], ok, confident count
 
 // torch.linspace(-1, 1, n)[i] in fp32 (start + i * step below the midpoint, end - (n - 1 - i) * step above it)
@@ -58,75 +59,6 @@ struct GaugeArgs {
     float* out;          // [B][8]
 };
 
-template <typename T>
-__device__ __forceinline__ T block_sum(T v, T* sm) {
-    v = warp_sum(v);
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    __syncthreads();
-    if (lane == 0) sm[wid] = v;
-    __syncthreads();
-    T t = 0;
-    if (threadIdx.x == 0) {
-        for (int k = 0; k < (int)(blockDim.x >> 5); ++k) t += sm[k];
-        sm[0] = t;
-    }
-    __syncthreads();
-    t = sm[0];
-    __syncthreads();
-    return t;
-}
-
-// k-th smallest (1-based) of the values in rb[0, n) other than the 0xFFFFFFFF code, by value bits (all >= +0).
-__device__ uint32_t block_select(const uint32_t* rb, int n, uint32_t k, uint32_t* hist, int* scan_sm) {
-    __shared__ uint32_t s_digit, s_before;
-    uint32_t prefix = 0, remaining = k;
-    const int lane = threadIdx.x & 31;
-    const int n_pad = (n + blockDim.x - 1) / blockDim.x * blockDim.x;
-    for (int pass = 0; pass < 3; ++pass) {
-        const int shift = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
-        const int nbits = pass == 2 ? 10 : 11;
-        const int nb = 1 << nbits;
-        for (int i = threadIdx.x; i < kGaugeBins; i += blockDim.x) hist[i] = 0;
-        __syncthreads();
-        for (int p = threadIdx.x; p < n_pad; p += blockDim.x) {
-            int bin = -1;
-            if (p < n) {
-                const uint32_t bits = rb[p];
-                if (bits != 0xFFFFFFFFu) {
-                    const uint32_t hi = pass == 0 ? 0u : bits >> (shift + nbits);
-                    if (hi == prefix) bin = (int)((bits >> shift) & (uint32_t)(nb - 1));
-                }
-            }
-            const unsigned peers = __match_any_sync(0xffffffffu, bin);
-            if (bin >= 0 && lane == __ffs(peers) - 1) atomicAdd(&hist[bin], (uint32_t)__popc(peers));
-        }
-        __syncthreads();
-        const int per = nb / (int)blockDim.x;   // 4 or 2 bins per thread
-        uint32_t local[4] = {0, 0, 0, 0}, sum = 0;
-        for (int q = 0; q < per; ++q) {
-            local[q] = hist[threadIdx.x * per + q];
-            sum += local[q];
-        }
-        int total;
-        const uint32_t before = (uint32_t)block_exclusive_scan((int)sum, scan_sm, &total);
-        if (before < remaining && before + sum >= remaining) {
-            uint32_t run = before;
-            for (int q = 0; q < per; ++q) {
-                if (run + local[q] >= remaining) {
-                    s_digit = threadIdx.x * per + q;
-                    s_before = run;
-                    break;
-                }
-                run += local[q];
-            }
-        }
-        __syncthreads();
-        prefix = (prefix << nbits) | s_digit;
-        remaining -= s_before;
-        __syncthreads();
-    }
-    return prefix;
-}
 
 __global__ void __launch_bounds__(kGaugeThreads) k_gauge_fit(GaugeArgs a) {
     const int b = blockIdx.x;

@@ -347,3 +347,61 @@ def gauge_poly(depth, lidar, conf=None, degree: int = 2, iters: int = 3, points=
     call("pmg_gauge_poly", _p(depth), _p(lidar.contiguous()), _p(conf.contiguous() if conf is not None else None), B,
          H, W, h, w, degree, iters, _p(corr), _p(out), _p(points), _p(coef), _p(ws), nbytes, _stream())
     return corr, out, coef
+
+
+# ----------------------------------------------------------------------------------------------------------------- #
+# LiDAR prompt preparation
+# ----------------------------------------------------------------------------------------------------------------- #
+def _frames(t: torch.Tensor, name: str):
+    if t.dim() < 2:
+        raise ValueError(f"{name} must be [..., h, w]")
+    h, w = t.shape[-2:]
+    return max(1, t.numel() // max(1, h * w)), h, w
+
+
+def nearest_fill(depth: torch.Tensor, conf: torch.Tensor | None = None, out=None):
+    """promptmoge.nearest_fill (promptmoge/model.py:61-72) on the GPU, per frame of [..., h, w] fp32 tensors: every
+    missing pixel (depth <= 0 or NaN) takes the depth of its Euclidean-nearest present pixel and confidence 1.
+    conf None means all-high (2), as promptmoge.infer does.  Returns (depth, conf) tensors of the input shape: new
+    ones, or `out` = (depth_out, conf_out) (contiguous fp32, not aliasing the inputs)."""
+    _dev(depth, torch.float32, "depth")
+    if conf is None:
+        conf = torch.full_like(depth, 2.0)
+    _dev(conf, torch.float32, "conf")
+    if conf.shape != depth.shape:
+        raise ValueError("conf must have depth's shape")
+    B, h, w = _frames(depth, "depth")
+    if out is None:
+        d_out, c_out = torch.empty_like(depth), torch.empty_like(conf)
+    else:
+        d_out, c_out = _dev(out[0], torch.float32, "depth_out"), _dev(out[1], torch.float32, "conf_out")
+        if d_out.shape != depth.shape or c_out.shape != depth.shape:
+            raise ValueError("out tensors must have depth's shape")
+    if depth.numel() == 0:
+        return d_out, c_out
+    nbytes = _lib.load().pmg_prompt_workspace_bytes(B, h, w)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=depth.device)
+    call("pmg_nearest_fill", _p(depth), _p(conf), B, h, w, _p(d_out), _p(c_out), _p(ws), nbytes, _stream())
+    return d_out, c_out
+
+
+def build_prompt(depth: torch.Tensor, conf: torch.Tensor, out_hw, conf_levels: float = 2.0, mono_z=None,
+                 prefill=None, conf_phase: bool = False):
+    """build_prompt (moge/model/modules/prompt_stem.py:45-105) on the GPU: depth, conf [B,1,h,w] fp32 -> (prompt
+    [B,4,H,W] fp32, {"mu": [B]}).  The optional mono / prefill / phase channels are not part of the deployed
+    4-channel prompt and are not implemented here."""
+    if mono_z is not None or prefill is not None or conf_phase:
+        raise NotImplementedError("only the 4-channel prompt (no mono_z / prefill / conf_phase) is implemented")
+    depth = _dev(depth.float().contiguous(), torch.float32, "depth")
+    conf = _dev(conf.float().contiguous(), torch.float32, "conf")
+    if depth.dim() != 4 or depth.shape[1] != 1 or conf.shape != depth.shape:
+        raise ValueError("depth and conf must be [B,1,h,w]")
+    B, _, h, w = depth.shape
+    H, W = int(out_hw[0]), int(out_hw[1])
+    prompt = torch.empty((B, 4, H, W), dtype=torch.float32, device=depth.device)
+    mu = torch.empty(B, dtype=torch.float32, device=depth.device)
+    nbytes = _lib.load().pmg_prompt_workspace_bytes(B, h, w)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=depth.device)
+    call("pmg_build_prompt", _p(depth), _p(conf), B, h, w, H, W, float(conf_levels), _p(prompt), _p(mu), _p(ws),
+         nbytes, _stream())
+    return prompt, {"mu": mu}

@@ -15,6 +15,7 @@ import torch
 
 from . import synth
 from .engine import Geometry, RefinerEngine
+from . import ops
 from .ops import fit_state_view
 
 _CLIPS = Path(__file__).resolve().parent / "synth_clips.json"
@@ -51,6 +52,7 @@ class Refiner:
         self.h_fit = torch.empty((B, 18), dtype=torch.int32).pin_memory()
         self.engine.set_inputs(self.d_pc, self.d_ld, self.d_lc)
         self._K = None
+        self._raw = None
 
     def input_bytes(self) -> int:
         return sum(t.numel() * t.element_size() for t in (self.d_pc, self.d_ld, self.d_lc, self.d_enc, self.d_uv))
@@ -65,15 +67,25 @@ class Refiner:
             self._K = K
 
     def refine(self, point_coord, lidar_depth, lidar_conf, encoder_feature, uv_bias=None, K: int = 1,
-               sync: bool = True):
+               sync: bool = True, fill: bool = False):
         """Refine a batch of frames.  Host arrays/tensors (pinned CPU tensors copy asynchronously):
         point_coord [B,H,W,3] fp32, lidar_depth/lidar_conf [B,1,192,256] fp32, encoder_feature [B,1024,h,w] fp16,
-        uv_bias [B,C,h,w] fp32 or None.  Returns (refined point map [B,H,W,3] host tensor, fit list)."""
+        uv_bias [B,C,h,w] fp32 or None.  fill=True first applies promptmoge.nearest_fill to the sensor frames on the
+        device (promptmoge.infer does so by default before the model sees them, promptmoge/model.py:93-94).
+        Returns (refined point map [B,H,W,3] host tensor, fit list)."""
         self._ensure_graph(K)
         s = torch.cuda.current_stream(self.device)
-        for dst, src in ((self.d_pc, point_coord), (self.d_ld, lidar_depth), (self.d_lc, lidar_conf),
+        if fill:
+            if self._raw is None:
+                self._raw = (torch.empty_like(self.d_ld), torch.empty_like(self.d_lc))
+            ld, lc = self._raw
+        else:
+            ld, lc = self.d_ld, self.d_lc
+        for dst, src in ((self.d_pc, point_coord), (ld, lidar_depth), (lc, lidar_conf),
                          (self.d_enc, encoder_feature)):
             dst.copy_(torch.as_tensor(src), non_blocking=True)
+        if fill:
+            ops.nearest_fill(ld, lc, out=(self.d_ld, self.d_lc))
         if uv_bias is not None:
             self.d_uv.copy_(torch.as_tensor(uv_bias), non_blocking=True)
         self.engine.set_frame(self.d_enc, self.d_uv if uv_bias is not None else None)
