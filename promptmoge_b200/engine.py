@@ -120,7 +120,11 @@ class RefinerEngine:
     def _load_weights(self, w: dict, clips: dict):
         L = self.geo.levels
         for name in quantised_layer_names(L):
-            q, s = quantise_weight(w[name + ".weight"])
+            if name + ".weight_q8" in w:      # already quantised (a deployed refiner.bin): used as stored
+                q = np.asarray(w[name + ".weight_q8"], np.int8)
+                s = np.asarray(w[name + ".weight_scale"], np.float32)
+            else:
+                q, s = quantise_weight(w[name + ".weight"])
             if q.ndim == 5:      # (Co, 3, 3, 3, Ci) -> tap-major [27][Co][Ci]
                 q = q.reshape(q.shape[0], 27, q.shape[-1]).transpose(1, 0, 2)
             call("pmg_refiner_set_qlayer", self._h, name.encode(), self._t(q, torch.int8),

@@ -32,10 +32,14 @@ def synthetic_model(model: str = "A", seed: int = 0):
 
 class Refiner:
     def __init__(self, weights: dict, clips: dict, model: str = "A", height: int | None = None,
-                 width: int | None = None, batch: int = 1, device="cuda", capacity=None):
-        m = synth.MODELS[model]
-        self.geo = Geometry(channels=m["model_channels"], height=height or m["H"], width=width or m["W"],
-                            batch=batch)
+                 width: int | None = None, batch: int = 1, device="cuda", capacity=None, channels=None,
+                 enc_channels: int = synth.ENC_CHANNELS, depth_resolution: float = synth.DEPTH_RESOLUTION,
+                 uv_bias=None):
+        m = synth.MODELS[model] if model is not None else {}
+        self.geo = Geometry(channels=list(channels or m["model_channels"]), height=height or m["H"],
+                            width=width or m["W"], batch=batch, enc_channels=enc_channels,
+                            depth_resolution=depth_resolution)
+        self.default_uv = uv_bias      # baked UV conditioning [C_last, h, w] used when refine() gets none
         self.device = torch.device(device)
         self.engine = RefinerEngine(weights, clips, self.geo, device=self.device, capacity=capacity)
         B, H, W = batch, self.geo.height, self.geo.width
@@ -46,13 +50,14 @@ class Refiner:
         self.d_pc = torch.empty((B, H, W, 3), dtype=torch.float32, device=dev)
         self.d_ld = torch.empty((B, 1, lh, lw), dtype=torch.float32, device=dev)
         self.d_lc = torch.empty((B, 1, lh, lw), dtype=torch.float32, device=dev)
-        self.d_enc = torch.empty((B, synth.ENC_CHANNELS, H // ed, W // ed), dtype=torch.float16, device=dev)
+        self.d_enc = torch.empty((B, self.geo.enc_channels, H // ed, W // ed), dtype=torch.float16, device=dev)
         self.d_uv = torch.empty((B, self.geo.channels[-1], H // ed, W // ed), dtype=torch.float32, device=dev)
         self.h_out = torch.empty((B, H, W, 3), dtype=torch.float32).pin_memory()
         self.h_fit = torch.empty((B, 18), dtype=torch.int32).pin_memory()
         self.engine.set_inputs(self.d_pc, self.d_ld, self.d_lc)
         self._K = None
         self._raw = None
+        self._uv_dev = None
 
     def input_bytes(self) -> int:
         return sum(t.numel() * t.element_size() for t in (self.d_pc, self.d_ld, self.d_lc, self.d_enc, self.d_uv))
@@ -86,7 +91,12 @@ class Refiner:
             dst.copy_(torch.as_tensor(src), non_blocking=True)
         if fill:
             ops.nearest_fill(ld, lc, out=(self.d_ld, self.d_lc))
-        if uv_bias is not None:
+        if uv_bias is None and self.default_uv is not None:
+            if self._uv_dev is None:
+                self._uv_dev = torch.as_tensor(self.default_uv).to(self.device).expand_as(self.d_uv).contiguous()
+            self.d_uv.copy_(self._uv_dev)
+            uv_bias = self._uv_dev
+        elif uv_bias is not None:
             self.d_uv.copy_(torch.as_tensor(uv_bias), non_blocking=True)
         self.engine.set_frame(self.d_enc, self.d_uv if uv_bias is not None else None)
         out, fit = self.engine.replay()
@@ -96,6 +106,17 @@ class Refiner:
             s.synchronize()
             return self.h_out, fit_state_view(self.h_fit)
         return self.h_out, None
+
+    @classmethod
+    def from_refiner_dir(cls, path, batch: int = 1, device="cuda", capacity=None):
+        """A Refiner running the deployed int8 weights of a refiner.bin / refiner.json directory (the Metal
+        engine's ``Refiner(dir:)``, Refiner.swift:65-116): int8 weights and scales as stored, fp16 parameters
+        widened to fp32, the baked UV conditioning used whenever refine() is given no uv_bias."""
+        from .refiner_bin import read_refiner_dir
+        dep = read_refiner_dir(path)
+        return cls(dep.weights, dep.clips, model=None, height=dep.height, width=dep.width, batch=batch,
+                   device=device, capacity=capacity, channels=dep.channels, enc_channels=dep.enc_channels,
+                   depth_resolution=dep.depth_resolution, uv_bias=dep.uv_bias)
 
     def close(self):
         self.engine.close()
