@@ -221,6 +221,35 @@ int pmg_build_prompt(const float* depth, const float* conf, int32_t B, int32_t h
                      void* stream);
 
 /* --------------------------------------------------------------------------------------------------------------
+ * Post-refinement output (MoGeModel.infer, moge/model/v3.py:580-604, 739-800)
+ * ------------------------------------------------------------------------------------------------------------ */
+
+/* Refined (x/z, y/z, log z) map coords [B,h,w,3] -> affine points [B,H,W,3]: F.interpolate 'bilinear'
+ * (align_corners=False) to the image size, then the 'exp' remap (x e^z, y e^z, e^z) (v3.py:580-594, v2.py:172-187). */
+int pmg_resize_remap(const float* coords, int32_t B, int32_t h, int32_t w, int32_t H, int32_t W, float* points,
+                     void* stream);
+
+/* recover_focal_shift (moge/utils/geometry_torch.py:118-170): per frame, the dh x dw 'nearest' samples of points
+ * [B,H,W,3] (and of mask [B,H,W] uint8, NULL = all) against normalized_view_plane_uv; the shift minimising
+ * sum |f xy / (z + shift) - uv|^2 with f in closed form (or f = focal_in[b] when focal_in is not NULL), found in
+ * float64 from shift 0 -- the minimiser the reference's scipy Levenberg-Marquardt converges to
+ * (geometry_numpy.py:82-119) -- and the focal from it; fewer than two samples give focal 1, shift 0.
+ * dh * dw <= 8192.  Writes focal [B], shift [B] (fp32) on the device: no host round trip. */
+int pmg_focal_shift(const float* points, const uint8_t* mask, const float* focal_in, int32_t B, int32_t H, int32_t W,
+                    int32_t dh, int32_t dw, float* focal, float* shift, void* stream);
+
+/* depth [B,H,W] = points[..., 2] + shift[b] (v3.py:764-766). */
+int pmg_shift_depth(const float* points, const float* shift, int32_t B, int32_t H, int32_t W, float* depth,
+                    void* stream);
+
+/* Point map of a depth map [B,H,W] with the normalised intrinsics of infer (fx = f/2 sqrt(1+a^2)/a,
+ * fy = f/2 sqrt(1+a^2), centre 0.5, a = W/H; v3.py:741-742) and pixel centres ((j+0.5)/W, (i+0.5)/H)
+ * (utils3d.pt.depth_map_to_point_map).  mask [B,H,W] uint8 (NULL = none): masked-out pixels become +inf in points
+ * and depth_out (v3.py:828-832).  depth_out may be NULL or alias depth. */
+int pmg_depth_to_points(const float* depth, const float* focal, int32_t B, int32_t H, int32_t W, const uint8_t* mask,
+                        float* points, float* depth_out, void* stream);
+
+/* --------------------------------------------------------------------------------------------------------------
  * Refiner glue
  * ------------------------------------------------------------------------------------------------------------ */
 

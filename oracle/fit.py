@@ -13,6 +13,20 @@ import numpy as np
 f32 = np.float32
 
 
+def linspace_f32(start: float, end: float, n: int) -> np.ndarray:
+    """torch.linspace(start, end, n, dtype=float32): step = (end - start) / (n - 1) in fp32, then start + step * i
+    below the midpoint and end - step * (n - 1 - i) above it, each a fused multiply-add (one rounding; the product
+    and sum are formed exactly in float64 and rounded once)."""
+    s, e = f32(start), f32(end)
+    if n == 1:
+        return np.array([s], f32)
+    step = f32(e - s) / f32(n - 1)
+    i = np.arange(n, dtype=np.float64)
+    lo = (np.float64(s) + np.float64(step) * i).astype(f32)
+    hi = (np.float64(e) - np.float64(step) * (n - 1 - i)).astype(f32)
+    return np.where(np.arange(n) < n // 2, lo, hi).astype(f32)
+
+
 def nearest_index(out_size: int, in_size: int) -> np.ndarray:
     """Source index of torch's 'nearest' resize on CPU: min(floor(dst * (float)in/out), in-1) in fp32; identity when
     sizes match, dst >> 1 when out == 2 in (aten UpSample.h nearest_idx)."""

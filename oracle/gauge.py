@@ -16,20 +16,14 @@ from __future__ import annotations
 
 import numpy as np
 
-from .fit import area_resize
+from .fit import area_resize, linspace_f32
 
 f32 = np.float32
 
 
 def linspace(n: int) -> np.ndarray:
-    """torch.linspace(-1, 1, n) in fp32: start + i * step below the midpoint, end - (n - 1 - i) * step above it."""
-    if n == 1:
-        return np.array([-1.0], dtype=f32)
-    step = f32(2.0) / f32(n - 1)
-    i = np.arange(n)
-    lo = (f32(-1.0) + (step * i.astype(f32)).astype(f32)).astype(f32)
-    hi = (f32(1.0) - (step * (n - 1 - i).astype(f32)).astype(f32)).astype(f32)
-    return np.where(i < n // 2, lo, hi).astype(f32)
+    """torch.linspace(-1, 1, n) in fp32 (fused multiply-add form, see fit.linspace_f32)."""
+    return linspace_f32(-1.0, 1.0, n)
 
 
 def basis(uu: np.ndarray, vv: np.ndarray, degree: int) -> np.ndarray:

@@ -51,6 +51,10 @@ SIGNATURES = {
     "pmg_prompt_workspace_bytes": (SZ, [I32, I32, I32]),
     "pmg_nearest_fill": (I32, [P, P, I32, I32, I32, P, P, P, SZ, P]),
     "pmg_build_prompt": (I32, [P, P, I32, I32, I32, I32, I32, F32, P, P, P, SZ, P]),
+    "pmg_resize_remap": (I32, [P, I32, I32, I32, I32, I32, P, P]),
+    "pmg_focal_shift": (I32, [P, P, P, I32, I32, I32, I32, I32, P, P, P]),
+    "pmg_shift_depth": (I32, [P, P, I32, I32, I32, P, P]),
+    "pmg_depth_to_points": (I32, [P, P, I32, I32, I32, P, P, P, P]),
     "pmg_spconv_i8": (I32, [P, I64, P, I64, P, P, I64, I32, I32, P, P, P, F32, I32, F32, P, P, I32, P, P]),
     "pmg_l0_tap_lanes_bytes": (SZ, [I32, I32, I32]),
     "pmg_l0_tap_lanes": (I32, [P, I32, I32, I32, P, P]),

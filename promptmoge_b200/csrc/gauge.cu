@@ -23,11 +23,12 @@ constexpr int kGaugeThreads = 512;   // 27 fp64 accumulators per thread need mor
 constexpr int kGaugeBins = kSelectBins;
 constexpr int kGaugeOut = 8;    // per frame: coef[6], ok, confident count
 
-// torch.linspace(-1, 1, n)[i] in fp32 (start + i * step below the midpoint, end - (n - 1 - i) * step above it)
+// torch.linspace(-1, 1, n)[i] in fp32: start + step * i below the midpoint, end - step * (n - 1 - i) above it, each
+// one fused multiply-add (as torch's kernels compute it)
 __device__ __forceinline__ float lin11(int i, int n) {
     if (n == 1) return -1.0f;
     const float step = __fdiv_rn(2.0f, (float)(n - 1));
-    return i < n / 2 ? __fadd_rn(-1.0f, __fmul_rn(step, (float)i)) : __fsub_rn(1.0f, __fmul_rn(step, (float)(n - 1 - i)));
+    return i < n / 2 ? __fmaf_rn(step, (float)i, -1.0f) : __fmaf_rn(-step, (float)(n - 1 - i), 1.0f);
 }
 
 __device__ __forceinline__ int gauge_basis(float u, float v, int degree, float (&a)[6]) {
