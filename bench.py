@@ -299,6 +299,7 @@ def run_ours(args, ws, rank, local):
         if ws == 1 and not args.no_cpu_baseline and args.model == "A":
             cpu = cpu_baseline(batch=1, steps=1)
         prep = prompt_prep(torch, sc, dev, cpu=ws == 1 and not args.no_cpu_baseline)
+        post_t = post_output(torch, out, sc, dev, cpu=ws == 1 and not args.no_cpu_baseline)
         line = {
             "metric": METRIC if args.model == "A" else METRIC_B, "value": round(value, 3), "unit": UNIT, "n_gpus": ws,
             "steps": args.steps,
@@ -322,9 +323,51 @@ def run_ours(args, ws, rank, local):
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
             "prompt_prep": prep,
+            "post_output": post_t,
         }
     ref.close()
     return line
+
+
+def post_output(torch, out, sc, dev, cpu: bool, reps: int = 20):
+    """The output path of infer after the refine loop on the refined frame (promptmoge_b200.post.postprocess:
+    resize + remap to the 480x640 image, focal / shift, shifted depth, final LiDAR fit, point map, gauge): device
+    time (CUDA events, mean of `reps`), and the CPU time of the same steps through torch's CPU resize, the numpy
+    focal / shift, fit, point-map and gauge oracle (the reference solves focal / shift with scipy on the host)."""
+    from promptmoge_b200 import post
+    coords = out.detach().clone()
+    ld = torch.from_numpy(sc.lidar_depth).to(dev)
+    lc = torch.from_numpy(sc.lidar_conf).to(dev)
+    H, W = coords.shape[1], coords.shape[2]
+    for _ in range(3):
+        post.postprocess(coords, (H, W), ld, lc)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        post.postprocess(coords, (H, W), ld, lc)
+    e1.record()
+    e1.synchronize()
+    res = {"frames": int(coords.shape[0]), "image_hw": [H, W], "gpu_us": round(e0.elapsed_time(e1) * 1e3 / reps, 1)}
+    if cpu:
+        import numpy as np
+        import torch.nn.functional as F
+        from oracle import fit as ofit
+        from oracle import gauge as ogauge
+        from oracle import post as opost
+        c = coords.cpu()
+        t0 = time.perf_counter()
+        r = F.interpolate(c.movedim(-1, -3), (H, W), mode="bilinear", align_corners=False).movedim(-3, -1).numpy()
+        pts = opost.remap_exp(r)
+        f, s = opost.recover_focal_shift(pts)
+        depth = (pts[..., 2] + s[:, None, None]).astype(np.float32)
+        depth, _, _ = ofit.final_fit(depth, sc.lidar_depth, sc.lidar_conf)
+        fx, fy = zip(*[opost.focal_to_fxfy(np.float32(x), W, H) for x in f])
+        points = opost.depth_to_points(depth, fx, fy)
+        corr = ogauge.prompt_gauge_poly(depth, sc.lidar_depth[:, 0], sc.lidar_conf[:, 0], degree=2)
+        _ = (points * corr[..., None], depth * corr)
+        res["cpu_us"] = round((time.perf_counter() - t0) * 1e6, 1)
+        res["cpu_kind"] = "torch CPU resize + numpy oracle of focal/shift, fit, point map, gauge; 1 thread"
+    return res
 
 
 def prompt_prep(torch, sc, dev, cpu: bool, reps: int = 50):

@@ -64,7 +64,7 @@ struct Cfg {
     static_assert(kStages >= 3, "two MMA warps need >= 3 ring stages for sound parity waits");
 };
 
-template <int KIND, int NT, int W, bool RES>
+template <int KIND, int NT, int W, bool RES, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
               const int8_t* __restrict__ in, int64_t in_rows, const int32_t* __restrict__ nmap, int64_t ld,
@@ -140,7 +140,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t M = rows_of(count, max_rows);
     const int64_t ntile = (M + kM - 1) / kM;
     const int nblk = Co / NT;
-    const int64_t nunits = ntile * nblk;
+    // split-K: the split count minimising ceil(units * S / CTAs) / S (ties to fewer splits), from the row count
+    int S = 1;
+    if (SPLIT && KIND == GATHER && e.nsplit > 1 && e.part && e.cnt) {
+        const int64_t tb_units = ntile * nblk;
+        int64_t best_num = (tb_units + gridDim.x - 1) / gridDim.x, best_den = 1;
+        for (int c = 2; c <= e.nsplit; ++c) {
+            const int64_t rounds = (tb_units * c + gridDim.x - 1) / gridDim.x;
+            if (rounds * best_den < best_num * c) {
+                best_num = rounds;
+                best_den = c;
+                S = c;
+            }
+        }
+    }
+    const int64_t nunits = ntile * nblk * S;
     const int tpi = (taps == 27 && Ci < kItemK) ? kItemK / Ci : 1;   // taps per item
     const int nkb = Ci > W ? Ci / W : 1;                               // K-blocks per tap
 
@@ -166,11 +180,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 4; ++i) w[i] = (tile_mask && i * 32 < mc) ? tile_mask[(m0 >> 5) + i] : 0u;
     };
-    auto record_of = [&](int64_t t, const uint32_t (&w)[4]) -> int4 {
+    auto record_of = [&](int64_t t, const uint32_t (&w)[4], int ks) -> int4 {
         const int64_t m0 = t * kM;
         const int mc = (int)min((int64_t)kM, M - m0);
         uint32_t mk = tile_mask ? ((w[0] | w[1] | w[2] | w[3]) & 0x7ffffffu) : 0x7ffffffu;
         if (!mk) mk = 1u;
+        if (SPLIT && S > 1) {
+            // split ks of S keeps the taps whose item falls in [i0, i1) of the tile's items (whole items, so a split
+            // never shares an item with another); an empty split contributes a zero partial
+            const int n = __popc(mk), nit = (n + tpi - 1) / tpi;
+            const int r0 = (nit * ks / S) * tpi, r1 = min((nit * (ks + 1) / S) * tpi, n);
+            uint32_t keep = 0u, rest = mk;
+            for (int rank = 0; rest; ++rank) {
+                const uint32_t bit = rest & (0u - rest);
+                if (rank >= r0 && rank < r1) keep |= bit;
+                rest ^= bit;
+            }
+            mk = keep;
+        }
         const int items = ((__popc(mk) + tpi - 1) / tpi) * nkb;
         return make_int4((int)m0, mc, (int)mk, items);
     };
@@ -242,7 +269,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive(&rec_full[slot]);
                 return true;
             };
-            auto unit_tile = [&](uint32_t j) -> int64_t { return ((int64_t)blockIdx.x + (int64_t)j * gridDim.x) / nblk; };
+            auto unit_tile = [&](uint32_t j) -> int64_t {
+                return ((int64_t)blockIdx.x + (int64_t)j * gridDim.x) / ((int64_t)nblk * S);
+            };
+            auto unit_split = [&](uint32_t j) -> int { return (int)(((int64_t)blockIdx.x + (int64_t)j * gridDim.x) % S); };
             auto unit_exists = [&](uint32_t j) -> bool { return (int64_t)blockIdx.x + (int64_t)j * gridDim.x < nunits; };
             // publish unit j from the prefetched words (loaded earlier), then start the loads for unit j + 1
             auto publish = [&](uint32_t j) -> bool {                 // thread 0; units in order
@@ -258,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mask_words(unit_tile(j + 1), pf_w);
                     pf_j = j + 1;
                 }
-                return publish_one(j, record_of(unit_tile(j), w));
+                return publish_one(j, record_of(unit_tile(j), w, unit_split(j)));
             };
             // Neighbour indices of a full tile are fetched with one 512-byte bulk copy per present tap (TMA, tracked
             // by bytes on idx_full): keeping them out of the producers' cp.async groups matters because a stage's
@@ -311,13 +341,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!ok) break;
                 const int4 ra = s_rec[k % kRecs];       // published (issue_ids(k) waited for it)
                 const int mc = ra.y;
-                const int n0 = (int)(u % nblk) * NT;
+                const int n0 = (int)((u / S) % nblk) * NT;
                 const uint32_t cidx_base = idx_base + (uint32_t)(cb * 27 * kM + my_row) * 4u;
                 uint32_t row_live = 0;                      // bit p: row my_row + p * RPP is inside the tile
 #pragma unroll
                 for (int p = 0; p < NP; ++p) row_live |= (my_row + p * RPP < mc ? 1u : 0u) << p;
                 bool prefetched = false;
                 uint32_t mk = (uint32_t)ra.z;
+                if (mk == 0u) {
+                    // an empty split: no items, so publish the next unit and start its index copies now
+                    prefetched = true;
+                    if (has_next) {
+                        if (threadIdx.x == 0) ok = publish(k + 3);
+                        ok = __all_sync(0xffffffffu, ok);
+                        ok = ok && issue_ids(k + 1);
+                    }
+                }
                 while (mk && ok) {
                     int tv[TPI];
                     const int nt = take(mk, tv);
@@ -513,12 +552,85 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tile_of(u / nblk, m0, mc, mk);
             }
             const bool two = ((__popc(mk) + tpi - 1) / tpi) * nkb > 1;
-            const int n0 = (int)(u % nblk) * NT;
+            const int64_t tb = u / S;
+            const int n0 = (int)(tb % nblk) * NT;
             const uint32_t b = k & 1u;
             if (!mbar_wait(&acc_full[b], (k >> 1) & 1u, &s_abort)) { ok = false; break; }
             tc_fence_after();
             const int rr = 32 * q + lane;
             const bool live = rr < mc;
+            if (SPLIT && S > 1) {
+                // split-K: store this split's partial sub-tile, release TMEM, count the arrival; the last split of
+                // the sub-tile to arrive sums all partials (exact int32) and runs the epilogue
+                const uint32_t t0 = tmem + 2 * b * NCOLS + ((uint32_t)(32 * q) << 16);
+                int32_t* prow = e.part + ((tb * S + (u % S)) * kM + rr) * NT;
+#pragma unroll 1
+                for (int jj = 0; jj < CH; ++jj) {
+                    const int j = j0 + jj;
+                    uint32_t acc[16];
+                    if (mk == 0u) {
+#pragma unroll
+                        for (int t = 0; t < 16; ++t) acc[t] = 0u;
+                    } else {
+                        tmem_ld16(t0 + (uint32_t)(j * 16), acc);
+                        if (two) {
+                            uint32_t acc1[16];
+                            tmem_ld16(t0 + NCOLS + (uint32_t)(j * 16), acc1);
+#pragma unroll
+                            for (int t = 0; t < 16; ++t) acc[t] += acc1[t];
+                        }
+                    }
+                    if (live) {
+                        int4* d = reinterpret_cast<int4*>(prow + j * 16);
+#pragma unroll
+                        for (int t4 = 0; t4 < 4; ++t4)
+                            d[t4] = make_int4((int)acc[4 * t4], (int)acc[4 * t4 + 1], (int)acc[4 * t4 + 2],
+                                              (int)acc[4 * t4 + 3]);
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[b]);
+                __threadfence();
+                __syncwarp();
+                int32_t* ctr = e.cnt + tb * kEpiWarps + (warp - kEpi0);
+                int old = 0;
+                if (lane == 0) old = atomicAdd(ctr, 1);
+                old = __shfl_sync(0xffffffffu, old, 0);
+                if (old == S - 1) {
+                    __threadfence();
+                    const float* rrow =
+                        (e.mode == PMG_EPI_F32_RESID && live) ? e.resid + (m0 + rr) * Co + n0 + j0 * 16 : nullptr;
+#pragma unroll 1
+                    for (int jj = 0; jj < CH; ++jj) {
+                        const int j = j0 + jj;
+                        float4 rcur[4];
+                        if (rrow) load_resid16(rrow + jj * 16, rcur);
+                        if (live) {
+                            uint32_t acc[16];
+#pragma unroll
+                            for (int t = 0; t < 16; ++t) acc[t] = 0u;
+#pragma unroll 1
+                            for (int sp = 0; sp < S; ++sp) {
+                                const int4* src = reinterpret_cast<const int4*>(e.part + ((tb * S + sp) * kM + rr) * NT +
+                                                                                j * 16);
+#pragma unroll
+                                for (int t4 = 0; t4 < 4; ++t4) {
+                                    const int4 v = __ldcg(src + t4);
+                                    acc[4 * t4] += (uint32_t)v.x;
+                                    acc[4 * t4 + 1] += (uint32_t)v.y;
+                                    acc[4 * t4 + 2] += (uint32_t)v.z;
+                                    acc[4 * t4 + 3] += (uint32_t)v.w;
+                                }
+                            }
+                            epi_store16(e, s_ws, s_bias, m0 + rr, n0 + j * 16, Co, acc, rcur);
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) *ctr = 0;          // every split has arrived: zero for the next launch
+                }
+                continue;
+            }
             const float* rrow =
                 (e.mode == PMG_EPI_F32_RESID && live) ? e.resid + (m0 + rr) * Co + n0 + j0 * 16 : nullptr;
             float4 rcur[4], rnext[4];
@@ -612,7 +724,7 @@ struct TcArgs {
     const int8_t* w;
 };
 
-template <int KIND, int NT, int W, bool RES>
+template <int KIND, int NT, int W, bool RES, bool SPLIT = false>
 int launch(const TcArgs& a, const Epi& e, cudaStream_t s) {
     using C = tc::Cfg<KIND, NT, W, RES>;
     static bool attr_set[64] = {};
@@ -620,11 +732,11 @@ int launch(const TcArgs& a, const Epi& e, cudaStream_t s) {
     PMG_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return PMG_ERR_UNSUPPORTED;
     if (!attr_set[dev]) {
-        PMG_CUDA_TRY(cudaFuncSetAttribute(tc::k_gemm_tc<KIND, NT, W, RES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        PMG_CUDA_TRY(cudaFuncSetAttribute(tc::k_gemm_tc<KIND, NT, W, RES, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           C::kSmem));
         attr_set[dev] = true;
     }
-    const int64_t units = (a.max_rows + tc::kM - 1) / tc::kM * (a.Co / NT);
+    const int64_t units = (a.max_rows + tc::kM - 1) / tc::kM * (a.Co / NT) * (SPLIT ? std::max(1, e.nsplit) : 1);
     const int grid = (int)std::min<int64_t>(units, (int64_t)kNumSMs);
     if (grid <= 0) return PMG_OK;
     CUtensorMap ma, mb;
@@ -634,7 +746,7 @@ int launch(const TcArgs& a, const Epi& e, cudaStream_t s) {
     if (rc != PMG_OK) return rc;
     rc = make_tensor_map(&mb, a.w, (uint64_t)a.taps * a.Co, (uint64_t)a.Ci, W, NT);
     if (rc != PMG_OK) return rc;
-    tc::k_gemm_tc<KIND, NT, W, RES><<<grid, tc::kThreads, C::kSmem, s>>>(
+    tc::k_gemm_tc<KIND, NT, W, RES, SPLIT><<<grid, tc::kThreads, C::kSmem, s>>>(
         ma, mb, a.in, a.in_rows, a.nmap, a.ld, a.tile_mask, a.count, a.max_rows, a.Ci, a.Co, a.taps, e);
     PMG_LAUNCH_CHECK();
     return PMG_OK;
@@ -642,6 +754,10 @@ int launch(const TcArgs& a, const Epi& e, cudaStream_t s) {
 
 template <int KIND, int NT, int W>
 int launch_res(const TcArgs& a, const Epi& e, cudaStream_t s) {
+    // split-K variant: the wide gather convs (the coarse levels, whose tile counts can leave SMs idle)
+    if constexpr (KIND == tc::GATHER && NT == 128 && W == 128) {
+        if (e.nsplit > 1 && e.part && e.cnt) return launch<KIND, NT, W, false, true>(a, e, s);
+    }
     // whole 27-tap weight resident in shared memory when it is one N block and leaves a ring of >= 4 stages
     if constexpr (KIND == tc::GATHER && W < tc::kItemK && 27 * NT * W <= tc::kResMax) {
         if constexpr (tc::Cfg<KIND, NT, W, true>::kStagesRaw >= 4) {

@@ -83,7 +83,7 @@ class RefinerEngine:
     """Device-resident int8 refiner.  All tensors it returns live on `device`."""
 
     def __init__(self, weights: dict, clips: dict, geometry: Geometry, device="cuda", capacity=None,
-                 use_prompt: bool = True, tensor_cores: bool = True):
+                 use_prompt: bool = True, tensor_cores: bool = True, max_split: int = 0):
         _lib.load()
         self.geo = geometry
         self.device = torch.device(device)
@@ -100,6 +100,7 @@ class RefinerEngine:
         cfg.soft_gate, cfg.fit_iters, cfg.fit_trim, cfg.fit_min_points = 1, 4, 0.2, 32
         cfg.use_prompt = int(use_prompt)
         cfg.use_tensor_cores = int(tensor_cores)
+        cfg.max_split = int(max_split)
         for k in range(L):
             cfg.capacity[k] = int(capacity[k]) if capacity is not None else 0
         self._cfg = cfg

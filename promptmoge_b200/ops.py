@@ -132,15 +132,23 @@ def grid0_supported(Ci: int, Co: int) -> bool:
 
 
 def spconv_i8(q_in, nmap, tile_mask, weight_tap_major, w_scale=None, bias=None, act_scale=1.0, mode=EPI_ACC32,
-              out_scale=1.0, resid=None, count=None, rows=None, tensor_cores=True, status=None):
+              out_scale=1.0, resid=None, count=None, rows=None, tensor_cores=True, status=None, split: int = 1):
     """Submanifold conv: q_in [M_in, Ci] int8, nmap [27, ld] int32, weight [27, Co, Ci] int8.  The tcgen05 kernel
-    runs where the shape allows unless tensor_cores is False."""
+    runs where the shape allows unless tensor_cores is False; split > 1 allows split-K (up to `split` CTAs per output
+    tile, same results)."""
     _dev(q_in, torch.int8, "q_in")
     _dev(weight_tap_major, torch.int8, "weight")
     ld = nmap.shape[1]
     rows = ld if rows is None else rows
     Co, Ci = weight_tap_major.shape[1], weight_tap_major.shape[2]
     out = _epi_out(mode, rows, Co, q_in.device)
+    if split > 1 and tensor_cores:
+        nbytes = _lib.load().pmg_spconv_i8_split_workspace_bytes(rows, Co, split)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=q_in.device)
+        call("pmg_spconv_i8_split", _p(q_in), q_in.shape[0], _p(nmap), ld, _p(tile_mask), _p(count), rows, Ci, Co,
+             _p(weight_tap_major), _p(w_scale), _p(bias), float(act_scale), mode, float(out_scale), _p(resid),
+             _p(out), int(split), _p(ws), nbytes, _p(status), _stream())
+        return out
     call("pmg_spconv_i8", _p(q_in), q_in.shape[0], _p(nmap), ld, _p(tile_mask), _p(count), rows, Ci, Co,
          _p(weight_tap_major), _p(w_scale), _p(bias), float(act_scale), mode, float(out_scale), _p(resid), _p(out),
          0 if tensor_cores else FLAG_SIMT, _p(status), _stream())

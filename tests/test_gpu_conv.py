@@ -208,3 +208,36 @@ def test_float_conv_matches_reference_semantics(golden):
     wt = torch.from_numpy(np.ascontiguousarray(w.reshape(48, 27, 64).transpose(1, 0, 2))).cuda()
     got = ops.spconv_f32(torch.from_numpy(x).cuda(), _tap_major(nm), _mask(nm), wt, torch.from_numpy(b).cuda())
     np.testing.assert_allclose(got.cpu().numpy(), want, rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("C,N,split", [(128, 3000, 4), (256, 3000, 3), (256, 12000, 2), (128, 60000, 4),
+                                       (256, 200, 4), (128, 129, 2)])
+def test_split_k_equals_single_pass(C, N, split):
+    """Split-K (several CTAs per output tile, partial int32 tiles summed by the last arrival): accumulators equal the
+    oracle's and every epilogue equals the single-pass kernel bit for bit, repeated launches included (the arrival
+    counters return to zero)."""
+    from promptmoge_b200 import ops, synth
+    from oracle import structure as ost
+    coords_np = synth.make_surface_voxels(N, seed=C + N)
+    coords = torch.from_numpy(coords_np).cuda()
+    ext = [1, 1 << 21, 1 << 21, 1 << 21]
+    tm, mask, _ = ops.nmap_hash(coords, ext)
+    rng = np.random.default_rng(C * 7 + N)
+    M = coords_np.shape[0]
+    q = torch.from_numpy(rng.integers(-127, 128, (M, C)).astype(np.int8)).cuda()
+    qw = rng.integers(-127, 128, (C, 3, 3, 3, C)).astype(np.int8)
+    wt = torch.from_numpy(np.ascontiguousarray(qw.reshape(C, 27, C).transpose(1, 0, 2))).cuda()
+    ws = torch.from_numpy(rng.uniform(1e-4, 1e-3, C).astype(np.float32)).cuda()
+    b = torch.from_numpy(rng.standard_normal(C).astype(np.float32)).cuda()
+    resid = torch.from_numpy(rng.standard_normal((M, C)).astype(np.float32)).cuda()
+    status = torch.zeros(1, dtype=torch.int32).cuda()
+    if N <= 3000:
+        want = oref.conv_acc(q.cpu().numpy(), ost.nmap_sorted(coords_np, ext), qw)
+        got = ops.spconv_i8(q, tm, mask, wt, split=split, status=status).cpu().numpy()
+        np.testing.assert_array_equal(got.astype(np.int64), want)
+    for mode in (ops.EPI_ACC32, ops.EPI_F32, ops.EPI_F32_RESID, ops.EPI_SILU_Q8):
+        one = ops.spconv_i8(q, tm, mask, wt, ws, b, 0.03, mode, 0.05, resid, status=status)
+        for _ in range(2):
+            sp = ops.spconv_i8(q, tm, mask, wt, ws, b, 0.03, mode, 0.05, resid, status=status, split=split)
+            assert torch.equal(sp, one), mode
+    assert int(status.item()) == 0

@@ -130,3 +130,31 @@ def test_tensor_core_plan_equals_simt_plan(golden):
         outs.append(out.clone())
         eng.close()
     assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("name", ["A_full", "A_small"])
+def test_split_k_plan_equals_unsplit_plan(golden, name):
+    """The plan's wide convs of the small levels split across CTAs (default) or not (max_split=1): identical bits,
+    over captured-graph replays, with capacities fitted to the counts (the split count is chosen on the device)."""
+    from promptmoge_b200 import synth
+    from promptmoge_b200.engine import Geometry, RefinerEngine
+    g = golden(name)
+    sc = g.scene()
+    c = g.config
+    geo = Geometry(channels=synth.MODELS[c["model"]]["model_channels"], height=c["H"], width=c["W"])
+    outs = []
+    for ms in (1, 0):
+        eng = RefinerEngine(g.weights(), g.clips, geo, max_split=ms)
+        _inputs(eng, sc)
+        eng.run(1)
+        rc, counts = eng.status()
+        assert rc == 0
+        eng.fit_to(counts)
+        _inputs(eng, sc)
+        eng.capture(1)
+        for _ in range(3):
+            out, _ = eng.replay()
+        assert eng.status()[0] == 0
+        outs.append(out.clone())
+        eng.close()
+    assert torch.equal(outs[0], outs[1])
