@@ -153,10 +153,10 @@ int pmg_spconv_i8(const int8_t* in_q8, int64_t in_rows, const int32_t* nmap, int
 size_t pmg_spconv_i8_split_workspace_bytes(int64_t max_rows, int32_t Co, int32_t max_split);
 
 /* pmg_spconv_i8 with split-K on the tensor-core path (Co = 128 or 256, Ci a multiple of 128): up to `max_split`
- * CTAs share one 128-row output tile, each over a contiguous group of its taps; partial int32 tiles go to the
- * workspace and the last split of a tile sums them (exact) and runs the epilogue, so results equal pmg_spconv_i8's
- * bit for bit.  The split count is chosen on the device from the row count (fewer tiles than SMs -> more splits).
- * Other shapes run as pmg_spconv_i8.  The plan's wide convs of small levels use the same path. */
+ * CTAs share one 128-row output tile, each over a contiguous group of its taps; each split's int32 partial sums go
+ * to a workspace plane and a second kernel adds the planes (exact) and runs the epilogue, so results equal
+ * pmg_spconv_i8's bit for bit.  The split count is chosen on the device from the row count (fewer tiles than SMs ->
+ * more splits).  Other shapes run as pmg_spconv_i8.  The plan's wide convs of small levels use the same path. */
 int pmg_spconv_i8_split(const int8_t* in_q8, int64_t in_rows, const int32_t* nmap, int64_t ld,
                         const uint32_t* tile_mask, const int32_t* count, int64_t max_rows, int32_t Ci, int32_t Co,
                         const int8_t* weight, const float* w_scale, const float* bias, float act_scale,
@@ -371,7 +371,7 @@ typedef struct pmg_refiner_config {
     int32_t use_prompt;         /* 1: feed the LiDAR residual channels (refiner_residual) */
     int64_t capacity[8];        /* voxel capacity per level (0 = B*H*W, which cannot overflow) */
     int32_t use_tensor_cores;   /* 1: tcgen05 int8 kernels where the shape allows; 0: SIMT dp4a everywhere */
-    int32_t max_split;          /* split-K limit for the wide convs of small levels (0 = 4, 1 = off); results are
+    int32_t max_split;          /* split-K limit for the wide convs of small levels (0 or 1 = off); results are
                                    identical for every value (exact int32 partial sums) */
 } pmg_refiner_config;
 

@@ -102,8 +102,7 @@ struct pmg_refiner {
     int32_t* zq = nullptr;         // [N]
     uint32_t* lanes0 = nullptr;    // level-0 tap masks of the frame-grid conv: [ceil(N / 128)][27][4]
     int32_t* zext = nullptr;       // [2B]: zmin[B], zmax[B]
-    int32_t* split_part = nullptr; // split-K partial tiles of the wide convs (shared by the levels, convs run in order)
-    int32_t* split_cnt = nullptr;  // split-K arrival counters, zero between launches
+    int32_t* split_part = nullptr; // split-K partial planes of the wide convs (shared by the levels, convs run in order)
     int lsplit[8] = {1, 1, 1, 1, 1, 1, 1, 1};   // per level: largest split count the conv may choose
     int32_t* counts = nullptr;     // [L][2]
     int32_t* status = nullptr;
@@ -212,10 +211,10 @@ int allocate(pmg_refiner* r) {
     PMG_CUDA_TRY(cudaMemset(r->fit_ws, 0, r->fit_ws_bytes));
     PMG_TRY(alloc(r, &r->zq, r->N));
     PMG_TRY(alloc(r, &r->lanes0, (size_t)((r->N + 127) / 128) * 27 * 4));
-    // split-K for the wide (C >= 128) convs of levels with fewer than two tile rounds per SM: up to 4 splits, the
-    // count itself chosen on the device from the level's actual size
-    size_t part_elems = 0, cnt_elems = 0;
-    const int max_split = c.max_split > 0 ? c.max_split : 4;
+    // split-K for the wide (C >= 128) convs of levels with fewer than two tile rounds per SM: up to max_split
+    // splits, the count itself chosen on the device from the level's actual size
+    size_t part_elems = 0;
+    const int max_split = c.max_split;
     for (int k = 1; k < r->L; ++k) {
         const LevelBuf& l = r->lv[k];
         r->lsplit[k] = 1;
@@ -225,14 +224,9 @@ int allocate(pmg_refiner* r) {
         const int sp = (int)std::min<int64_t>(max_split, std::max<int64_t>(1, want));
         if (sp < 2) continue;
         r->lsplit[k] = sp;
-        part_elems = std::max(part_elems, (size_t)(units * sp * 128 * 128));
-        cnt_elems = std::max(cnt_elems, (size_t)(units * 8));
+        part_elems = std::max(part_elems, (size_t)(sp * l.cap * l.C));
     }
-    if (part_elems) {
-        PMG_TRY(alloc(r, &r->split_part, part_elems));
-        PMG_TRY(alloc(r, &r->split_cnt, cnt_elems));
-        PMG_CUDA_TRY(cudaMemset(r->split_cnt, 0, cnt_elems * sizeof(int32_t)));
-    }
+    if (part_elems) PMG_TRY(alloc(r, &r->split_part, part_elems));
     PMG_TRY(alloc(r, &r->zext, 2 * B));
     PMG_TRY(alloc(r, &r->counts, 2 * r->L));
     PMG_TRY(alloc(r, &r->status, 1));
@@ -335,7 +329,6 @@ int conv(const pmg_refiner* r, int k, const LevelBuf& l, const int8_t* in, const
     if (r->lsplit[k] > 1 && r->split_part) {
         e.nsplit = r->lsplit[k];
         e.part = r->split_part;
-        e.cnt = r->split_cnt;
     }
     if (k == 0 && grid0_used(r))
         return conv_grid0_tc(in, r->lanes0, r->cfg.batch, r->cfg.height, r->cfg.width, l.C, l.C, q.w, e, s);

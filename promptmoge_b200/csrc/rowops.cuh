@@ -17,12 +17,11 @@ struct Epi {
     int8_t* q2 = nullptr;        // F32 / F32_RESID: also write q(y, q2_scale) here (the next layer's int8 input)
     float q2_scale = 0.f;
     // split-K (tensor-core gather convs): up to `nsplit` CTAs share one output tile, each over a contiguous group of
-    // its taps; partial int32 tiles go to `part` ([tile-block][split][128][NT]) and the last of a tile's splits to
-    // arrive (per-epilogue-warp counters `cnt`, zero between launches) sums them and runs the epilogue.  The split
-    // count actually used is chosen on the device from the level's row count (1 when there are enough tiles).
+    // its items; split s writes its int32 partial sums to plane s of `part` ([nsplit][max_rows][Co]) and a second
+    // kernel sums the planes and runs the epilogue.  The split count actually used is chosen on the device from the
+    // level's row count (1 when there are enough tiles, and then the conv kernel runs the epilogue itself).
     int nsplit = 1;
     int32_t* part = nullptr;
-    int32_t* cnt = nullptr;
 };
 
 int gemm_i8_simt(const int8_t* in, const int32_t* nmap, int64_t ld, const uint32_t* tile_mask, const int32_t* count,

