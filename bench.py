@@ -636,8 +636,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--K", type=int, default=1, help="refine steps per graph (the workload's K)")
     ap.add_argument("--batch", type=int, default=1, help="frames per GPU per step")
-    ap.add_argument("--max-split", type=int, default=0,
-                    help="split-K limit of the plan's wide convs (0 or 1 = off)")
+    ap.add_argument("--max-split", type=int, default=4,
+                    help="split-K limit of the plan's wide convs of levels with fewer tiles than SMs (1 = off)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ncu", action="store_true", help="profiling mode: warm-up + timed replays only, no extras")
     ap.add_argument("--profile-conv", type=int, default=None, metavar="LEVEL",

@@ -211,8 +211,8 @@ int allocate(pmg_refiner* r) {
     PMG_CUDA_TRY(cudaMemset(r->fit_ws, 0, r->fit_ws_bytes));
     PMG_TRY(alloc(r, &r->zq, r->N));
     PMG_TRY(alloc(r, &r->lanes0, (size_t)((r->N + 127) / 128) * 27 * 4));
-    // split-K for the wide (C >= 128) convs of levels with fewer than two tile rounds per SM: up to max_split
-    // splits, the count itself chosen on the device from the level's actual size
+    // split-K for the wide (C >= 128) convs of levels with fewer tile blocks than SMs: up to max_split splits, the
+    // count itself chosen on the device from the level's actual size
     size_t part_elems = 0;
     const int max_split = c.max_split;
     for (int k = 1; k < r->L; ++k) {
@@ -220,9 +220,8 @@ int allocate(pmg_refiner* r) {
         r->lsplit[k] = 1;
         if (!c.use_tensor_cores || l.C < 128 || max_split < 2) continue;
         const int64_t units = l.cap / 128 * (l.C / 128);
-        const int64_t want = (2 * kNumSMs + units - 1) / units;
-        const int sp = (int)std::min<int64_t>(max_split, std::max<int64_t>(1, want));
-        if (sp < 2) continue;
+        if (units >= kNumSMs) continue;       // a level that fills the SMs never splits
+        const int sp = max_split;
         r->lsplit[k] = sp;
         part_elems = std::max(part_elems, (size_t)(sp * l.cap * l.C));
     }

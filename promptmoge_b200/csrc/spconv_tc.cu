@@ -64,20 +64,14 @@ struct Cfg {
     static_assert(kStages >= 3, "two MMA warps need >= 3 ring stages for sound parity waits");
 };
 
-// Split count for `units` tile blocks over `ctas` CTAs: the S <= limit minimising ceil(units * S / ctas) / S
-// (rounds of 1/S-size units), ties to fewer splits.  The conv kernel and its split epilogue compute it alike.
+// Split count for `units` tile blocks over `ctas` CTAs: only a conv with fewer tile blocks than CTAs splits (SMs
+// would idle), into as many splits as still fit one round (at most `limit`).  Splitting a multi-round conv was
+// measured slower: its saving is smaller than the partial-plane round trip.  The conv kernel and its split epilogue
+// compute it alike.
 __host__ __device__ __forceinline__ int split_count(int64_t units, int limit, int ctas) {
-    int S = 1;
-    int64_t best_num = (units + ctas - 1) / ctas, best_den = 1;
-    for (int c = 2; c <= limit; ++c) {
-        const int64_t rounds = (units * c + ctas - 1) / ctas;
-        if (rounds * best_den < best_num * c) {
-            best_num = rounds;
-            best_den = c;
-            S = c;
-        }
-    }
-    return S;
+    if (units <= 0 || units >= ctas) return 1;
+    const int64_t fit = ctas / units;
+    return (int)(fit < limit ? fit : limit);
 }
 
 // Taps of split ks of S of a tile's tap mask: the taps whose item falls in [i0, i1) of the tile's items (whole

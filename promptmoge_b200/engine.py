@@ -83,7 +83,7 @@ class RefinerEngine:
     """Device-resident int8 refiner.  All tensors it returns live on `device`."""
 
     def __init__(self, weights: dict, clips: dict, geometry: Geometry, device="cuda", capacity=None,
-                 use_prompt: bool = True, tensor_cores: bool = True, max_split: int = 0):
+                 use_prompt: bool = True, tensor_cores: bool = True, max_split: int = 4):
         _lib.load()
         self.geo = geometry
         self.device = torch.device(device)

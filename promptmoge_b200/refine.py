@@ -34,7 +34,7 @@ class Refiner:
     def __init__(self, weights: dict, clips: dict, model: str = "A", height: int | None = None,
                  width: int | None = None, batch: int = 1, device="cuda", capacity=None, channels=None,
                  enc_channels: int = synth.ENC_CHANNELS, depth_resolution: float = synth.DEPTH_RESOLUTION,
-                 uv_bias=None, max_split: int = 0):
+                 uv_bias=None, max_split: int = 4):
         m = synth.MODELS[model] if model is not None else {}
         self.geo = Geometry(channels=list(channels or m["model_channels"]), height=height or m["H"],
                             width=width or m["W"], batch=batch, enc_channels=enc_channels,
