@@ -349,6 +349,19 @@ int pmg_prompt_feats(const float* logz, int64_t logz_stride, const float* lidar,
 /* depth = s * depth + t per frame, in place (v3.py:777). */
 int pmg_apply_affine(float* depth, const pmg_fit_state* state, int32_t B, int64_t N, void* stream);
 
+/* Refiner output gate (v3.py:565-569, off in the released configs): out = cur + g * (refined - cur) with
+ * g = floor + (1 - floor) * u, u = 1 - c * (1 - clamp((d - 3) / 2, 0, 1)) of the nearest-resized sensor (1 where it has
+ * no value; MoGeModel._lidar_uncertainty, v3.py:385-393).  logz arrays [B,H,W] with element stride `stride`
+ * (3 for the z channel of a point map); out may alias cur or refined. */
+int pmg_output_gate(const float* cur_logz, const float* refined_logz, float* out_logz, int64_t stride,
+                    const float* lidar, const float* conf, int32_t B, int32_t H, int32_t W, int32_t h, int32_t w,
+                    double floor_v, void* stream);
+
+/* Elastic anchor (v3.py:570-573): with `state` = pmg_fit_solve of the logz's _lidar_in_affine_frame fit,
+ * logz += (beta * c * ok) * (log d_aff - logz) in place. */
+int pmg_anchor_apply(float* logz, int64_t stride, const float* lidar, const float* conf, const pmg_fit_state* state,
+                     int32_t B, int32_t H, int32_t W, int32_t h, int32_t w, float beta, void* stream);
+
 /* --------------------------------------------------------------------------------------------------------------
  * The fused refiner: one plan per (model geometry, batch); all K steps captured in one CUDA graph.
  * Replaces the refine loop of MoGeModel.forward (v3.py:537-576) with _refine_logz / _voxelize / Sparse3DUNet /
@@ -373,6 +386,9 @@ typedef struct pmg_refiner_config {
     int32_t use_tensor_cores;   /* 1: tcgen05 int8 kernels where the shape allows; 0: SIMT dp4a everywhere */
     int32_t max_split;          /* split-K limit for the wide convs of small levels (0 or 1 = off); results are
                                    identical for every value (exact int32 partial sums) */
+    int32_t output_gate;        /* 1: refiner output gate (v3.py:565-569), off in the released configs */
+    float anchor_beta;          /* > 0: elastic anchor strength (v3.py:570-573), 0 in the released configs */
+    double output_gate_floor;   /* the gate's floor (the reference's default 0.1) */
 } pmg_refiner_config;
 
 int pmg_refiner_create(const pmg_refiner_config* cfg, pmg_refiner** out);

@@ -182,9 +182,44 @@ def pool_mean(x: np.ndarray, seg_indices: np.ndarray, seg_offsets: np.ndarray) -
     return (out / np.maximum(cnt, 1).astype(f32)[:, None]).astype(f32)
 
 
-def refine_step(model, point_coord, lidar_depth, lidar_conf, encoder_feature, uv_bias, trace=None, res=256.0):
+def lidar_uncertainty(H, W, lidar_depth, lidar_conf):
+    """MoGeModel._lidar_uncertainty (v3.py:385-393): u = 1 - c (1 - clamp((d - 3) / 2, 0, 1)) on the nearest-resized
+    sensor, 1 where it has no value.  [B, H, W] fp32."""
+    from .fit import nearest_resize
+    d = nearest_resize(np.asarray(lidar_depth, f32), H, W)[:, 0]
+    c = np.clip((nearest_resize(np.asarray(lidar_conf, f32), H, W)[:, 0] / f32(2.0)).astype(f32), f32(0), f32(1))
+    with np.errstate(invalid="ignore"):
+        valid = np.isfinite(d) & (d > 0)
+        rng = np.clip(((d - f32(3.0)) / f32(2.0)).astype(f32), f32(0), f32(1))
+    u = (f32(1.0) - (c * (f32(1.0) - rng).astype(f32)).astype(f32)).astype(f32)
+    return np.where(valid, u, f32(1.0)).astype(f32)
+
+
+def refiner_gates(cur_logz, new_logz, lidar_depth, lidar_conf, output_gate_floor=None, anchor_beta=0.0):
+    """The optional refiner-side gates of the refine loop (v3.py:565-573): the output gate scales the update by
+    floor + (1 - floor) u; the elastic anchor relaxes toward the re-aligned LiDAR, logz += beta gate (log_d_aff -
+    logz) with a hard gate (a fresh fit on the gated logz).  fp32 in the reference's order."""
+    from .fit import lidar_in_affine_frame
+    cur = np.asarray(cur_logz, f32)
+    new = np.asarray(new_logz, f32)
+    B, H, W = new.shape
+    if output_gate_floor is not None:
+        u = lidar_uncertainty(H, W, lidar_depth, lidar_conf)
+        fl = float(output_gate_floor)
+        g = (f32(fl) + (f32(1.0 - fl) * u).astype(f32)).astype(f32)
+        new = (cur + (g * (new - cur).astype(f32)).astype(f32)).astype(f32)
+    if anchor_beta > 0:
+        log_d_aff, gate, _, _ = lidar_in_affine_frame(new, lidar_depth, lidar_conf, soft_gate=False)
+        bg = (f32(anchor_beta) * gate).astype(f32)
+        new = (new + (bg * (log_d_aff - new).astype(f32)).astype(f32)).astype(f32)
+    return new
+
+
+def refine_step(model, point_coord, lidar_depth, lidar_conf, encoder_feature, uv_bias, trace=None, res=256.0,
+                output_gate_floor=None, anchor_beta=0.0):
     """One step of the refine loop (v3.py:547-576 with the soft-gated LiDAR residual): fit -> prompt feats ->
-    voxelise -> U-Net -> logz += delta.  Returns (new point_coord, info)."""
+    voxelise -> U-Net -> logz += delta (-> the optional output gate and elastic anchor).  Returns (new point_coord,
+    info)."""
     from . import fit as fitmod
     pc = np.asarray(point_coord, f32)
     B, H, W, _ = pc.shape
@@ -194,6 +229,8 @@ def refine_step(model, point_coord, lidar_depth, lidar_conf, encoder_feature, uv
     levels, pools = structure.build_levels(coords, shape, model.factors)
     out = model.forward(feats, pf, levels, pools, encoder_feature, uv_bias, trace)
     new_logz = (logz + out[:, 0].reshape(B, H, W)).astype(f32)
+    if output_gate_floor is not None or anchor_beta > 0:
+        new_logz = refiner_gates(logz, new_logz, lidar_depth, lidar_conf, output_gate_floor, anchor_beta)
     new_pc = pc.copy()
     new_pc[..., 2] = new_logz
     return new_pc, dict(s=s, t=t, prompt_feats=pf, levels=levels, pools=pools, delta=out[:, 0], shape=shape)

@@ -28,7 +28,8 @@ class RefinerConfig(C.Structure):
     _fields_ = [("batch", I32), ("height", I32), ("width", I32), ("levels", I32), ("channels", I32 * 8),
                 ("enc_channels", I32), ("lidar_h", I32), ("lidar_w", I32), ("depth_resolution", F32),
                 ("soft_gate", I32), ("fit_iters", I32), ("fit_trim", F32), ("fit_min_points", I32),
-                ("use_prompt", I32), ("capacity", I64 * 8), ("use_tensor_cores", I32), ("max_split", I32)]
+                ("use_prompt", I32), ("capacity", I64 * 8), ("use_tensor_cores", I32), ("max_split", I32),
+                ("output_gate", I32), ("anchor_beta", F32), ("output_gate_floor", C.c_double)]
 
 
 # name -> (restype, argtypes)
@@ -55,6 +56,8 @@ SIGNATURES = {
     "pmg_focal_shift": (I32, [P, P, P, I32, I32, I32, I32, I32, P, P, P]),
     "pmg_shift_depth": (I32, [P, P, I32, I32, I32, P, P]),
     "pmg_depth_to_points": (I32, [P, P, I32, I32, I32, P, P, P, P]),
+    "pmg_output_gate": (I32, [P, P, P, I64, P, P, I32, I32, I32, I32, I32, C.c_double, P]),
+    "pmg_anchor_apply": (I32, [P, I64, P, P, P, I32, I32, I32, I32, I32, F32, P]),
     "pmg_spconv_i8": (I32, [P, I64, P, I64, P, P, I64, I32, I32, P, P, P, F32, I32, F32, P, P, I32, P, P]),
     "pmg_spconv_i8_split_workspace_bytes": (SZ, [I64, I32, I32]),
     "pmg_spconv_i8_split": (I32, [P, I64, P, I64, P, P, I64, I32, I32, P, P, P, F32, I32, F32, P, P, I32, P, SZ, P, P]),

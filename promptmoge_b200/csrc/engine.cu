@@ -29,6 +29,10 @@ int fit_prep_prompt(const float* logz, int64_t stride, const float* lidar, const
                     int h, int w, float* z, float* y, uint8_t* flags, cudaStream_t s);
 int prompt_feats(const float* logz, int64_t stride, const float* lidar, const float* conf, const pmg_fit_state* st,
                  int B, int H, int W, int h, int w, int soft, float* out, cudaStream_t s);
+int output_gate(const float* cur, const float* refined, float* out, int64_t stride, const float* lidar,
+                const float* conf, int B, int H, int W, int h, int w, double floor_v, cudaStream_t s);
+int anchor_apply(float* logz, int64_t stride, const float* lidar, const float* conf, const pmg_fit_state* st, int B,
+                 int H, int W, int h, int w, float beta, cudaStream_t s);
 }  // namespace pmg
 
 using namespace pmg;
@@ -97,6 +101,8 @@ struct pmg_refiner {
     float* fy = nullptr;           // fit target
     uint8_t* fflags = nullptr;
     pmg_fit_state* fst = nullptr;  // [B]
+    pmg_fit_state* fst2 = nullptr; // [B] the elastic anchor's fit
+    float* pc_next = nullptr;      // [N][3] the refined map before the output gate
     void* fit_ws = nullptr;
     size_t fit_ws_bytes = 0;
     int32_t* zq = nullptr;         // [N]
@@ -206,6 +212,8 @@ int allocate(pmg_refiner* r) {
     PMG_TRY(alloc(r, &r->fy, r->N));
     PMG_TRY(alloc(r, &r->fflags, r->N));
     PMG_TRY(alloc(r, &r->fst, B));
+    if (c.anchor_beta > 0.f) PMG_TRY(alloc(r, &r->fst2, B));
+    if (c.output_gate) PMG_TRY(alloc(r, &r->pc_next, r->N * 3));
     r->fit_ws_bytes = fit_workspace_bytes(B, (int64_t)c.height * c.width);
     PMG_TRY(alloc(r, reinterpret_cast<char**>(&r->fit_ws), r->fit_ws_bytes));
     PMG_CUDA_TRY(cudaMemset(r->fit_ws, 0, r->fit_ws_bytes));
@@ -426,7 +434,23 @@ int enqueue_step(pmg_refiner* r, cudaStream_t s) {
         PMG_TRY(resblock(r, t, r->up[i], ls.uc, lt.parent, s, nl, feeds_up ? lt.uq : nullptr,
                          feeds_up ? r->upl[i + 1].sa : 0.f));
     }
-    LAUNCH(out_apply(l0.S, r->N, l0.C, r->out_proj.w, r->out_proj.b, r->pc, r->pc, r->delta, s));
+    const bool gate = c.output_gate && r->lidar && r->conf;
+    LAUNCH(out_apply(l0.S, r->N, l0.C, r->out_proj.w, r->out_proj.b, r->pc, gate ? r->pc_next : r->pc, r->delta, s));
+    // --- optional refiner-side gates (v3.py:565-573) -------------------------------------------------------------- //
+    if (gate)
+        LAUNCH(output_gate(r->pc + 2, r->pc_next + 2, r->pc + 2, 3, r->lidar, r->conf, B, H, W, c.lidar_h, c.lidar_w,
+                           c.output_gate_floor, s));
+    if (c.anchor_beta > 0.f && r->lidar && r->conf) {
+        LAUNCH(fit_prep_prompt(r->pc + 2, 3, r->lidar, r->conf, B, H, W, c.lidar_h, c.lidar_w, r->fz, r->fy,
+                               r->fflags, s));
+        size_t nclr = 0;
+        void* clr = fit_clear_region(r->fit_ws, B, (int64_t)H * W, &nclr);
+        PMG_CUDA_TRY(cudaMemsetAsync(clr, 0, nclr, s));
+        PMG_TRY(fit_solve(r->fz, r->fy, r->fflags, B, (int64_t)H * W, c.fit_iters, c.fit_trim, c.fit_min_points,
+                          r->fst2, r->fit_ws, s));
+        nl += 4 * c.fit_iters + 1;
+        LAUNCH(anchor_apply(r->pc + 2, 3, r->lidar, r->conf, r->fst2, B, H, W, c.lidar_h, c.lidar_w, c.anchor_beta, s));
+    }
     r->launches = nl;
     return PMG_OK;
 }

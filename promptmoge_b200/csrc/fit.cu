@@ -386,6 +386,71 @@ void* fit_clear_region(void* ws, int B, int64_t N, size_t* bytes) {
     return p;
 }
 
+// Refiner output gate (v3.py:565-569): u = 1 - c (1 - clamp((d - 3) / 2, 0, 1)) on the nearest-resized sensor
+// (1 where it has no value, v3.py:385-393), g = floor + (1 - floor) u, logz = cur + g (refined - cur).  Reads the
+// step's input logz `cur` and the refined logz, writes the gated logz (strided point-map channel 2).
+__global__ void k_output_gate(const float* __restrict__ cur, const float* __restrict__ refined, float* __restrict__ out,
+                              int64_t stride, const float* __restrict__ lidar, const float* __restrict__ conf, int B,
+                              int H, int W, int h, int w, float sy, float sx, float floor_v, float one_minus_floor) {
+    const int64_t N = (int64_t)B * H * W;
+    for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < N; m += (int64_t)gridDim.x * blockDim.x) {
+        const int b = (int)(m / ((int64_t)H * W));
+        const int rem = (int)(m - (int64_t)b * H * W);
+        const int i = rem / W, j = rem - (rem / W) * W;
+        const int64_t l = ((int64_t)b * h + nearest_src(i, H, h, sy)) * w + nearest_src(j, W, w, sx);
+        const float d = lidar[l];
+        const float c = fminf(fmaxf(__fdiv_rn(conf[l], 2.0f), 0.0f), 1.0f);
+        const bool valid = isfinite(d) && d > 0.0f;
+        const float rng = fminf(fmaxf(__fdiv_rn(__fsub_rn(d, 3.0f), 2.0f), 0.0f), 1.0f);
+        const float u = valid ? __fsub_rn(1.0f, __fmul_rn(c, __fsub_rn(1.0f, rng))) : 1.0f;
+        const float g = __fadd_rn(floor_v, __fmul_rn(one_minus_floor, u));
+        const float c0 = cur[m * stride], r0 = refined[m * stride];
+        out[m * stride] = __fadd_rn(c0, __fmul_rn(g, __fsub_rn(r0, c0)));
+    }
+}
+
+// Elastic anchor (v3.py:570-573): with a fresh fit state of the gated logz (hard gate c * ok), logz += (beta * gate) *
+// (log_d_aff - logz).
+__global__ void k_anchor_apply(float* __restrict__ logz, int64_t stride, const float* __restrict__ lidar,
+                               const float* __restrict__ conf, const pmg_fit_state* __restrict__ st, int B, int H,
+                               int W, int h, int w, float sy, float sx, float beta) {
+    const int64_t N = (int64_t)B * H * W;
+    for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < N; m += (int64_t)gridDim.x * blockDim.x) {
+        const int b = (int)(m / ((int64_t)H * W));
+        const int rem = (int)(m - (int64_t)b * H * W);
+        const int i = rem / W, j = rem - (rem / W) * W;
+        const int64_t l = ((int64_t)b * h + nearest_src(i, H, h, sy)) * w + nearest_src(j, W, w, sx);
+        const float d = lidar[l];
+        const float c = fminf(fmaxf(__fdiv_rn(conf[l], 2.0f), 0.0f), 1.0f);
+        const bool valid = isfinite(d) && d > 0.0f;
+        const float s = st[b].s, t = st[b].t;
+        const float d_aff = __fdiv_rn(__fsub_rn(d, t), fmaxf(s, 1e-6f));
+        const bool ok = valid && d_aff > 1e-4f;
+        const float lz = logz[m * stride];
+        const float log_d_aff = ok ? logf(fmaxf(d_aff, 1e-4f)) : lz;
+        const float gate = __fmul_rn(c, ok ? 1.0f : 0.0f);
+        logz[m * stride] = __fadd_rn(lz, __fmul_rn(__fmul_rn(beta, gate), __fsub_rn(log_d_aff, lz)));
+    }
+}
+
+int output_gate(const float* cur, const float* refined, float* out, int64_t stride, const float* lidar,
+                const float* conf, int B, int H, int W, int h, int w, double floor_v, cudaStream_t s) {
+    const float sy = (float)h / (float)H, sx = (float)w / (float)W;
+    k_output_gate<<<grid_for((int64_t)B * H * W), 256, 0, s>>>(cur, refined, out, stride, lidar, conf, B, H, W, h, w,
+                                                               sy, sx, (float)floor_v, (float)(1.0 - floor_v));
+    PMG_LAUNCH_CHECK();
+    return PMG_OK;
+}
+
+int anchor_apply(float* logz, int64_t stride, const float* lidar, const float* conf, const pmg_fit_state* st, int B,
+                 int H, int W, int h, int w, float beta, cudaStream_t s) {
+    const float sy = (float)h / (float)H, sx = (float)w / (float)W;
+    k_anchor_apply<<<grid_for((int64_t)B * H * W), 256, 0, s>>>(logz, stride, lidar, conf, st, B, H, W, h, w, sy, sx,
+                                                                beta);
+    PMG_LAUNCH_CHECK();
+    return PMG_OK;
+}
+
 int fit_prep_prompt(const float* logz, int64_t stride, const float* lidar, const float* conf, int B, int H, int W,
                     int h, int w, float* z, float* y, uint8_t* flags, cudaStream_t s) {
     const float sy = (float)h / (float)H, sx = (float)w / (float)W;
@@ -452,4 +517,22 @@ extern "C" int pmg_apply_affine(float* depth, const pmg_fit_state* state, int32_
     k_apply_affine<<<grid_for((int64_t)B * N), 256, 0, as_stream(stream)>>>(depth, state, B, N);
     PMG_LAUNCH_CHECK();
     return PMG_OK;
+}
+
+extern "C" int pmg_output_gate(const float* cur_logz, const float* refined_logz, float* out_logz, int64_t stride,
+                               const float* lidar, const float* conf, int32_t B, int32_t H, int32_t W, int32_t h,
+                               int32_t w, double floor_v, void* stream) {
+    if (!cur_logz || !refined_logz || !out_logz || !lidar || !conf || B <= 0 || H <= 0 || W <= 0 || h <= 0 || w <= 0 ||
+        stride < 1)
+        return PMG_ERR_BAD_ARG;
+    return output_gate(cur_logz, refined_logz, out_logz, stride, lidar, conf, B, H, W, h, w, floor_v,
+                       as_stream(stream));
+}
+
+extern "C" int pmg_anchor_apply(float* logz, int64_t stride, const float* lidar, const float* conf,
+                                const pmg_fit_state* state, int32_t B, int32_t H, int32_t W, int32_t h, int32_t w,
+                                float beta, void* stream) {
+    if (!logz || !lidar || !conf || !state || B <= 0 || H <= 0 || W <= 0 || h <= 0 || w <= 0 || stride < 1)
+        return PMG_ERR_BAD_ARG;
+    return anchor_apply(logz, stride, lidar, conf, state, B, H, W, h, w, beta, as_stream(stream));
 }

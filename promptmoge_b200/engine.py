@@ -83,7 +83,8 @@ class RefinerEngine:
     """Device-resident int8 refiner.  All tensors it returns live on `device`."""
 
     def __init__(self, weights: dict, clips: dict, geometry: Geometry, device="cuda", capacity=None,
-                 use_prompt: bool = True, tensor_cores: bool = True, max_split: int = 4):
+                 use_prompt: bool = True, tensor_cores: bool = True, max_split: int = 4,
+                 output_gate_floor: float | None = None, anchor_beta: float = 0.0):
         _lib.load()
         self.geo = geometry
         self.device = torch.device(device)
@@ -101,6 +102,11 @@ class RefinerEngine:
         cfg.use_prompt = int(use_prompt)
         cfg.use_tensor_cores = int(tensor_cores)
         cfg.max_split = int(max_split)
+        # the optional refiner-side gates (off in the released configs): refiner_output_gate / output_gate_floor,
+        # anchor_strength (moge/model/v3.py:116-118, 565-573)
+        cfg.output_gate = int(output_gate_floor is not None)
+        cfg.output_gate_floor = float(output_gate_floor) if output_gate_floor is not None else 0.1
+        cfg.anchor_beta = float(anchor_beta)
         for k in range(L):
             cfg.capacity[k] = int(capacity[k]) if capacity is not None else 0
         self._cfg = cfg

@@ -413,3 +413,31 @@ def build_prompt(depth: torch.Tensor, conf: torch.Tensor, out_hw, conf_levels: f
     call("pmg_build_prompt", _p(depth), _p(conf), B, h, w, H, W, float(conf_levels), _p(prompt), _p(mu), _p(ws),
          nbytes, _stream())
     return prompt, {"mu": mu}
+
+
+# ----------------------------------------------------------------------------------------------------------------- #
+# Optional refiner-side gates (moge/model/v3.py:565-573)
+# ----------------------------------------------------------------------------------------------------------------- #
+def output_gate(cur_logz, refined_logz, lidar, conf, floor: float = 0.1):
+    """cur + g (refined - cur), g = floor + (1 - floor) u (the refiner output gate).  logz [B,H,W]."""
+    cur = _dev(cur_logz.contiguous(), torch.float32, "cur_logz")
+    ref = _dev(refined_logz.contiguous(), torch.float32, "refined_logz")
+    out = torch.empty_like(ref)
+    B, H, W = ref.shape
+    h, w = lidar.shape[-2:]
+    call("pmg_output_gate", _p(cur), _p(ref), _p(out), 1, _p(lidar.contiguous()), _p(conf.contiguous()), B, H, W, h,
+         w, float(floor), _stream())
+    return out
+
+
+def anchor(logz, lidar, conf, beta: float, iters: int = 4, trim: float = 0.2, min_points: int = 32):
+    """The elastic anchor: a fresh _lidar_in_affine_frame fit of logz, then logz + beta gate (log d_aff - logz)."""
+    lz = _dev(logz.contiguous(), torch.float32, "logz")
+    z, y, fl = fit_prep_prompt(lz, lidar.contiguous(), conf.contiguous())
+    st = fit_solve(z, y, fl, iters=iters, trim=trim, min_points=min_points)
+    out = lz.clone()
+    B, H, W = lz.shape
+    h, w = lidar.shape[-2:]
+    call("pmg_anchor_apply", _p(out), 1, _p(lidar.contiguous()), _p(conf.contiguous()), _p(st), B, H, W, h, w,
+         float(beta), _stream())
+    return out

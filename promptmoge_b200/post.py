@@ -118,3 +118,41 @@ def postprocess(coords: torch.Tensor, image_hw, lidar_depth: torch.Tensor, lidar
 
 
 __all__ = ["normalized_view_plane_uv", "resize_remap", "recover_focal_shift", "intrinsics_from_focal", "postprocess"]
+
+
+class PostGraph:
+    """postprocess captured once into a CUDA graph for fixed shapes (one launch per frame batch instead of a dozen
+    kernel launches and allocations from Python); run() copies the inputs into the graph's static buffers and
+    replays it.  The returned tensors are the graph's static outputs (overwritten by the next run)."""
+
+    def __init__(self, batch: int, coords_hw, image_hw, lidar_hw=(192, 256), masked: bool = False,
+                 gauge_poly: int = 2, device="cuda"):
+        dev = torch.device(device)
+        h, w = coords_hw
+        lh, lw = lidar_hw
+        self.coords = torch.zeros((batch, h, w, 3), dtype=torch.float32, device=dev)
+        self.lidar = torch.ones((batch, 1, lh, lw), dtype=torch.float32, device=dev)
+        self.conf = torch.full((batch, 1, lh, lw), 2.0, dtype=torch.float32, device=dev)
+        self.mask = torch.ones((batch, image_hw[0], image_hw[1]), dtype=torch.bool, device=dev) if masked else None
+        self.image_hw = tuple(image_hw)
+        self.gauge_poly = gauge_poly
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            self._run()                                   # warm-up: attributes set, allocator primed
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = self._run()
+
+    def _run(self):
+        return postprocess(self.coords, self.image_hw, self.lidar, self.conf, self.mask, gauge_poly=self.gauge_poly)
+
+    def run(self, coords, lidar_depth, lidar_conf, mask=None) -> dict:
+        self.coords.copy_(coords, non_blocking=True)
+        self.lidar.copy_(lidar_depth, non_blocking=True)
+        self.conf.copy_(lidar_conf, non_blocking=True)
+        if self.mask is not None:
+            self.mask.copy_(mask, non_blocking=True)
+        self.graph.replay()
+        return self.out

@@ -113,3 +113,16 @@ def test_postprocess_equals_oracle(masked, gauge):
     np.testing.assert_allclose(p[fin], points[fin], rtol=1e-4 if gauge else 1e-5, atol=1e-6)
     K = out["intrinsics"].cpu().numpy()
     assert K.shape == (2, 3, 3) and np.allclose(K[:, :2, 2], 0.5)
+
+
+def test_post_graph_equals_eager():
+    from promptmoge_b200 import post, synth
+    sc = synth.make_scene(9, 240, 320, 8, 256, batch=1)
+    c = torch.from_numpy(sc.point_coord.astype(np.float32)).cuda()
+    ld, lc = torch.from_numpy(sc.lidar_depth).cuda(), torch.from_numpy(sc.lidar_conf).cuda()
+    eager = post.postprocess(c, (480, 640), ld, lc)
+    pg = post.PostGraph(1, (240, 320), (480, 640))
+    for _ in range(2):
+        got = pg.run(c, ld, lc)
+        for k in ("points", "depth", "focal", "shift", "metric_fit"):
+            assert torch.equal(got[k], eager[k]), k
