@@ -70,13 +70,13 @@ def solve_shift(uv: np.ndarray, xyz: np.ndarray, focal: float | None = None, ite
         if not (jj > 0.0):
             break
         step = -rj / (jj + lam)
+        if abs(step) <= 1e-12 * max(1.0, abs(s)):
+            break
         c2, rj2, jj2 = terms(s + step)
         if np.isfinite(c2) and c2 <= cost:
             s += step
             cost, rj, jj = c2, rj2, jj2
             lam *= 0.25
-            if abs(step) <= 1e-12 * max(1.0, abs(s)):
-                break
         else:
             lam = max(lam * 8.0, 1e-6 * jj)
     shift = f32(s)

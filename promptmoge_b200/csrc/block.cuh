@@ -39,17 +39,26 @@ static __device__ uint32_t block_select(const uint32_t* rb, int n, uint32_t k, u
         const int nb = 1 << nbits;
         for (int i = threadIdx.x; i < kSelectBins; i += blockDim.x) hist[i] = 0;
         __syncthreads();
-        for (int p = threadIdx.x; p < n_pad; p += blockDim.x) {
-            int bin = -1;
-            if (p < n) {
-                const uint32_t bits = rb[p];
+        // four keys per thread per round, loads first (several loads in flight per thread); every lane of a warp
+        // runs every match (out-of-range keys take bin -1)
+        for (int base = 0; base < n_pad; base += 4 * blockDim.x) {
+            uint32_t kv[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int p = base + u * blockDim.x + threadIdx.x;
+                kv[u] = p < n ? rb[p] : 0xFFFFFFFFu;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                int bin = -1;
+                const uint32_t bits = kv[u];
                 if (bits != 0xFFFFFFFFu) {
                     const uint32_t hi = pass == 0 ? 0u : bits >> (shift + nbits);
                     if (hi == prefix) bin = (int)((bits >> shift) & (uint32_t)(nb - 1));
                 }
+                const unsigned peers = __match_any_sync(0xffffffffu, bin);
+                if (bin >= 0 && lane == __ffs(peers) - 1) atomicAdd(&hist[bin], (uint32_t)__popc(peers));
             }
-            const unsigned peers = __match_any_sync(0xffffffffu, bin);
-            if (bin >= 0 && lane == __ffs(peers) - 1) atomicAdd(&hist[bin], (uint32_t)__popc(peers));
         }
         __syncthreads();
         const int per = nb / (int)blockDim.x;   // 4 or 2 bins per thread

@@ -1,7 +1,8 @@
 // Per-frame polynomial prompt gauge: MoGeModel.prompt_gauge_poly (moge/model/v3.py:151-183), applied after the
 // refinement when promptmoge.infer runs with gauge_poly > 0 (v3.py:841-846, promptmoge/model.py:77).
 //
-// One CTA of 512 threads per frame does the whole fit on the sensor grid (h x w, 49 152 pixels at 192 x 256):
+// A prep kernel over every sensor pixel of every frame, then one CTA of 512 threads per frame for the fit on the
+// sensor grid (h x w, 49 152 pixels at 192 x 256):
 //   prep     the prediction's depth area-averaged onto the sensor grid over finite positive pixels (two area means,
 //            each summed in row order and divided by the window height then width, as aten's adaptive average pool
 //            does), the confident mask conf >= 2 & lidar > 0 & z_lr > 0 and y = log(max(lidar, 1e-3)) -
@@ -61,22 +62,14 @@ struct GaugeArgs {
 };
 
 
-__global__ void __launch_bounds__(kGaugeThreads) k_gauge_fit(GaugeArgs a) {
-    const int b = blockIdx.x;
-    const int n_px = a.h * a.w;
-    float* y = a.y + (int64_t)b * n_px;
-    uint8_t* mk = a.mask + (int64_t)b * n_px;
-    uint32_t* rb = a.rbits + (int64_t)b * n_px;
-    const float* depth = a.depth + (int64_t)b * a.H * a.W;
-    __shared__ double sd[32];
-    __shared__ int si[33];
-    __shared__ double red[kGaugeThreads / 32][27];
-    __shared__ uint32_t hist[kGaugeBins];
-    __shared__ float s_coef[6];
-    __shared__ int s_ok;
-    // ---- prep: sensor-grid depth, mask, log ratio ---- //
-    int cnt = 0;
-    for (int p = threadIdx.x; p < n_px; p += blockDim.x) {
+// Prep, one thread per sensor pixel over all frames: the prediction's depth area-averaged onto the sensor grid over
+// finite positive pixels, the confident mask and the log ratio y.
+__global__ void k_gauge_prep(GaugeArgs a) {
+    const int64_t n_px = (int64_t)a.h * a.w, total = (int64_t)a.B * n_px;
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+        const int b = (int)(e / n_px);
+        const int p = (int)(e - (int64_t)b * n_px);
+        const float* depth = a.depth + (int64_t)b * a.H * a.W;
         const int oh = p / a.w, ow = p - oh * a.w;
         const int h0 = (int)(((int64_t)oh * a.H) / a.h), h1 = (int)(((int64_t)(oh + 1) * a.H + a.h - 1) / a.h);
         const int w0 = (int)(((int64_t)ow * a.W) / a.w), w1 = (int)(((int64_t)(ow + 1) * a.W + a.w - 1) / a.w);
@@ -92,12 +85,41 @@ __global__ void __launch_bounds__(kGaugeThreads) k_gauge_fit(GaugeArgs a) {
         num = __fdiv_rn(__fdiv_rn(num, kh), kw);
         den = __fdiv_rn(__fdiv_rn(den, kh), kw);
         const float z_lr = den > 0.5f ? __fdiv_rn(num, fmaxf(den, 1e-6f)) : 0.0f;
-        const float ld = a.lidar[(int64_t)b * n_px + p];
-        const float cf = a.conf ? a.conf[(int64_t)b * n_px + p] : 2.0f;
+        const float ld = a.lidar[e];
+        const float cf = a.conf ? a.conf[e] : 2.0f;
         const bool m = cf >= 2.0f && ld > 0.0f && z_lr > 0.0f;
-        y[p] = m ? __fsub_rn(logf(fmaxf(ld, 1e-3f)), logf(fmaxf(z_lr, 1e-3f))) : 0.0f;
-        mk[p] = m ? 1 : 0;
-        cnt += m ? 1 : 0;
+        a.y[e] = m ? __fsub_rn(logf(fmaxf(ld, 1e-3f)), logf(fmaxf(z_lr, 1e-3f))) : 0.0f;
+        a.mask[e] = m ? 1 : 0;
+    }
+}
+
+// Per-pixel passes over a frame's sensor grid run kUnroll pixels per thread per round, all loads first, so each
+// thread keeps several loads in flight (a one-pixel-at-a-time loop waits out the L2 latency per pixel); a thread still
+// visits its pixels in increasing order, so the float64 sums are the same.
+constexpr int kUnroll = 8;
+
+__global__ void __launch_bounds__(kGaugeThreads) k_gauge_fit(GaugeArgs a) {
+    const int b = blockIdx.x;
+    const int n_px = a.h * a.w;
+    float* y = a.y + (int64_t)b * n_px;
+    uint8_t* mk = a.mask + (int64_t)b * n_px;
+    uint32_t* rb = a.rbits + (int64_t)b * n_px;
+    __shared__ double sd[32];
+    __shared__ int si[33];
+    __shared__ double red[kGaugeThreads / 32][27];
+    __shared__ uint32_t hist[kGaugeBins];
+    __shared__ float s_coef[6];
+    __shared__ int s_ok;
+    int cnt = 0;
+    for (int base = 0; base < n_px; base += kUnroll * blockDim.x) {
+        uint8_t mv[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const int p = base + u * blockDim.x + threadIdx.x;
+            mv[u] = p < n_px ? mk[p] : 0;
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) cnt += mv[u];
     }
     const int n = (int)block_sum((double)cnt, sd);
     if (n < 200) {
@@ -116,24 +138,39 @@ __global__ void __launch_bounds__(kGaugeThreads) k_gauge_fit(GaugeArgs a) {
         double acc[27];
 #pragma unroll
         for (int q = 0; q < 27; ++q) acc[q] = 0.0;
-        for (int p = threadIdx.x; p < n_px; p += blockDim.x) {
-            if (!mk[p]) continue;
-            const int oh = p / a.w, ow = p - oh * a.w;
-            float av[6];
-            gauge_basis(lin11(ow, a.w), lin11(oh, a.h), a.degree, av);
-            float wgt = 1.0f;
-            if (it > 0) wgt = fminf(__fdiv_rn(__fmul_rn(2.0f, sc), fmaxf(__uint_as_float(rb[p]), 1e-6f)), 1.0f);
-            float wa[6];
+        for (int base = 0; base < n_px; base += kUnroll * blockDim.x) {
+            uint8_t mv[kUnroll];
+            float yv[kUnroll];
+            uint32_t rv[kUnroll];
 #pragma unroll
-            for (int i = 0; i < 6; ++i) wa[i] = __fmul_rn(av[i], wgt);
-            const double wy = (double)__fmul_rn(y[p], wgt);
-            int q = 0;
+            for (int u = 0; u < kUnroll; ++u) {
+                const int p = base + u * blockDim.x + threadIdx.x;
+                const bool in = p < n_px;
+                mv[u] = in ? mk[p] : 0;
+                yv[u] = in ? y[p] : 0.0f;
+                rv[u] = (in && it > 0) ? rb[p] : 0u;
+            }
 #pragma unroll
-            for (int i = 0; i < 6; ++i)
+            for (int u = 0; u < kUnroll; ++u) {
+                if (!mv[u]) continue;
+                const int p = base + u * blockDim.x + threadIdx.x;
+                const int oh = p / a.w, ow = p - oh * a.w;
+                float av[6];
+                gauge_basis(lin11(ow, a.w), lin11(oh, a.h), a.degree, av);
+                float wgt = 1.0f;
+                if (it > 0) wgt = fminf(__fdiv_rn(__fmul_rn(2.0f, sc), fmaxf(__uint_as_float(rv[u]), 1e-6f)), 1.0f);
+                float wa[6];
 #pragma unroll
-                for (int j = i; j < 6; ++j) acc[q++] += (double)wa[i] * (double)wa[j];
+                for (int i = 0; i < 6; ++i) wa[i] = __fmul_rn(av[i], wgt);
+                const double wy = (double)__fmul_rn(yv[u], wgt);
+                int q = 0;
 #pragma unroll
-            for (int i = 0; i < 6; ++i) acc[21 + i] += (double)wa[i] * wy;
+                for (int i = 0; i < 6; ++i)
+#pragma unroll
+                    for (int j = i; j < 6; ++j) acc[q++] += (double)wa[i] * (double)wa[j];
+#pragma unroll
+                for (int i = 0; i < 6; ++i) acc[21 + i] += (double)wa[i] * wy;
+            }
         }
         const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
 #pragma unroll
@@ -194,15 +231,29 @@ __global__ void __launch_bounds__(kGaugeThreads) k_gauge_fit(GaugeArgs a) {
         __syncthreads();
         if (!s_ok || it + 1 == a.iters) break;   // the last solve's residuals are not used
         // ---- residuals, lower median of |r|, next weights' scale ---- //
-        for (int p = threadIdx.x; p < n_px; p += blockDim.x) {
-            uint32_t bits = 0xFFFFFFFFu;
-            if (mk[p]) {
-                const int oh = p / a.w, ow = p - oh * a.w;
-                float av[6];
-                gauge_basis(lin11(ow, a.w), lin11(oh, a.h), a.degree, av);
-                bits = __float_as_uint(fabsf(__fsub_rn(y[p], gauge_poly(av, s_coef, nc))));
+        for (int base = 0; base < n_px; base += kUnroll * blockDim.x) {
+            uint8_t mv[kUnroll];
+            float yv[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int p = base + u * blockDim.x + threadIdx.x;
+                const bool in = p < n_px;
+                mv[u] = in ? mk[p] : 0;
+                yv[u] = in ? y[p] : 0.0f;
             }
-            rb[p] = bits;
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int p = base + u * blockDim.x + threadIdx.x;
+                if (p >= n_px) break;
+                uint32_t bits = 0xFFFFFFFFu;
+                if (mv[u]) {
+                    const int oh = p / a.w, ow = p - oh * a.w;
+                    float av[6];
+                    gauge_basis(lin11(ow, a.w), lin11(oh, a.h), a.degree, av);
+                    bits = __float_as_uint(fabsf(__fsub_rn(yv[u], gauge_poly(av, s_coef, nc))));
+                }
+                rb[p] = bits;
+            }
         }
         __syncthreads();
         const uint32_t med = block_select(rb, n_px, (uint32_t)((n - 1) / 2 + 1), hist, si);
@@ -284,6 +335,9 @@ extern "C" int pmg_gauge_poly(const float* depth, const float* lidar, const floa
     p += (size_t)B * n_px * sizeof(uint32_t);
     a.mask = reinterpret_cast<uint8_t*>(p);
     const cudaStream_t s = as_stream(stream);
+    const int64_t prep = (int64_t)B * n_px;
+    k_gauge_prep<<<(int)std::max<int64_t>(1, std::min<int64_t>((prep + 255) / 256, (int64_t)kNumSMs * 8)), 256, 0, s>>>(a);
+    PMG_LAUNCH_CHECK();
     k_gauge_fit<<<B, kGaugeThreads, 0, s>>>(a);
     PMG_LAUNCH_CHECK();
     if (corr || depth_out || points) {

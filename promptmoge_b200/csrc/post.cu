@@ -181,6 +181,9 @@ __global__ void __launch_bounds__(kFsThreads) k_focal_shift(FsArgs a) {
     for (int it = 0; it < 100; ++it) {
         if (!(jj > 0.0)) break;
         const double step = -rj / (jj + lam);
+        // converged: the next step no longer moves s (near the minimiser a rounding-level cost increase would
+        // otherwise reject every step until the iteration limit)
+        if (fabs(step) <= 1e-12 * fmax(1.0, fabs(s))) break;
         double c2, rj2, jj2;
         terms(s + step, c2, rj2, jj2);
         if (isfinite(c2) && c2 <= cost) {
@@ -189,7 +192,6 @@ __global__ void __launch_bounds__(kFsThreads) k_focal_shift(FsArgs a) {
             rj = rj2;
             jj = jj2;
             lam *= 0.25;
-            if (fabs(step) <= 1e-12 * fmax(1.0, fabs(s))) break;
         } else {
             lam = fmax(lam * 8.0, 1e-6 * jj);
         }

@@ -31,6 +31,7 @@ constexpr int kColTile = 32;        // columns per k_fill_cols CTA
 constexpr int kRowSegs = 32;        // row segments per column
 constexpr int kRowThreads = 256;
 constexpr int kMuThreads = 1024;
+constexpr size_t kMuSmemKeys = 200 * 1024;     // dynamic shared memory for one frame's keys (+8.5 KB static)
 constexpr uint32_t kNone = 0xFFFFFFFFu;
 
 __device__ __forceinline__ bool present(float d) { return d > 0.0f; }     // NaN compares false
@@ -172,31 +173,54 @@ __device__ __forceinline__ float conf_frac(float c, float levels) {
 
 __global__ void __launch_bounds__(kMuThreads) k_prompt_mu(const float* __restrict__ depth,
                                                           const float* __restrict__ conf, int64_t n_px, float levels,
-                                                          uint32_t* __restrict__ keys, float* __restrict__ mu) {
+                                                          uint32_t* __restrict__ keys, float* __restrict__ mu,
+                                                          int keys_in_smem) {
     __shared__ uint32_t hist[kSelectBins];
     __shared__ int scan_sm[33];
     __shared__ int sum_sm[32];
+    extern __shared__ uint32_t s_keys[];        // the frame's keys when they fit (a sensor frame: 192 KB)
     const int b = blockIdx.x;
     const float* d = depth + (int64_t)b * n_px;
     const float* c = conf + (int64_t)b * n_px;
-    uint32_t* kb = keys + (int64_t)b * n_px;
+    uint32_t* kb = keys_in_smem ? s_keys : keys + (int64_t)b * n_px;
+    // four pixels per thread per round, loads first, so several loads are in flight per thread
     int nv = 0, nh = 0;
-    for (int64_t p = threadIdx.x; p < n_px; p += blockDim.x) {
-        const float dv = d[p];
-        if (prompt_valid(dv)) {
-            ++nv;
-            nh += conf_frac(c[p], levels) >= 0.999f;
+    for (int64_t base = 0; base < n_px; base += 4 * (int64_t)blockDim.x) {
+        float dv[4], cv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t p = base + u * blockDim.x + threadIdx.x;
+            dv[u] = p < n_px ? d[p] : 0.0f;
+            cv[u] = p < n_px ? c[p] : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            if (prompt_valid(dv[u])) {
+                ++nv;
+                nh += conf_frac(cv[u], levels) >= 0.999f;
+            }
         }
     }
     nv = block_sum(nv, sum_sm);
     nh = block_sum(nh, sum_sm);
     const bool use_hi = nh > 0;
     const int n = use_hi ? nh : nv;
-    for (int64_t p = threadIdx.x; p < n_px; p += blockDim.x) {
-        const float dv = d[p];
-        const bool v = prompt_valid(dv);
-        const bool sel = v && (!use_hi || conf_frac(c[p], levels) >= 0.999f);
-        kb[p] = sel ? f2key(logf(dv)) : kNone;
+    for (int64_t base = 0; base < n_px; base += 4 * (int64_t)blockDim.x) {
+        float dv[4], cv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t p = base + u * blockDim.x + threadIdx.x;
+            dv[u] = p < n_px ? d[p] : 0.0f;
+            cv[u] = p < n_px ? c[p] : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t p = base + u * blockDim.x + threadIdx.x;
+            if (p >= n_px) break;
+            const bool v = prompt_valid(dv[u]);
+            const bool sel = v && (!use_hi || conf_frac(cv[u], levels) >= 0.999f);
+            kb[p] = sel ? f2key(logf(dv[u])) : kNone;
+        }
     }
     __syncthreads();
     float m = 0.0f;
@@ -287,7 +311,13 @@ extern "C" int pmg_build_prompt(const float* depth, const float* conf, int32_t B
     if (n_px >= INT32_MAX || !(conf_levels > 0.0f) || workspace_bytes < prompt_ws(B, n_px)) return PMG_ERR_BAD_ARG;
     uint32_t* keys = reinterpret_cast<uint32_t*>(ws_base(workspace));
     const cudaStream_t s = as_stream(stream);
-    k_prompt_mu<<<B, kMuThreads, 0, s>>>(depth, conf, n_px, conf_levels, keys, mu);
+    // the select's three passes read the keys from shared memory when a frame's keys fit beside the histogram
+    const size_t key_bytes = (size_t)n_px * sizeof(uint32_t);
+    const bool in_smem = key_bytes <= kMuSmemKeys;
+    if (in_smem) PMG_CUDA_TRY(cudaFuncSetAttribute(k_prompt_mu, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                    (int)kMuSmemKeys));
+    k_prompt_mu<<<B, kMuThreads, in_smem ? key_bytes : 0, s>>>(depth, conf, n_px, conf_levels, keys, mu,
+                                                                in_smem ? 1 : 0);
     PMG_LAUNCH_CHECK();
     const int64_t total = (int64_t)B * H * W;
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, (int64_t)kNumSMs * 8));
