@@ -97,6 +97,7 @@ __global__ void k_gauge_prep(GaugeArgs a) {
 // thread keeps several loads in flight (a one-pixel-at-a-time loop waits out the L2 latency per pixel); a thread still
 // visits its pixels in increasing order, so the float64 sums are the same.
 constexpr int kUnroll = 8;
+constexpr int kGaugeGridMax = 1024;   // sensor grids up to this many rows and columns use shared linspace tables
 
 __global__ void __launch_bounds__(kGaugeThreads) k_gauge_fit(GaugeArgs a) {
     const int b = blockIdx.x;
@@ -110,6 +111,17 @@ __global__ void __launch_bounds__(kGaugeThreads) k_gauge_fit(GaugeArgs a) {
     __shared__ uint32_t hist[kGaugeBins];
     __shared__ float s_coef[6];
     __shared__ int s_ok;
+    // the linspace coordinates of the sensor grid's columns and rows, computed once (each is an IEEE divide and a
+    // fused multiply-add) instead of per pixel and pass
+    __shared__ float s_lu[kGaugeGridMax], s_lv[kGaugeGridMax];
+    const bool tables = a.w <= kGaugeGridMax && a.h <= kGaugeGridMax;
+    if (tables) {
+        for (int i = threadIdx.x; i < a.w; i += blockDim.x) s_lu[i] = lin11(i, a.w);
+        for (int i = threadIdx.x; i < a.h; i += blockDim.x) s_lv[i] = lin11(i, a.h);
+    }
+    __syncthreads();
+    auto lu = [&](int i) { return tables ? s_lu[i] : lin11(i, a.w); };
+    auto lv = [&](int i) { return tables ? s_lv[i] : lin11(i, a.h); };
     int cnt = 0;
     for (int base = 0; base < n_px; base += kUnroll * blockDim.x) {
         uint8_t mv[kUnroll];
@@ -156,7 +168,7 @@ __global__ void __launch_bounds__(kGaugeThreads) k_gauge_fit(GaugeArgs a) {
                 const int p = base + u * blockDim.x + threadIdx.x;
                 const int oh = p / a.w, ow = p - oh * a.w;
                 float av[6];
-                gauge_basis(lin11(ow, a.w), lin11(oh, a.h), a.degree, av);
+                gauge_basis(lu(ow), lv(oh), a.degree, av);
                 float wgt = 1.0f;
                 if (it > 0) wgt = fminf(__fdiv_rn(__fmul_rn(2.0f, sc), fmaxf(__uint_as_float(rv[u]), 1e-6f)), 1.0f);
                 float wa[6];
@@ -249,7 +261,7 @@ __global__ void __launch_bounds__(kGaugeThreads) k_gauge_fit(GaugeArgs a) {
                 if (mv[u]) {
                     const int oh = p / a.w, ow = p - oh * a.w;
                     float av[6];
-                    gauge_basis(lin11(ow, a.w), lin11(oh, a.h), a.degree, av);
+                    gauge_basis(lu(ow), lv(oh), a.degree, av);
                     bits = __float_as_uint(fabsf(__fsub_rn(yv[u], gauge_poly(av, s_coef, nc))));
                 }
                 rb[p] = bits;
