@@ -185,7 +185,7 @@ def run_ours(args, ws, rank, local):
     mdl = synth.MODELS[args.model]
     weights, clips = synthetic_model(args.model, 0)
     batch = args.batch
-    ref = Refiner(weights, clips, args.model, batch=batch, device=dev, max_split=args.max_split)
+    ref = Refiner(weights, clips, args.model, batch=batch, device=dev, max_split=args.max_split, pdl=not args.no_pdl)
     sc = synth.make_scene(1000 * rank, mdl["H"], mdl["W"], mdl["encoder_downsample"], mdl["model_channels"][-1],
                           batch=batch)
     h_pc, h_ld, h_lc = pinned(sc.point_coord), pinned(sc.lidar_depth), pinned(sc.lidar_conf)
@@ -649,6 +649,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--K", type=int, default=1, help="refine steps per graph (the workload's K)")
     ap.add_argument("--batch", type=int, default=1, help="frames per GPU per step")
+    ap.add_argument("--no-pdl", action="store_true",
+                    help="ordinary instead of programmatic kernel-to-kernel edges in the step graph")
     ap.add_argument("--max-split", type=int, default=4,
                     help="split-K limit of the plan's wide convs of levels with fewer tiles than SMs (1 = off)")
     ap.add_argument("--no-cpu-baseline", action="store_true")

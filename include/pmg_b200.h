@@ -389,6 +389,8 @@ typedef struct pmg_refiner_config {
     int32_t output_gate;        /* 1: refiner output gate (v3.py:565-569), off in the released configs */
     float anchor_beta;          /* > 0: elastic anchor strength (v3.py:570-573), 0 in the released configs */
     double output_gate_floor;   /* the gate's floor (the reference's default 0.1) */
+    int32_t use_pdl;            /* 1: the captured step graph's kernel-to-kernel edges are programmatic (each kernel
+                                   is scheduled while its predecessor finishes and waits for it on the device) */
 } pmg_refiner_config;
 
 int pmg_refiner_create(const pmg_refiner_config* cfg, pmg_refiner** out);

@@ -29,7 +29,7 @@ class RefinerConfig(C.Structure):
                 ("enc_channels", I32), ("lidar_h", I32), ("lidar_w", I32), ("depth_resolution", F32),
                 ("soft_gate", I32), ("fit_iters", I32), ("fit_trim", F32), ("fit_min_points", I32),
                 ("use_prompt", I32), ("capacity", I64 * 8), ("use_tensor_cores", I32), ("max_split", I32),
-                ("output_gate", I32), ("anchor_beta", F32), ("output_gate_floor", C.c_double)]
+                ("output_gate", I32), ("anchor_beta", F32), ("output_gate_floor", C.c_double), ("use_pdl", I32)]
 
 
 # name -> (restype, argtypes)

@@ -22,6 +22,13 @@ void set_cuda_error(cudaError_t e);
 
 #define PMG_LAUNCH_CHECK() PMG_CUDA_TRY(cudaGetLastError())
 
+// Programmatic dependent launch.  Every kernel of the library starts by waiting until the kernels it depends on have
+// completed and their memory is visible.  In a captured step graph whose kernel-to-kernel edges are programmatic, the
+// next kernel's launch is then prepared while this one runs and released when it completes (the implicit trigger at
+// exit: an explicit early trigger let waiting CTAs of the next kernel sit beside the issue-bound convs and measured
+// slower).  A no-op in a launch without a programmatic dependency (standalone calls, ordinary graph edges).
+__device__ __forceinline__ void pdl_begin() { cudaGridDependencySynchronize(); }
+
 constexpr int kTaps = 27;
 constexpr int kNumSMs = 148;
 

@@ -612,6 +612,31 @@ extern "C" int pmg_refiner_enqueue(pmg_refiner* r, int32_t K, float* point_coord
     return enqueue_run(r, K, point_coord_out, fit_out, as_stream(stream));
 }
 
+// Turn every kernel-to-kernel edge of a captured graph into a programmatic one: the downstream kernel's launch is
+// prepared while the upstream kernel runs, and the downstream kernel waits on the device (pdl_begin) for the upstream
+// kernel to complete before touching memory.  Edges that involve a memset, a copy or an event stay ordinary.
+static int programmatic_edges(cudaGraph_t g) {
+    size_t n = 0;
+    PMG_CUDA_TRY(cudaGraphGetEdges_v2(g, nullptr, nullptr, nullptr, &n));
+    if (n == 0) return PMG_OK;
+    std::vector<cudaGraphNode_t> from(n), to(n);
+    std::vector<cudaGraphEdgeData> ed(n);
+    PMG_CUDA_TRY(cudaGraphGetEdges_v2(g, from.data(), to.data(), ed.data(), &n));
+    for (size_t i = 0; i < n; ++i) {
+        cudaGraphNodeType ta, tb;
+        PMG_CUDA_TRY(cudaGraphNodeGetType(from[i], &ta));
+        PMG_CUDA_TRY(cudaGraphNodeGetType(to[i], &tb));
+        if (ta != cudaGraphNodeTypeKernel || tb != cudaGraphNodeTypeKernel) continue;
+        if (ed[i].type != cudaGraphDependencyTypeDefault || ed[i].from_port != cudaGraphKernelNodePortDefault) continue;
+        PMG_CUDA_TRY(cudaGraphRemoveDependencies_v2(g, &from[i], &to[i], &ed[i], 1));
+        cudaGraphEdgeData pe = {};
+        pe.from_port = cudaGraphKernelNodePortProgrammatic;
+        pe.type = cudaGraphDependencyTypeProgrammatic;
+        PMG_CUDA_TRY(cudaGraphAddDependencies_v2(g, &from[i], &to[i], &pe, 1));
+    }
+    return PMG_OK;
+}
+
 extern "C" int pmg_refiner_capture(pmg_refiner* r, int32_t K, float* point_coord_out, pmg_fit_state* fit_out,
                                    void* stream) {
     (void)stream;
@@ -630,6 +655,13 @@ extern "C" int pmg_refiner_capture(pmg_refiner* r, int32_t K, float* point_coord
         return rc;
     }
     PMG_CUDA_TRY(e);
+    if (r->cfg.use_pdl) {
+        const int prc = programmatic_edges(g);
+        if (prc != PMG_OK) {
+            cudaGraphDestroy(g);
+            return prc;
+        }
+    }
     const cudaError_t ie = cudaGraphInstantiate(&r->exec, g, 0);
     cudaGraphDestroy(g);
     PMG_CUDA_TRY(ie);

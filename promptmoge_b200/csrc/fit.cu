@@ -31,6 +31,7 @@ __device__ __forceinline__ int nearest_src(int dst, int out, int in, float scale
 __global__ void k_fit_prep_prompt(const float* __restrict__ logz, int64_t stride, const float* __restrict__ lidar,
                                   const float* __restrict__ conf, int B, int H, int W, int h, int w, float sy, float sx,
                                   float* __restrict__ z, float* __restrict__ target, uint8_t* __restrict__ flags) {
+    pdl_begin();
     const int64_t N = (int64_t)B * H * W;
     for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < N; m += (int64_t)gridDim.x * blockDim.x) {
         const int b = (int)(m / ((int64_t)H * W));
@@ -54,6 +55,7 @@ __global__ void k_fit_prep_final(const float* __restrict__ depth, const float* _
                                  const float* __restrict__ lidar, const float* __restrict__ conf, int B, int H, int W,
                                  int h, int w, float* __restrict__ z, float* __restrict__ target,
                                  uint8_t* __restrict__ flags) {
+    pdl_begin();
     const int64_t N = (int64_t)B * h * w;
     for (int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; p < N; p += (int64_t)gridDim.x * blockDim.x) {
         const int b = (int)(p / ((int64_t)h * w));
@@ -104,6 +106,7 @@ constexpr int kFitPer = 4;   // elements per thread and sweep (loads issued toge
 // Sums over the current weights (iteration 0: the mask; later: mask & r <= thr with the residuals cached by the
 // previous iteration's first select pass), then the last CTA of the frame solves.  gridDim = (nblk, B).
 __global__ void __launch_bounds__(kFitThreads) k_fit_sums(FitArgs a, int iter) {
+    pdl_begin();
     const int b = blockIdx.y;
     pmg_fit_state* st = a.st + b;
     const float* z = a.z + (int64_t)b * a.N;
@@ -198,6 +201,7 @@ __global__ void __launch_bounds__(kFitThreads) k_fit_sums(FitArgs a, int iter) {
 // One radix pass of the k-th smallest r over the masked points.  pass 0: bits 31..21 (and caches every masked
 // point's r for the later passes and the next sums), 1: 20..10, 2: 9..0.
 __global__ void __launch_bounds__(kFitThreads) k_fit_select(FitArgs a, int pass) {
+    pdl_begin();
     const int b = blockIdx.y;
     pmg_fit_state* st = a.st + b;
     if (st->k > st->count) {          // the k-th value is one of the +inf fill values: thr = inf (w = mask)
@@ -303,6 +307,7 @@ __global__ void __launch_bounds__(kFitThreads) k_fit_select(FitArgs a, int pass)
 __global__ void k_prompt_feats(const float* __restrict__ logz, int64_t stride, const float* __restrict__ lidar,
                                const float* __restrict__ conf, const pmg_fit_state* __restrict__ st, int B, int H,
                                int W, int h, int w, float sy, float sx, int soft, float* __restrict__ out) {
+    pdl_begin();
     const int64_t N = (int64_t)B * H * W;
     for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < N; m += (int64_t)gridDim.x * blockDim.x) {
         const int b = (int)(m / ((int64_t)H * W));
@@ -326,6 +331,7 @@ __global__ void k_prompt_feats(const float* __restrict__ logz, int64_t stride, c
 }
 
 __global__ void k_apply_affine(float* __restrict__ depth, const pmg_fit_state* __restrict__ st, int B, int64_t N) {
+    pdl_begin();
     const int64_t total = (int64_t)B * N;
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
         const int b = (int)(e / N);
@@ -392,6 +398,7 @@ void* fit_clear_region(void* ws, int B, int64_t N, size_t* bytes) {
 __global__ void k_output_gate(const float* __restrict__ cur, const float* __restrict__ refined, float* __restrict__ out,
                               int64_t stride, const float* __restrict__ lidar, const float* __restrict__ conf, int B,
                               int H, int W, int h, int w, float sy, float sx, float floor_v, float one_minus_floor) {
+    pdl_begin();
     const int64_t N = (int64_t)B * H * W;
     for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < N; m += (int64_t)gridDim.x * blockDim.x) {
         const int b = (int)(m / ((int64_t)H * W));
@@ -414,6 +421,7 @@ __global__ void k_output_gate(const float* __restrict__ cur, const float* __rest
 __global__ void k_anchor_apply(float* __restrict__ logz, int64_t stride, const float* __restrict__ lidar,
                                const float* __restrict__ conf, const pmg_fit_state* __restrict__ st, int B, int H,
                                int W, int h, int w, float sy, float sx, float beta) {
+    pdl_begin();
     const int64_t N = (int64_t)B * H * W;
     for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < N; m += (int64_t)gridDim.x * blockDim.x) {
         const int b = (int)(m / ((int64_t)H * W));

@@ -65,6 +65,7 @@ struct GaugeArgs {
 // Prep, one thread per sensor pixel over all frames: the prediction's depth area-averaged onto the sensor grid over
 // finite positive pixels, the confident mask and the log ratio y.
 __global__ void k_gauge_prep(GaugeArgs a) {
+    pdl_begin();
     const int64_t n_px = (int64_t)a.h * a.w, total = (int64_t)a.B * n_px;
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
         const int b = (int)(e / n_px);
@@ -100,6 +101,7 @@ constexpr int kUnroll = 8;
 constexpr int kGaugeGridMax = 1024;   // sensor grids up to this many rows and columns use shared linspace tables
 
 __global__ void __launch_bounds__(kGaugeThreads) k_gauge_fit(GaugeArgs a) {
+    pdl_begin();
     const int b = blockIdx.x;
     const int n_px = a.h * a.w;
     float* y = a.y + (int64_t)b * n_px;
@@ -283,6 +285,7 @@ __global__ void __launch_bounds__(kGaugeThreads) k_gauge_fit(GaugeArgs a) {
 __global__ void k_gauge_apply(const float* __restrict__ out, int B, int H, int W, int degree, float* __restrict__ corr,
                               const float* __restrict__ depth_in, float* __restrict__ depth_out,
                               float* __restrict__ points) {
+    pdl_begin();
     const int64_t total = (int64_t)B * H * W;
     const int nc = degree < 2 ? 3 : 6;
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {

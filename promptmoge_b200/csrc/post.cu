@@ -30,6 +30,7 @@ __device__ __forceinline__ float bilinear_src(int dst, float scale) {
 
 __global__ void k_resize_remap(const float* __restrict__ coords, int B, int h, int w, int H, int W,
                                float* __restrict__ points) {
+    pdl_begin();
     const float sh = __fdiv_rn((float)h, (float)H), sw = __fdiv_rn((float)w, (float)W);
     const int64_t total = (int64_t)B * H * W;
     for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
@@ -98,6 +99,7 @@ __device__ __forceinline__ double block_sum_d(double v, double* sm) {
 }
 
 __global__ void __launch_bounds__(kFsThreads) k_focal_shift(FsArgs a) {
+    pdl_begin();
     extern __shared__ float s_smp[];     // [n][5]: x, y, z, u, v of the kept samples in raster order
     __shared__ double red[32];
     __shared__ int scan_sm[33];
@@ -219,6 +221,7 @@ __global__ void __launch_bounds__(kFsThreads) k_focal_shift(FsArgs a) {
 
 __global__ void k_shift_depth(const float* __restrict__ points, const float* __restrict__ shift, int B, int64_t HW,
                               float* __restrict__ depth) {
+    pdl_begin();
     const int64_t total = (int64_t)B * HW;
     for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x)
         depth[t] = __fadd_rn(points[t * 3 + 2], shift[t / HW]);
@@ -227,6 +230,7 @@ __global__ void k_shift_depth(const float* __restrict__ points, const float* __r
 __global__ void k_depth_points(const float* __restrict__ depth, const float* __restrict__ focal, int B, int H, int W,
                                float diag, float aspect, const uint8_t* __restrict__ mask, float* __restrict__ points,
                                float* __restrict__ depth_out) {
+    pdl_begin();
     const int64_t HW = (int64_t)H * W, total = (int64_t)B * HW;
     for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
         const int b = (int)(t / HW);

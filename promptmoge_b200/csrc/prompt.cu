@@ -38,6 +38,7 @@ __device__ __forceinline__ bool present(float d) { return d > 0.0f; }     // NaN
 
 __global__ void __launch_bounds__(kColTile * kRowSegs) k_fill_cols(const float* __restrict__ depth, int h, int w,
                                                                      int* __restrict__ near, int* __restrict__ count) {
+    pdl_begin();
     __shared__ int s_last[kRowSegs][kColTile + 1];
     __shared__ int s_first[kRowSegs][kColTile + 1];
     const int tx = threadIdx.x & (kColTile - 1), ty = threadIdx.x / kColTile;
@@ -106,6 +107,7 @@ __global__ void __launch_bounds__(kRowThreads) k_fill_rows(const float* __restri
                                                            const float* __restrict__ conf, int h, int w,
                                                            const int* __restrict__ near, const int* __restrict__ count,
                                                            float* __restrict__ depth_out, float* __restrict__ conf_out) {
+    pdl_begin();
     extern __shared__ uint32_t s_g[];      // [w] squared row distance of each column's candidate (kNone: none)
     int* s_row = reinterpret_cast<int*>(s_g + w);
     const int i = blockIdx.x, b = blockIdx.y;
@@ -175,6 +177,7 @@ __global__ void __launch_bounds__(kMuThreads) k_prompt_mu(const float* __restric
                                                           const float* __restrict__ conf, int64_t n_px, float levels,
                                                           uint32_t* __restrict__ keys, float* __restrict__ mu,
                                                           int keys_in_smem) {
+    pdl_begin();
     __shared__ uint32_t hist[kSelectBins];
     __shared__ int scan_sm[33];
     __shared__ int sum_sm[32];
@@ -238,6 +241,7 @@ __device__ __forceinline__ int nearest_src(int dst, int in, int out, float scale
 
 __global__ void k_prompt_emit(const float* __restrict__ depth, const float* __restrict__ conf, int B, int h, int w,
                               int H, int W, float levels, const float* __restrict__ mu, float* __restrict__ prompt) {
+    pdl_begin();
     const int64_t plane = (int64_t)H * W;
     const int64_t total = (int64_t)B * plane;
     const float sh = __fdiv_rn((float)h, (float)H), sw = __fdiv_rn((float)w, (float)W);

@@ -16,6 +16,7 @@
 namespace pmg {
 
 __global__ void k_quantize(const float* __restrict__ x, int64_t n, float s, int8_t* __restrict__ q) {
+    pdl_begin();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         q[i] = (int8_t)quant8(x[i], s);
 }
@@ -27,6 +28,7 @@ __global__ void k_ln_silu_q8(const float* __restrict__ x, const float* __restric
                              float* __restrict__ x_out, const int32_t* __restrict__ count, int64_t max_rows, int C,
                              const float* __restrict__ gamma, const float* __restrict__ beta, double eps, float scale,
                              int8_t* __restrict__ q) {
+    pdl_begin();
     const int64_t M = rows_of(count, max_rows);
     const int lane = threadIdx.x & 31;
     const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -83,6 +85,7 @@ template <bool QUANT>
 __global__ void k_pool_mean(const float* __restrict__ x, const int32_t* __restrict__ seg_idx,
                             const int32_t* __restrict__ seg_off, const int32_t* __restrict__ count, int64_t max_rows,
                             int C, float scale, int8_t* __restrict__ q, float* __restrict__ out, bool mean) {
+    pdl_begin();
     const int64_t M = rows_of(count, max_rows);
     const int64_t total = M * C;
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
@@ -99,6 +102,7 @@ __global__ void k_pool_mean(const float* __restrict__ x, const int32_t* __restri
 
 __global__ void k_gather_rows(const float* __restrict__ x, const int32_t* __restrict__ parent,
                               const int32_t* __restrict__ count, int64_t max_rows, int C, float* __restrict__ out) {
+    pdl_begin();
     const int64_t M = rows_of(count, max_rows);
     const int64_t total = M * C;
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
@@ -112,6 +116,7 @@ __global__ void k_gather_rows(const float* __restrict__ x, const int32_t* __rest
 __global__ void k_concat_q8(const float* __restrict__ x, const float* __restrict__ enc_tok,
                             const int32_t* __restrict__ col, const int32_t* __restrict__ count, int64_t max_rows,
                             int C, float scale, int8_t* __restrict__ q) {
+    pdl_begin();
     const int64_t M = rows_of(count, max_rows);
     const int64_t total = M * 2 * C;
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
@@ -125,6 +130,7 @@ __global__ void k_concat_q8(const float* __restrict__ x, const float* __restrict
 // Token grid prep: planar fp16 encoder feature [B][K][T] -> int8 rows [B*T][K]; planar fp32 UV bias [B][C][T] ->
 // rows [B*T][C].
 __global__ void k_tokens_q8(const __half* __restrict__ f, int B, int K, int T, float scale, int8_t* __restrict__ q) {
+    pdl_begin();
     const int64_t total = (int64_t)B * K * T;
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
         const int64_t bt = e / K;
@@ -135,6 +141,7 @@ __global__ void k_tokens_q8(const __half* __restrict__ f, int B, int K, int T, f
 }
 
 __global__ void k_planar_to_rows(const float* __restrict__ f, int B, int C, int T, float* __restrict__ out) {
+    pdl_begin();
     const int64_t total = (int64_t)B * C * T;
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
         const int64_t bt = e / C;
@@ -148,6 +155,7 @@ __global__ void k_planar_to_rows(const float* __restrict__ f, int B, int C, int 
 __global__ void k_input_proj(const float* __restrict__ pc, const float* __restrict__ prompt, int64_t N, int C,
                              const float* __restrict__ wi, const float* __restrict__ bi, const float* __restrict__ wp,
                              const float* __restrict__ bp, float* __restrict__ x0) {
+    pdl_begin();
     const int64_t total = N * C;
     for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
         const int64_t m = e / C;
@@ -170,6 +178,7 @@ __global__ void k_input_proj(const float* __restrict__ pc, const float* __restri
 __global__ void k_out_apply(const float* __restrict__ x, int64_t N, int C, const float* __restrict__ wo,
                             const float* __restrict__ bo, const float* __restrict__ pc_in, float* __restrict__ pc_out,
                             float* __restrict__ delta_out) {
+    pdl_begin();
     const int lane = threadIdx.x & 31;
     const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
     for (int64_t m = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; m < N; m += warps) {
@@ -248,6 +257,7 @@ __global__ void __launch_bounds__(256) k_ln_silu_rows(const float* __restrict__ 
                                                       const int32_t* __restrict__ count, int64_t max_rows,
                                                       const float* __restrict__ gamma, const float* __restrict__ beta,
                                                       double eps, float scale, int8_t* __restrict__ q) {
+    pdl_begin();
     constexpr int G = RowMap<C>::G, RPB = RowMap<C>::RPB;
     const float inv_s = 1.0f / scale;
     __shared__ float sg[C], sb[C];
@@ -342,6 +352,7 @@ __global__ void __launch_bounds__(256) k_pool_mean_rows_q(const float* __restric
                                                           const int32_t* __restrict__ count, int64_t max_rows,
                                                           float scale, int8_t* __restrict__ q, float* __restrict__ out,
                                                           bool mean) {
+    pdl_begin();
     pool_mean_rows<C, true>(x, seg_idx, seg_off, count, max_rows, scale, q, out, mean);
 }
 
@@ -351,6 +362,7 @@ __global__ void __launch_bounds__(256) k_pool_mean_rows_f(const float* __restric
                                                           const int32_t* __restrict__ count, int64_t max_rows,
                                                           float scale, int8_t* __restrict__ q, float* __restrict__ out,
                                                           bool mean) {
+    pdl_begin();
     pool_mean_rows<C, false>(x, seg_idx, seg_off, count, max_rows, scale, q, out, mean);
 }
 
@@ -359,6 +371,7 @@ __global__ void __launch_bounds__(256) k_input_proj_rows(const float* __restrict
                                                          int64_t N, const float* __restrict__ wi,
                                                          const float* __restrict__ bi, const float* __restrict__ wp,
                                                          const float* __restrict__ bp, float* __restrict__ x0) {
+    pdl_begin();
     constexpr int G = RowMap<C>::G, RPB = RowMap<C>::RPB;
     __shared__ float s_wi[3 * C], s_bi[C], s_wp[2 * C], s_bp[C];
     for (int i = threadIdx.x; i < C; i += blockDim.x) {
@@ -405,6 +418,7 @@ __global__ void __launch_bounds__(256) k_out_apply_rows(const float* __restrict_
                                                         const float* __restrict__ wo, const float* __restrict__ bo,
                                                         const float* __restrict__ pc_in, float* __restrict__ pc_out,
                                                         float* __restrict__ delta_out) {
+    pdl_begin();
     constexpr int G = RowMap<C>::G, RPB = RowMap<C>::RPB;
     __shared__ float s_wo[C];
     for (int i = threadIdx.x; i < C; i += blockDim.x) s_wo[i] = wo[i];

@@ -45,6 +45,7 @@ __global__ void __launch_bounds__(kThreads) k_gemm_i8_simt(const int8_t* __restr
                                                        int64_t ld, const uint32_t* __restrict__ tile_mask,
                                                        const int32_t* __restrict__ count, int64_t max_rows, int Ci,
                                                        int taps, const int8_t* __restrict__ w, Epi e) {
+    pdl_begin();
     constexpr int RN = CO / 16;
     constexpr int KS = kKC + 16;   // row stride in bytes (keeps 16-byte alignment, staggers banks)
     __shared__ __align__(16) int8_t sA[kTM * KS];
@@ -168,6 +169,7 @@ __global__ void __launch_bounds__(256) k_spconv_f32(const float* __restrict__ in
                                                    const int32_t* __restrict__ count, int64_t max_rows, int Ci, int Co,
                                                    const float* __restrict__ w, const float* __restrict__ bias,
                                                    float* __restrict__ out) {
+    pdl_begin();
     extern __shared__ float sm_f[];
     float* sX = sm_f;                 // 32 x Ci
     const int64_t M = rows_of(count, max_rows);

@@ -69,6 +69,7 @@ template <int NT, int W>
 __global__ void __launch_bounds__(kThreads, 1)
     k_conv_grid0(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const uint32_t* __restrict__ lanes, int B, int H, int Wd, Epi e) {
+    pdl_begin();
     using C = GCfg<NT, W>;
     constexpr int NS = C::kStages;
     constexpr int NCOLS = tmem_cols<NT>();
@@ -329,6 +330,7 @@ int conv_grid0_tc(const int8_t* in, const uint32_t* lanes, int B, int H, int W, 
 
 __global__ void __launch_bounds__(256) k_l0_tap_lanes(const int32_t* __restrict__ zq, int B, int H, int W,
                                                       uint32_t* __restrict__ lanes) {
+    pdl_begin();
     const int64_t N = (int64_t)B * H * W;
     const int64_t groups = (N + 127) / 128 * 4;
     const int lane = threadIdx.x & 31;

@@ -93,6 +93,7 @@ __device__ __noinline__ uint32_t split_taps(uint32_t mk, int tpi, int ks, int S)
 // the conv ran unsplit (the same split_count over the same grid said 1).
 __global__ void __launch_bounds__(256) k_split_epilogue(Epi e, const int32_t* __restrict__ count, int64_t max_rows,
                                                         int Co, int NT, int conv_grid) {
+    pdl_begin();
     const int64_t M = rows_of(count, max_rows);
     const int64_t ntile = (M + kM - 1) / kM;
     const int S = split_count(ntile * (Co / NT), e.nsplit, conv_grid);
@@ -129,6 +130,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int8_t* __restrict__ in, int64_t in_rows, const int32_t* __restrict__ nmap, int64_t ld,
               const uint32_t* __restrict__ tile_mask, const int32_t* __restrict__ count, int64_t max_rows, int Ci,
               int Co, int taps, Epi e) {
+    pdl_begin();
     using C = Cfg<KIND, NT, W, RES>;
     constexpr int NST = C::kStages;
     constexpr int NCOLS = tmem_cols<NT>();

@@ -31,6 +31,7 @@ __device__ __forceinline__ int zq_of(const float* pc, int64_t pix, float res) {
 __global__ void k_voxelize_l0(const float* __restrict__ pc, int B, int H, int W, float res, int32_t* __restrict__ zq,
                               int32_t* __restrict__ zmin, int32_t* __restrict__ zmax, int32_t* __restrict__ nmap,
                               int64_t ld, uint32_t* __restrict__ tile_mask) {
+    pdl_begin();
     const int64_t N = (int64_t)B * H * W;
     const int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const bool live = m < N;
@@ -82,6 +83,7 @@ __global__ void k_voxelize_l0(const float* __restrict__ pc, int B, int H, int W,
 
 __global__ void k_l0_coords(const int32_t* __restrict__ zq, const int32_t* __restrict__ zmin, int B, int H, int W,
                             int4* __restrict__ coords) {
+    pdl_begin();
     const int64_t N = (int64_t)B * H * W;
     const int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (m >= N) return;
@@ -123,6 +125,7 @@ constexpr int kPoolThreads = 256;
 __global__ void k_pool_count(int B, int Hf, int Wf, int Hc, int Wc, const int32_t* __restrict__ fcs,
                              const int32_t* __restrict__ fz, const int32_t* __restrict__ zmin,
                              int32_t* __restrict__ cnt, int32_t* __restrict__ fcnt, int2* __restrict__ bsum) {
+    pdl_begin();
     __shared__ int sm[33];
     const int64_t ncol = (int64_t)B * Hc * Wc;
     const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -157,6 +160,7 @@ __global__ void k_pool_count(int B, int Hf, int Wf, int Hc, int Wc, const int32_
 // CSR sentinels and the overflow flag.
 __global__ void k_pool_scan(int nb, int2* __restrict__ bsum, int64_t ncol, int64_t cap, int32_t* __restrict__ count,
                             int32_t* __restrict__ ccs, int32_t* __restrict__ seg_offsets, int32_t* __restrict__ status) {
+    pdl_begin();
     __shared__ int sm[33];
     __shared__ int carry_n, carry_f;
     if (threadIdx.x == 0) { carry_n = 0; carry_f = 0; }
@@ -190,6 +194,7 @@ __global__ void k_pool_emit(int B, int Hf, int Wf, int Hc, int Wc, const int32_t
                             int32_t* __restrict__ ccol, int32_t* __restrict__ ccs, int4* __restrict__ ccoords,
                             int32_t* __restrict__ parent, int32_t* __restrict__ seg_indices,
                             int32_t* __restrict__ seg_offsets) {
+    pdl_begin();
     __shared__ int sm[33];
     const int64_t ncol = (int64_t)B * Hc * Wc;
     const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -240,6 +245,7 @@ __global__ void k_nmap_frames(int B, int H, int W, const int32_t* __restrict__ c
                               const int32_t* __restrict__ z, const int32_t* __restrict__ col,
                               const int32_t* __restrict__ cs, int32_t* __restrict__ nmap, int64_t ld,
                               uint32_t* __restrict__ tile_mask) {
+    pdl_begin();
     const int64_t M = rows_of(count, max_rows);
     const int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if ((o & ~31LL) >= M) return;     // whole warp past the end
@@ -314,6 +320,7 @@ __device__ __forceinline__ bool linear_key(int b, int x, int y, int z, const Ext
 // leader claims it with a CAS; a full bucket moves the probe to the next one.  Bounded by the bucket count.
 __global__ void k_hash_insert(const int4* __restrict__ coords, int64_t M, Extents ex, uint64_t* __restrict__ keys,
                               int32_t* __restrict__ vals, int64_t nbuckets, int32_t* __restrict__ status) {
+    pdl_begin();
     const int lane = threadIdx.x & 31;
     const int g = lane >> 3, gl = lane & 7;
     const unsigned gmask = 0xffu << (g * 8);
@@ -380,6 +387,7 @@ __device__ __forceinline__ int32_t hash_find(uint64_t key, const uint64_t* __res
 __global__ void k_hash_nmap(const int4* __restrict__ coords, int64_t M, Extents ex, const uint64_t* __restrict__ keys,
                             const int32_t* __restrict__ vals, int64_t nbuckets, int32_t* __restrict__ nmap,
                             int64_t ld, int row_major, uint32_t* __restrict__ tile_mask) {
+    pdl_begin();
     const int lane = threadIdx.x & 31;
     const int g = lane >> 3, gl = lane & 7;
     const unsigned gmask = 0xffu << (g * 8);
@@ -483,6 +491,7 @@ extern "C" int pmg_pool_frames(int32_t B, int32_t Hf, int32_t Wf, const int32_t*
 // entry is written exactly once.  Out-of-range or out-of-order voxels set PMG_ERR_RANGE and write nothing.
 __global__ void k_frame_csr(const int32_t* __restrict__ coords, int64_t M, int B, int H, int W, int64_t Z,
                             int32_t* __restrict__ col_start, int32_t* __restrict__ z_out, int32_t* __restrict__ status) {
+    pdl_begin();
     const int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (m > M) return;
     const int64_t ncol = (int64_t)B * H * W;

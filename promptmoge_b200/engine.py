@@ -84,7 +84,7 @@ class RefinerEngine:
 
     def __init__(self, weights: dict, clips: dict, geometry: Geometry, device="cuda", capacity=None,
                  use_prompt: bool = True, tensor_cores: bool = True, max_split: int = 4,
-                 output_gate_floor: float | None = None, anchor_beta: float = 0.0):
+                 output_gate_floor: float | None = None, anchor_beta: float = 0.0, pdl: bool = True):
         _lib.load()
         self.geo = geometry
         self.device = torch.device(device)
@@ -107,6 +107,7 @@ class RefinerEngine:
         cfg.output_gate = int(output_gate_floor is not None)
         cfg.output_gate_floor = float(output_gate_floor) if output_gate_floor is not None else 0.1
         cfg.anchor_beta = float(anchor_beta)
+        cfg.use_pdl = int(pdl)
         for k in range(L):
             cfg.capacity[k] = int(capacity[k]) if capacity is not None else 0
         self._cfg = cfg

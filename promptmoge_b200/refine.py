@@ -34,7 +34,7 @@ class Refiner:
     def __init__(self, weights: dict, clips: dict, model: str = "A", height: int | None = None,
                  width: int | None = None, batch: int = 1, device="cuda", capacity=None, channels=None,
                  enc_channels: int = synth.ENC_CHANNELS, depth_resolution: float = synth.DEPTH_RESOLUTION,
-                 uv_bias=None, max_split: int = 4):
+                 uv_bias=None, max_split: int = 4, pdl: bool = True):
         m = synth.MODELS[model] if model is not None else {}
         self.geo = Geometry(channels=list(channels or m["model_channels"]), height=height or m["H"],
                             width=width or m["W"], batch=batch, enc_channels=enc_channels,
@@ -42,7 +42,7 @@ class Refiner:
         self.default_uv = uv_bias      # baked UV conditioning [C_last, h, w] used when refine() gets none
         self.device = torch.device(device)
         self.engine = RefinerEngine(weights, clips, self.geo, device=self.device, capacity=capacity,
-                                    max_split=max_split)
+                                    max_split=max_split, pdl=pdl)
         B, H, W = batch, self.geo.height, self.geo.width
         ed = 2 ** (self.geo.levels - 1)
         lh, lw = self.geo.lidar_hw

@@ -159,3 +159,28 @@ def test_split_k_plan_equals_unsplit_plan(golden, name):
         outs.append(out.clone())
         eng.close()
     assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("name", ["A_full", "B_small"])
+def test_programmatic_edges_equal_ordinary_edges(golden, name):
+    """The step graph with programmatic kernel-to-kernel edges (each kernel scheduled during its predecessor's tail,
+    waiting on the device) refines to the same bits as the graph with ordinary edges, replay after replay."""
+    from promptmoge_b200 import synth
+    from promptmoge_b200.engine import Geometry, RefinerEngine
+    g = golden(name)
+    sc = g.scene()
+    c = g.config
+    geo = Geometry(channels=synth.MODELS[c["model"]]["model_channels"], height=c["H"], width=c["W"])
+    outs = []
+    for pdl in (False, True):
+        eng = RefinerEngine(g.weights(), g.clips, geo, pdl=pdl)
+        _inputs(eng, sc)
+        eng.capture(1)
+        for _ in range(5):
+            out, fit = eng.replay()
+            outs.append((pdl, out.clone(), fit.clone()))
+        assert eng.status()[0] == 0
+        eng.close()
+    ref = outs[0]
+    for pdl, o, f in outs[1:]:
+        assert torch.equal(o, ref[1]) and torch.equal(f, ref[2]), pdl
