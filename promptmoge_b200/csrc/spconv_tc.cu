@@ -23,7 +23,8 @@
 //               reference's rounding, while the next unit accumulates into the other buffer.
 // Weights arrive by 2-D TMA tile loads from the plain tap-major [taps][Co][Ci] tensor (swizzle matching the row
 // width W = min(Ci, 128)); a conv whose whole 27-tap weight fits (Co = NT, Ci <= 64) keeps it resident in shared
-// memory for the kernel's lifetime.  Every TMA copy lands in this CTA's own shared memory (no multicast).  Every wait
+// memory for the kernel's lifetime.  The SPLIT variant (wide convs of small levels) lets several CTAs share a tile,
+// each over a group of its items, writing int32 partial planes that k_split_epilogue sums before the epilogue.  Every TMA copy lands in this CTA's own shared memory (no multicast).  Every wait
 // is bounded: on timeout the CTA records PMG_ERR_TIMEOUT in the status word, lets issued MMAs retire, frees its TMEM
 // and returns.
 #include <algorithm>
