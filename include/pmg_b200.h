@@ -409,7 +409,10 @@ int pmg_refiner_set_norm(pmg_refiner* r, const char* name, const float* gamma, c
 int pmg_refiner_set_proj(pmg_refiner* r, const char* name, const float* weight, const float* bias);
 
 /* Per-frame conditioning: encoder feature [B,enc_channels,h,w] fp16 and the UV bias map [B,C_last,h,w] fp32
- * (may be NULL).  Runs encoder_fuse on the token grid once (sparse_unet.py:227-233; Refiner.swift:208-221). */
+ * (may be NULL).  Runs encoder_fuse on the token grid once (sparse_unet.py:227-233; Refiner.swift:208-221) on
+ * `stream`, which may differ from the step's stream: the step (enqueued or a captured graph launched after this
+ * call) waits for it only before the encoder fusion, so the two overlap.  The caller must not call it again while
+ * a step that reads the previous frame's tokens is still running. */
 int pmg_refiner_set_frame(pmg_refiner* r, const uint16_t* encoder_feature_f16, const float* uv_bias, void* stream);
 
 /* Inputs of a refine run: point map [B,H,W,3] fp32 (read once, copied into the plan's state), LiDAR depth and

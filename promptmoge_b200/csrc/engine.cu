@@ -130,6 +130,7 @@ struct pmg_refiner {
     // LiDAR fit: it runs on `side`, forked from the step's stream and joined before the U-Net needs it.
     cudaStream_t side = nullptr;
     cudaEvent_t ev_fork = nullptr, ev_vox = nullptr, ev_struct = nullptr;
+    cudaEvent_t ev_frame = nullptr;   // recorded by set_frame; the step waits for it before the encoder fusion
     cudaGraphExec_t exec = nullptr;
     std::vector<void*> allocs;
     int launches = 0;
@@ -418,6 +419,12 @@ int enqueue_step(pmg_refiner* r, cudaStream_t s) {
     {
         LevelBuf& l = r->lv[L - 1];
         const int32_t* cnt = r->counts + 2 * (L - 1);
+        // the frame's encoder tokens (set_frame, possibly on another stream, overlapping the levels above): wait
+        // for the latest set_frame -- in a captured graph, for the latest one issued before the graph's launch
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        PMG_CUDA_TRY(cudaStreamIsCapturing(s, &cs));
+        PMG_CUDA_TRY(cudaStreamWaitEvent(s, r->ev_frame,
+                                         cs == cudaStreamCaptureStatusActive ? cudaEventWaitExternal : 0));
         LAUNCH(concat_q8(l.S, r->enc_tok, l.col ? l.col : nullptr, cnt, l.cap, l.C, r->fuse0.sa, r->aq, s));
         LAUNCH(dense(r, r->aq, cnt, l.cap, 2 * l.C, l.C, r->fuse0, PMG_EPI_SILU_Q8, r->fuse2.sa, nullptr, r->g8, s));
         LAUNCH(dense(r, r->g8, cnt, l.cap, l.C, l.C, r->fuse2, PMG_EPI_F32, 0.f, nullptr, l.X, s));
@@ -472,7 +479,7 @@ namespace {
 void destroy_streams(pmg_refiner* r) {
     if (r->exec) cudaGraphExecDestroy(r->exec);
     r->exec = nullptr;
-    for (cudaEvent_t* e : {&r->ev_fork, &r->ev_vox, &r->ev_struct})
+    for (cudaEvent_t* e : {&r->ev_fork, &r->ev_vox, &r->ev_struct, &r->ev_frame})
         if (*e) {
             cudaEventDestroy(*e);
             *e = nullptr;
@@ -502,6 +509,7 @@ extern "C" int pmg_refiner_create(const pmg_refiner_config* cfg, pmg_refiner** o
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&r->ev_fork, cudaEventDisableTiming);
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&r->ev_vox, cudaEventDisableTiming);
         if (e == cudaSuccess) e = cudaEventCreateWithFlags(&r->ev_struct, cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&r->ev_frame, cudaEventDisableTiming);
         if (e != cudaSuccess) {
             set_cuda_error(e);
             rc = PMG_ERR_CUDA;
@@ -593,8 +601,10 @@ extern "C" int pmg_refiner_set_frame(pmg_refiner* r, const uint16_t* enc_f16, co
     if (uv_bias) PMG_TRY(planar_to_rows(uv_bias, B, C, r->T, r->uv_rows, s));
     Epi e{uv_bias ? PMG_EPI_F32_RESID : PMG_EPI_F32, r->enc.sa, 0.f, r->enc.ws, r->enc.b, uv_bias ? r->uv_rows : nullptr,
           r->enc_tok, r->status};
-    return gemm_i8(r->tok_q, (int64_t)B * r->T, nullptr, 0, nullptr, nullptr, (int64_t)B * r->T, K, C, 1, r->enc.w,
-                   flags_of(r), e, s);
+    PMG_TRY(gemm_i8(r->tok_q, (int64_t)B * r->T, nullptr, 0, nullptr, nullptr, (int64_t)B * r->T, K, C, 1, r->enc.w,
+                    flags_of(r), e, s));
+    PMG_CUDA_TRY(cudaEventRecord(r->ev_frame, s));
+    return PMG_OK;
 }
 
 extern "C" int pmg_refiner_set_inputs(pmg_refiner* r, const float* point_coord, const float* lidar_depth,

@@ -59,6 +59,7 @@ class Refiner:
         self._K = None
         self._raw = None
         self._uv_dev = None
+        self._side = None
 
     def input_bytes(self) -> int:
         return sum(t.numel() * t.element_size() for t in (self.d_pc, self.d_ld, self.d_lc, self.d_enc, self.d_uv))
@@ -87,19 +88,26 @@ class Refiner:
             ld, lc = self._raw
         else:
             ld, lc = self.d_ld, self.d_lc
-        for dst, src in ((self.d_pc, point_coord), (ld, lidar_depth), (lc, lidar_conf),
-                         (self.d_enc, encoder_feature)):
+        # the step's own inputs on the step's stream; the per-frame conditioning (encoder feature, UV planes,
+        # encoder_fuse) on a side stream that the step waits for only before its encoder fusion, so its copy and
+        # kernels overlap the finer levels.  The side stream first waits for the previous call's step.
+        if self._side is None:
+            self._side = torch.cuda.Stream(self.device)
+        self._side.wait_stream(s)
+        for dst, src in ((self.d_pc, point_coord), (ld, lidar_depth), (lc, lidar_conf)):
             dst.copy_(torch.as_tensor(src), non_blocking=True)
         if fill:
             ops.nearest_fill(ld, lc, out=(self.d_ld, self.d_lc))
-        if uv_bias is None and self.default_uv is not None:
-            if self._uv_dev is None:
-                self._uv_dev = torch.as_tensor(self.default_uv).to(self.device).expand_as(self.d_uv).contiguous()
-            self.d_uv.copy_(self._uv_dev)
-            uv_bias = self._uv_dev
-        elif uv_bias is not None:
-            self.d_uv.copy_(torch.as_tensor(uv_bias), non_blocking=True)
-        self.engine.set_frame(self.d_enc, self.d_uv if uv_bias is not None else None)
+        with torch.cuda.stream(self._side):
+            self.d_enc.copy_(torch.as_tensor(encoder_feature), non_blocking=True)
+            if uv_bias is None and self.default_uv is not None:
+                if self._uv_dev is None:
+                    self._uv_dev = torch.as_tensor(self.default_uv).to(self.device).expand_as(self.d_uv).contiguous()
+                self.d_uv.copy_(self._uv_dev)
+                uv_bias = self._uv_dev
+            elif uv_bias is not None:
+                self.d_uv.copy_(torch.as_tensor(uv_bias), non_blocking=True)
+            self.engine.set_frame(self.d_enc, self.d_uv if uv_bias is not None else None)
         out, fit = self.engine.replay()
         self.h_out.copy_(out, non_blocking=True)
         self.h_fit.copy_(fit, non_blocking=True)

@@ -184,3 +184,36 @@ def test_programmatic_edges_equal_ordinary_edges(golden, name):
     ref = outs[0]
     for pdl, o, f in outs[1:]:
         assert torch.equal(o, ref[1]) and torch.equal(f, ref[2]), pdl
+
+
+def test_refiner_frame_conditioning_follows_each_call():
+    """Refiner.refine runs the per-frame conditioning (encoder tokens) on a side stream that the step waits for
+    only before its encoder fusion: alternating two frames, every call refines with its own frame's tokens (same
+    bits as the first call of that frame, and as the engine with set_frame on the step's stream)."""
+    from promptmoge_b200 import synth
+    from promptmoge_b200.engine import Geometry, RefinerEngine
+    from promptmoge_b200.refine import Refiner, pinned, synthetic_model
+    m = synth.MODELS["B"]
+    weights, clips = synthetic_model("B", 0)
+    scenes = [synth.make_scene(s, m["H"], m["W"], m["encoder_downsample"], m["model_channels"][-1], batch=1)
+              for s in (21, 22)]
+    args = [tuple(pinned(x) for x in (sc.point_coord, sc.lidar_depth, sc.lidar_conf, sc.encoder_feature, sc.uv_bias))
+            for sc in scenes]
+    ref = Refiner(weights, clips, "B", batch=1)
+    try:
+        first = [ref.refine(*a)[0].clone() for a in args]
+        assert not torch.equal(first[0], first[1])
+        for _ in range(3):
+            for i, a in enumerate(args):
+                assert torch.equal(ref.refine(*a)[0], first[i])
+    finally:
+        ref.close()
+    geo = Geometry(channels=m["model_channels"], height=m["H"], width=m["W"])
+    eng = RefinerEngine(weights, clips, geo)
+    try:
+        for i, sc in enumerate(scenes):
+            _inputs(eng, sc)
+            out, _ = eng.run(1)
+            assert torch.equal(out.cpu(), first[i])
+    finally:
+        eng.close()
