@@ -198,6 +198,9 @@ __device__ __forceinline__ void epi_store16(const Epi& e, const float* ws, const
 #pragma unroll
         for (int q = 0; q < 4; ++q) d[q] = make_int4((int)r[4 * q], (int)r[4 * q + 1], (int)r[4 * q + 2], (int)r[4 * q + 3]);
     } else if (e.mode == PMG_EPI_SILU_Q8) {
+        // SiLU + requantise by the reciprocal-estimate path that falls back to the exact IEEE chain near a
+        // rounding boundary (silu_quant8_fast): the same integers as quant8(silu(y), s), fewer divides
+        const float inv = __fdiv_rn(1.0f, e.out_scale);
         uint32_t packed[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -205,7 +208,7 @@ __device__ __forceinline__ void epi_store16(const Epi& e, const float* ws, const
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
                 const int n = n0 + 4 * q + t;
-                const int v = quant8(silu(dequant((int)r[4 * q + t], e.sa, ws[n], bias[n])), e.out_scale);
+                const int v = silu_quant8_fast(dequant((int)r[4 * q + t], e.sa, ws[n], bias[n]), e.out_scale, inv);
                 w |= ((uint32_t)(v & 0xFF)) << (8 * t);
             }
             packed[q] = w;
