@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload: Model A refiner, one refine step (K=1), batch 1, 480x640 synthetic room frame per
+Workload (benchmark configuration 2): Model A refiner, one refine step (K=1), batch 1, 480x640 synthetic room frame per
 GPU (seed = rank), random-init int8 weights with the reference observer's clips.  A "step" = fit -> prompt features
 -> voxelise -> 5-level structure (dedup + neighbour maps) -> int8 U-Net -> logz update, replayed as one CUDA graph.
 With N > 1 every rank refines its own independent frames (frame-batch sharding, weak scaling) and the per-frame fits
@@ -29,7 +29,7 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "refine steps/s (Model A, 480x640, K=1)"
 METRIC_B = "refine steps/s (Model B, 240x320, K=1)"
-# the only published numbers for this path (int8 Metal, iPad Pro 11" M5, warm, K = 1)
+# The only published numbers for this path (int8 Metal, iPad Pro 11" M5, warm, K = 1)
 PUBLISHED_MS = {"A": 27.3, "B": 10.4}
 PUBLISHED_STEPS_S = {k: 1000.0 / v for k, v in PUBLISHED_MS.items()}
 UNIT = "steps/s"
@@ -484,7 +484,7 @@ def profile_conv(args):
 
 
 def conv_sweep(args):
-    """the isolated int8 submanifold conv on surface-shell voxel sets (about 9 occupied taps per
+    """Benchmark configuration 3: the isolated int8 submanifold conv on surface-shell voxel sets (about 9 occupied taps per
     voxel) of N in {1e5, 5e5, 2e6, 8e6} voxels, C in {16, 32, 64, 128}: neighbour map by the hash builder, then the
     conv (tcgen05 where the width allows, SIMT dp4a at C = 16) with the SiLU + requantise epilogue, timed alone with
     CUDA events (median of --steps, inputs 2-128 MB, L2 flushed before each launch).  One JSON line per (N, C) with
@@ -529,7 +529,7 @@ def conv_sweep(args):
 
 
 def fused_scene(args, ws, rank, local):
-    """one synthetic 12 x 12 x 3 m room seen from 200 poses (480 x 640, random walk), fused into a
+    """Benchmark configuration 5: one synthetic 12 x 12 x 3 m room seen from 200 poses (480 x 640, random walk), fused into a
     1 cm voxel grid, Morton-range sharded over the ranks; a stack of --fused-layers int8 submanifold convs (C = 32,
     Model A's level-0 width, SiLU + requantise epilogue) with a one-voxel halo exchange (NCCL all-to-all of int8
     rows) before every layer.  value = voxel-layers/s of the whole job (strong scaling: the scene is fixed);

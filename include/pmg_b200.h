@@ -103,7 +103,7 @@ size_t pmg_nmap_hash_workspace_bytes(int64_t capacity);
 /* Neighbour map of an arbitrary voxel set (any order) by warp-cooperative open-addressing hashing of 64-bit
  * linearised keys.  Replaces build_submanifold_cache's "sorted" backend for generic coordinates
  * (_core.py:105-124, 298-336).  coords [M,4] int32 (b, x, y, z); extents [4] host int64 = the sparse shape
- * (product < 2^63); coordinates outside it set PMG_ERR_RANGE in `status`; neighbours outside it are absent
+ * (product < 2^64: the largest linear key, product - 1, never equals the all-ones empty-slot key); coordinates outside it set PMG_ERR_RANGE in `status`; neighbours outside it are absent
  * (_core.py:97-102).  nmap: tap-major [27][ld] when row_major == 0, else [M][27]. tile_mask may be NULL. */
 int pmg_nmap_hash(const int32_t* coords, int64_t M, const int64_t* extents_host, int32_t* nmap, int64_t ld,
                   int32_t row_major, uint32_t* tile_mask, void* workspace, size_t workspace_bytes, int32_t* status,
@@ -115,7 +115,7 @@ int pmg_nmap_hash(const int32_t* coords, int64_t M, const int64_t* extents_host,
  * fixed 6 MiB array compiled into the library and resident on every GPU that loads it until the process exits;
  * M must be <= 262144 voxels (larger M returns PMG_ERR_BAD_ARG without touching the device).  It calls no
  * allocator.  The first call on a device looks the table's address up (cudaGetSymbolAddress) with that device
- * current: make that first call before any stream capture.  Every call reuses the same table, clearing the part it
+ * current: make that first call before any stream capture (and, after a device reset, the first call after it).  Every call reuses the same table, clearing the part it
  * needs at its start, so calls whose executions overlap on the GPU (other streams, other host threads) race and
  * corrupt each other; serialise them.  Same arguments and results as pmg_nmap_hash. */
 int pmg_nmap_hash_noalloc(const int32_t* coords, int64_t M, const int64_t* extents_host, int32_t* nmap, int64_t ld,

@@ -131,6 +131,10 @@ struct pmg_refiner {
     cudaStream_t side = nullptr;
     cudaEvent_t ev_fork = nullptr, ev_vox = nullptr, ev_struct = nullptr;
     cudaEvent_t ev_frame = nullptr;   // recorded by set_frame; the step waits for it before the encoder fusion
+    // When set_frame was itself recorded into a stream capture, the id of that capture: a step captured into the
+    // same graph then joins the record as an ordinary graph dependency, not as an external event wait.
+    unsigned long long frame_capture_id = 0;
+    bool frame_in_capture = false;
     cudaGraphExec_t exec = nullptr;
     std::vector<void*> allocs;
     int launches = 0;
@@ -421,10 +425,14 @@ int enqueue_step(pmg_refiner* r, cudaStream_t s) {
         const int32_t* cnt = r->counts + 2 * (L - 1);
         // the frame's encoder tokens (set_frame, possibly on another stream, overlapping the levels above): wait
         // for the latest set_frame -- in a captured graph, for the latest one issued before the graph's launch
+        // (an external event-wait node), unless set_frame was recorded into this same capture, where the record
+        // is a graph node and an ordinary wait adds the dependency on it
         cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-        PMG_CUDA_TRY(cudaStreamIsCapturing(s, &cs));
-        PMG_CUDA_TRY(cudaStreamWaitEvent(s, r->ev_frame,
-                                         cs == cudaStreamCaptureStatusActive ? cudaEventWaitExternal : 0));
+        unsigned long long cap_id = 0;
+        PMG_CUDA_TRY(cudaStreamGetCaptureInfo(s, &cs, &cap_id));
+        const bool capturing = cs == cudaStreamCaptureStatusActive;
+        const bool same_capture = capturing && r->frame_in_capture && r->frame_capture_id == cap_id;
+        PMG_CUDA_TRY(cudaStreamWaitEvent(s, r->ev_frame, capturing && !same_capture ? cudaEventWaitExternal : 0));
         LAUNCH(concat_q8(l.S, r->enc_tok, l.col ? l.col : nullptr, cnt, l.cap, l.C, r->fuse0.sa, r->aq, s));
         LAUNCH(dense(r, r->aq, cnt, l.cap, 2 * l.C, l.C, r->fuse0, PMG_EPI_SILU_Q8, r->fuse2.sa, nullptr, r->g8, s));
         LAUNCH(dense(r, r->g8, cnt, l.cap, l.C, l.C, r->fuse2, PMG_EPI_F32, 0.f, nullptr, l.X, s));
@@ -603,6 +611,11 @@ extern "C" int pmg_refiner_set_frame(pmg_refiner* r, const uint16_t* enc_f16, co
           r->enc_tok, r->status};
     PMG_TRY(gemm_i8(r->tok_q, (int64_t)B * r->T, nullptr, 0, nullptr, nullptr, (int64_t)B * r->T, K, C, 1, r->enc.w,
                     flags_of(r), e, s));
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    unsigned long long cap_id = 0;
+    PMG_CUDA_TRY(cudaStreamGetCaptureInfo(s, &cs, &cap_id));
+    r->frame_in_capture = cs == cudaStreamCaptureStatusActive;
+    r->frame_capture_id = r->frame_in_capture ? cap_id : 0;
     PMG_CUDA_TRY(cudaEventRecord(r->ev_frame, s));
     return PMG_OK;
 }

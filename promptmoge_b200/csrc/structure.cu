@@ -13,6 +13,8 @@
 // column index, so their neighbour map comes from a hash table of 64-bit linearised keys probed by groups of 8
 // lanes that read one 64-byte bucket per step (warp-cooperative bucketed linear probing).
 #include <algorithm>
+#include <cuda.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -604,18 +606,25 @@ static __device__ __align__(256) unsigned char g_nmap_noalloc_table[kNoAllocByte
 
 static std::mutex g_noalloc_mu;
 static void* g_noalloc_addr[256] = {};
+static CUcontext g_noalloc_ctx[256] = {};
 
 // Device address of the table on the current device.  Host code cannot use the symbol itself (on the host it names a
-// shadow variable, not device memory), so the address is looked up once per device, with that device current.
+// shadow variable, not device memory), so the address is looked up once per device, with that device current.  The
+// cached address belongs to the context it was looked up in: when the device's current context is a different one
+// (the primary context was reset and re-created, e.g. after cudaDeviceReset), the address is looked up again.
 static int noalloc_table(void** out) {
     int dev = 0;
     PMG_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 256) return PMG_ERR_UNSUPPORTED;
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (!g_noalloc_addr[dev]) {
+    CUcontext ctx = nullptr;
+    if (cuCtxGetCurrent(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+    if (!g_noalloc_addr[dev] || !ctx || ctx != g_noalloc_ctx[dev]) {
         void* p = nullptr;
-        PMG_CUDA_TRY(cudaGetSymbolAddress(&p, g_nmap_noalloc_table));
+        PMG_CUDA_TRY(cudaGetSymbolAddress(&p, g_nmap_noalloc_table));   // makes the device's context current
+        if (cuCtxGetCurrent(&ctx) != CUDA_SUCCESS) ctx = nullptr;
         g_noalloc_addr[dev] = p;
+        g_noalloc_ctx[dev] = ctx;
     }
     *out = g_noalloc_addr[dev];
     return PMG_OK;

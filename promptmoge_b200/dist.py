@@ -1,4 +1,4 @@
-"""Multi-GPU frame sharding for batched refinement (many independent frames over 1-8 GPUs).
+"""Multi-GPU frame sharding for batched refinement (benchmark configuration 4: many independent frames over 1-8 GPUs).
 
 Frames are independent units (the reference batches them column-wise with per-frame z offsets, moge/model/v3.py:333,
 and fits them row by row, prompt_stem.py:211-240), so each rank refines a contiguous range of frames with its own

@@ -1,4 +1,4 @@
-"""Fused multi-frame scene: one voxel grid back-projected from many camera poses, sharded over
+"""Fused multi-frame scene (benchmark configuration 5): one voxel grid back-projected from many camera poses, sharded over
 GPUs by Morton (Z-order) ranges, with a one-voxel halo exchange before every submanifold conv.
 
 The reference refines one frame at a time (moge/model/v3.py:305-344 voxelises one point map, one voxel per pixel);

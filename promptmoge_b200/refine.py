@@ -99,6 +99,10 @@ class Refiner:
         if fill:
             ops.nearest_fill(ld, lc, out=(self.d_ld, self.d_lc))
         with torch.cuda.stream(self._side):
+            for src in (encoder_feature, uv_bias):
+                # a device tensor read on the side stream stays allocated until that stream is done with it
+                if isinstance(src, torch.Tensor) and src.is_cuda:
+                    src.record_stream(self._side)
             self.d_enc.copy_(torch.as_tensor(encoder_feature), non_blocking=True)
             if uv_bias is None and self.default_uv is not None:
                 if self._uv_dev is None:

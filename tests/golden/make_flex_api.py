@@ -40,4 +40,6 @@ def main(fallback_dir: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference/promptmoge/_fallback")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {sys.argv[0]} /path/to/PromptMoGe/promptmoge/_fallback")
+    main(sys.argv[1])

@@ -5,7 +5,7 @@ runs prompt_stem.fit_scale_shift) on seeded synthetic frames:
     output gate      g = floor + (1 - floor) * u;  logz = cur + g * (refined - cur)
     elastic anchor   log_d_aff, gate = _lidar_in_affine_frame(logz);  logz = logz + beta * gate * (log_d_aff - logz)
 
-    python tests/golden/make_gates.py [/path/to/reference]
+    python tests/golden/make_gates.py /path/to/PromptMoGe
 
 Writes tests/golden/gates.npz: per case the inputs (cur, refined [B,H,W], lidar / conf [B,1,192,256]), floor,
 beta, and the reference's gated logz."""
@@ -59,4 +59,6 @@ def main(ref: Path):
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {sys.argv[0]} /path/to/PromptMoGe")
+    main(Path(sys.argv[1]))

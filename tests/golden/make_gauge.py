@@ -2,7 +2,7 @@
 MoGeModel.prompt_gauge_poly (moge/model/v3.py:151-183) on seeded synthetic frames: a ray-cast room's depth with a
 smooth multiplicative distortion and noise as the prediction, the scene's LiDAR and confidence as the prompt.
 
-    python tests/golden/make_gauge.py [/path/to/reference]
+    python tests/golden/make_gauge.py /path/to/PromptMoGe
 
 Writes tests/golden/gauge.npz: per case the inputs (depth [B,H,W], lidar [B,h,w], conf [B,h,w]), degree, and the
 reference output corr [B,H,W] (fp32)."""
@@ -84,4 +84,6 @@ def main(ref):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {sys.argv[0]} /path/to/PromptMoGe")
+    main(sys.argv[1])

@@ -2,7 +2,7 @@
 moge.utils.geometry_torch.recover_focal_shift (moge/utils/geometry_torch.py:118-170: nearest downsample to 64 x 64,
 scipy least_squares 'lm' per frame, geometry_numpy.py:82-119) and normalized_view_plane_uv (geometry_torch.py:43-55).
 
-    python tests/golden/make_post.py [/path/to/reference]
+    python tests/golden/make_post.py /path/to/PromptMoGe
 
 Writes tests/golden/post.npz: per case the affine point map [B,H,W,3], the optional mask [B,H,W] and fixed focal
 [B], and the reference's focal [B] and shift [B]; and the view-plane uv grids of a few sizes."""
@@ -88,4 +88,6 @@ def main(ref: Path):
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {sys.argv[0]} /path/to/PromptMoGe")
+    main(Path(sys.argv[1]))

@@ -2,7 +2,7 @@
 exporter, promptmoge/export/refiner.py:28-111, for the synthetic Model A and Model B refiners of
 promptmoge_b200.synth (seed 0) with the activation clips of promptmoge_b200/synth_clips.json.
 
-    python tests/golden/make_refiner_bin.py [/path/to/reference]
+    python tests/golden/make_refiner_bin.py /path/to/PromptMoGe
 
 The exporter normally loads a trained checkpoint (load_model); here its ``load_model`` is replaced by a function
 returning the reference's own Sparse3DUNet with the synthetic weights, QAT enabled (enable_refiner_qat) and each
@@ -73,4 +73,6 @@ def main(ref: Path):
 
 
 if __name__ == "__main__":
-    main(Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {sys.argv[0]} /path/to/PromptMoGe")
+    main(Path(sys.argv[1]))

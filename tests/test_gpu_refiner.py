@@ -217,3 +217,51 @@ def test_refiner_frame_conditioning_follows_each_call():
             assert torch.equal(out.cpu(), first[i])
     finally:
         eng.close()
+
+
+def test_set_frame_captured_with_the_steps():
+    """set_frame recorded into the same stream capture as the steps: the step's encoder fusion depends on that
+    capture's encoder GEMM (an ordinary graph edge), so each replay refines with the tokens copied in right before
+    it.  Two frames alternate through one graph; every replay matches the uncaptured run of its frame."""
+    from promptmoge_b200 import synth
+    from promptmoge_b200.engine import Geometry, RefinerEngine
+    from promptmoge_b200.refine import synthetic_model
+    m = synth.MODELS["B"]
+    weights, clips = synthetic_model("B", 0)
+    scenes = [synth.make_scene(s, m["H"], m["W"], m["encoder_downsample"], m["model_channels"][-1], batch=1)
+              for s in (31, 32)]
+    geo = Geometry(channels=m["model_channels"], height=m["H"], width=m["W"])
+    eng = RefinerEngine(weights, clips, geo)
+    try:
+        want = []
+        for sc in scenes:
+            _inputs(eng, sc)
+            out, _ = eng.run(1)
+            want.append(out.clone())
+        torch.cuda.synchronize()
+        assert not torch.equal(want[0], want[1])
+        pc = torch.empty_like(want[0])
+        ld = torch.empty(scenes[0].lidar_depth.shape, dtype=torch.float32, device="cuda")
+        lc = torch.empty_like(ld)
+        enc = torch.empty(scenes[0].encoder_feature.shape, dtype=torch.float16, device="cuda")
+        uv = torch.empty(scenes[0].uv_bias.shape, dtype=torch.float32, device="cuda")
+        eng.set_inputs(pc, ld, lc)
+        eng._outputs()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            eng.set_frame(enc, uv)
+            out, _ = eng.run(1)
+        for _ in range(2):
+            for i, sc in enumerate(scenes):
+                for dst, src in ((pc, sc.point_coord), (ld, sc.lidar_depth), (lc, sc.lidar_conf),
+                                 (enc, sc.encoder_feature), (uv, sc.uv_bias)):
+                    dst.copy_(torch.from_numpy(src))
+                g.replay()
+                torch.cuda.synchronize()
+                assert torch.equal(out, want[i]), i
+        assert eng.status()[0] == 0
+        del g
+    finally:
+        eng.close()

@@ -60,6 +60,27 @@ def test_noalloc_equals_workspace_entry_point_on_consecutive_calls():
             assert torch.equal(mask[:n_groups], want_mask[:n_groups])
 
 
+def test_noalloc_at_its_size_limit_then_a_smaller_call():
+    """M equal to the fixed limit (a dense 64^3 block: 262,144 voxels, so the table's slots are all in use and
+    the values end at the array's last byte), then a smaller set on the same table: both equal pmg_nmap_hash."""
+    from promptmoge_b200 import ops, synth
+    r = torch.arange(64, dtype=torch.int32)
+    x, y, z = torch.meshgrid(r, r, r, indexing="ij")
+    cube = torch.stack([torch.zeros_like(x), x, y, z], -1).reshape(-1, 4).contiguous().cuda()
+    assert cube.shape[0] == MAX_VOXELS
+    small = torch.from_numpy(synth.make_surface_voxels(20000, seed=5)).cuda()
+    cases = [(cube, [1, 64, 64, 64]), (small, [1, 1 << 21, 1 << 21, 1 << 21])]
+    results = [_noalloc(c, e, False) for c, e in cases]
+    torch.cuda.synchronize()
+    for (coords, ext), (nm, mask, st) in zip(cases, results):
+        want, want_mask, want_st = ops.nmap_hash(coords, ext, row_major=False)
+        torch.cuda.synchronize()
+        assert int(st.item()) == 0 and int(want_st.item()) == 0
+        assert torch.equal(nm, want)
+        n_groups = (coords.shape[0] + 31) // 32
+        assert torch.equal(mask[:n_groups], want_mask[:n_groups])
+
+
 def test_noalloc_refuses_inputs_above_its_fixed_table():
     from promptmoge_b200 import _lib
     lib = _lib.load()
