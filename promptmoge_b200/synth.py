@@ -259,3 +259,13 @@ def make_surface_voxels(n: int, seed: int = 0, axis_bits: int = 21) -> np.ndarra
     coords = np.zeros((p.shape[0], 4), np.int32)
     coords[:, 1:] = p
     return coords
+
+
+def seeded_conv_input(layer: str, rows: int, channels: int) -> np.ndarray:
+    """Seeded int8 input [rows, channels], uniform in [-127, 127], for pinning one conv layer's int32 accumulators
+    at full size: the fixture generator feeds it to the reference's own submanifold_conv on the reference-built
+    neighbour cache, the GPU tests feed the same array to the library's conv kernels.  The seed is derived from the
+    layer's reference module name, so every layer gets its own input."""
+    seed = int.from_bytes(layer.encode(), "little") % (2 ** 61 - 1)
+    rng = np.random.default_rng(seed)
+    return rng.integers(-127, 128, size=(rows, channels)).astype(np.int8)

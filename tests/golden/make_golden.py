@@ -14,12 +14,13 @@ and runs the reference refine loop (moge/model/v3.py:547-576: ``_lidar_in_affine
 * per quantised layer: its int8 input q (the reference rule round(x / (clip/127)) applied to the layer's real
   input), the exact int32 accumulators computed by the reference's own operators on the integers in float64
   (submanifold_conv for convs, the verify_int8.py:86-103 float64 GEMM for linears) as a SHA-256 plus sampled rows,
-  and the reference layer's float output on the sampled rows;
+  and the reference layer's float output on the sampled rows; for every conv, also the SHA-256 of the exact int32
+  accumulators of the same layer on a seeded int8 input (synth.seeded_conv_input) and the reference's neighbour cache;
 * per step: the fit (s, t), prompt features, the refined logz;
 * the final 'lidar_ls' fit (v3.py:768-777) on the refined depth and the gauge polynomial (v3.py:151-183).
 
-Full-size configurations store SHA-256 digests of the structure arrays and sampled outputs only, so the committed
-files stay small.  The synthetic model's activation clips for the benchmark configurations are also written to
+Full-size configurations store SHA-256 digests of the structure arrays and accumulators, sampled outputs and the
+frame's refinement (delta log-depth) in float16, so the committed files stay small.  The synthetic model's activation clips for the benchmark configurations are also written to
 promptmoge_b200/synth_clips.json.
 """
 from __future__ import annotations
@@ -203,6 +204,16 @@ def run_config(R, name, model, H, W, ed, K, seed, full_dump):
                 out[key + "_y_rows"] = outs[n].float().numpy()[rows]
                 if full_dump:
                     out[key + "_q"] = q8
+                if n in caches:
+                    # the same layer on a seeded int8 input (synth.seeded_conv_input, regenerated by the GPU tests):
+                    # pins the int32 accumulators at every size, independently of upstream float rounding
+                    qs = synth.seeded_conv_input(n, M, q8.shape[1])
+                    acc_s, _ = R.flex_gemm.ops.submanifold_conv(torch.from_numpy(qs).double(), cache.input_coords,
+                                                                shape, qw.double(), None, neighbor_cache=cache)
+                    assert float((acc_s - acc_s.round()).abs().max()) == 0.0
+                    acc_s = acc_s.long()
+                    assert int(acc_s.abs().max()) < 2 ** 31
+                    digests[P + "S_" + n + "_acc"] = sha(acc_s.numpy().astype(np.int32))
             out[P + "prompt_feats_digest_rows"] = prompt_feats.numpy()[:: max(1, prompt_feats.shape[0] // 2048)]
             delta = (refined - logz).numpy()
             if full_dump:
@@ -210,6 +221,7 @@ def run_config(R, name, model, H, W, ed, K, seed, full_dump):
                 out[P + "prompt_feats"] = prompt_feats.numpy().astype(np.float32)
                 out[P + "delta"] = delta.astype(np.float32)
             else:
+                out[P + "delta_f16"] = delta.astype(np.float16)       # the whole frame's refinement, half precision
                 pix = np.sort(rng.choice(delta.size, 8192, replace=False))
                 out[P + "pix"] = pix
                 out[P + "delta_pix"] = delta.reshape(-1)[pix].astype(np.float32)

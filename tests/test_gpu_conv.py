@@ -241,3 +241,74 @@ def test_split_k_equals_single_pass(C, N, split):
             sp = ops.spconv_i8(q, tm, mask, wt, ws, b, 0.03, mode, 0.05, resid, status=status, split=split)
             assert torch.equal(sp, one), mode
     assert int(status.item()) == 0
+
+
+def _plan_structure(g):
+    """Run one step of the refiner plan on the fixture's scene; return the engine (its level structures are
+    SHA-equal to the reference's, tests/test_gpu_structure.py) and the per-level voxel counts."""
+    from promptmoge_b200 import synth
+    from promptmoge_b200.engine import Geometry, RefinerEngine
+    c = g.config
+    sc = g.scene()
+    geo = Geometry(channels=synth.MODELS[c["model"]]["model_channels"], height=c["H"], width=c["W"])
+    eng = RefinerEngine(g.weights(), g.clips, geo)
+    eng.set_frame(torch.from_numpy(sc.encoder_feature).cuda(), torch.from_numpy(sc.uv_bias).cuda())
+    eng.set_inputs(torch.from_numpy(sc.point_coord).cuda(), torch.from_numpy(sc.lidar_depth).cuda(),
+                   torch.from_numpy(sc.lidar_conf).cuda())
+    eng.run(1)
+    rc, counts = eng.status()
+    assert rc == 0
+    return eng, counts
+
+
+@pytest.mark.parametrize("name", ["A_full", "B_full", "A_small", "B_small"])
+def test_seeded_accumulators_of_every_conv_bit_exact(golden, name):
+    """Every submanifold conv layer of the refiner at the benchmark size, on a seeded int8 input
+    (synth.seeded_conv_input) and the plan's own level structure, through the kernel the plan runs for that level:
+    the frame-grid kernel at level 0, the tcgen05 gather kernel above it, and the split-K variant wherever the plan
+    may split (levels with fewer output tiles than SMs; both split counts are run there).  The int32 accumulators
+    hash to the reference's exact accumulators of the same layer on the same input (the bundled FlexGEMM fallback's
+    submanifold_conv in float64 on its own neighbour cache)."""
+    from promptmoge_b200 import ops, synth
+    from promptmoge_b200.engine import quantise_weight
+    g = golden(name)
+    keys = sorted(k for k in g.digests if k.startswith("s0_S_"))
+    assert keys, "fixture without seeded accumulator digests"
+    widths = _widths(g)
+    L = len(widths)
+    B, H, W = 1, g.config["H"], g.config["W"]
+    w = g.weights()
+    eng, counts = _plan_structure(g)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    checked = 0
+    try:
+        for key in keys:
+            n = key[len("s0_S_"):-len("_acc")]
+            k = _level_for_conv(n, L)
+            M, Cc = counts[k], widths[k]
+            qs = torch.from_numpy(synth.seeded_conv_input(n, M, Cc)).cuda()
+            qw, _ = quantise_weight(w[n + ".weight"])
+            wt = torch.from_numpy(np.ascontiguousarray(qw.reshape(qw.shape[0], 27, -1).transpose(1, 0, 2))).cuda()
+            info = eng.level_info(k)
+            runs = []
+            if k == 0 and ops.grid0_supported(Cc, Cc):
+                lanes = eng.debug_tensor("lanes0", 0, ((B * H * W + 127) // 128, 27, 4), torch.int32)
+                runs.append(("grid0", ops.spconv_i8_grid0(qs, lanes, B, H, W, wt, status=status)))
+            else:
+                cap = info["cap"]
+                nmap = eng.debug_tensor("nmap", k, (27, cap), torch.int32)
+                mask = eng.debug_tensor("tile_mask", k, (cap // 32 + 2,), torch.int32)
+                cnt = torch.tensor([M], dtype=torch.int32, device="cuda")
+                runs.append(("gather", ops.spconv_i8(qs, nmap, mask, wt, count=cnt, rows=M, status=status)))
+                if Cc >= 128 and (M + 127) // 128 * (Cc // 128) < 148:
+                    for sp in (2, 4):
+                        runs.append((f"split{sp}", ops.spconv_i8(qs, nmap, mask, wt, count=cnt, rows=M,
+                                                                 status=status, split=sp)))
+            torch.cuda.synchronize()
+            for kind, acc in runs:
+                assert sha(acc[:M].cpu().numpy()) == g.digests[key], (n, kind)
+                checked += 1
+        assert int(status.item()) == 0
+        assert checked >= len(keys)
+    finally:
+        eng.close()

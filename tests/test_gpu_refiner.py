@@ -71,8 +71,8 @@ def test_graph_replay_is_bitwise_deterministic(golden):
 
 @pytest.mark.parametrize("name", ["B_full", "A_full"])
 def test_full_size_step_against_reference(golden, name):
-    """480x640 / 240x320: the plan's level structure hashes to the reference's, and the refined log-depth agrees on
-    the reference's sampled pixels (depth AbsRel-delta < 0.2 %)."""
+    """480x640 / 240x320: the plan's level structure hashes to the reference's, and the refined log-depth agrees with
+    the reference's on its sampled pixels and over the whole frame (depth AbsRel-delta < 0.2 %)."""
     from promptmoge_b200 import synth
     g = golden(name)
     sc = g.scene()
@@ -93,6 +93,13 @@ def test_full_size_step_against_reference(golden, name):
     d_g, d_r = np.exp(got[pix].astype(np.float64)), np.exp(ref_logz.astype(np.float64))
     assert np.mean(np.abs(d_g - d_r) / d_r) < 2e-3
     np.testing.assert_allclose(got[pix], ref_logz, atol=5e-3)
+    # the whole frame: the reference's refinement of every pixel (stored in float16, ~1e-4 of a delta of ~0.1) added
+    # to the input log-depth, depth AbsRel-delta < 0.2 %
+    logz_in = sc.point_coord[..., 2].reshape(-1).astype(np.float64)
+    ref_full = logz_in + g["s0_delta_f16"].reshape(-1).astype(np.float64)
+    d_g, d_r = np.exp(got.astype(np.float64)), np.exp(ref_full)
+    absrel = float(np.mean(np.abs(d_g - d_r) / d_r))
+    assert absrel < 2e-3, absrel
 
 
 def test_batched_frames_equal_single_frames(golden):

@@ -91,6 +91,25 @@ def test_layer_accumulators_and_dequant(golden, name):
         assert rel <= 1e-3, (n, rel)
 
 
+@pytest.mark.parametrize("name", SMALL)
+def test_seeded_conv_accumulators(golden, name):
+    """Each conv layer on its seeded int8 input (synth.seeded_conv_input): the oracle's accumulators over the
+    reference's neighbour maps hash to the reference's (the digests the GPU tests also check at full size)."""
+    from promptmoge_b200 import synth
+    g = golden(name)
+    widths = ost_levels_widths(g)
+    qr = oref.QuantRefiner(g.weights(), g.clips, widths, [2] * (len(widths) - 1))
+    keys = sorted(k for k in g.digests if k.startswith("s0_S_"))
+    assert len(keys) == (20 if g.config["model"] == "A" else 16)
+    for key in keys:
+        n = key[len("s0_S_"):-len("_acc")]
+        nmap = g[f"s0_L{_level_for_conv(n, widths)}_nmap"]
+        qw, _ = qr.qw[n]
+        q = synth.seeded_conv_input(n, nmap.shape[0], qw.shape[-1])
+        acc = oref.conv_acc(q, nmap, qw)
+        assert sha(acc.astype(np.int32)) == g.digests[key], n
+
+
 def _level_for_conv(name, widths):
     L = len(widths)
     if name.startswith("down_stages."):
