@@ -346,6 +346,14 @@ int pmg_prompt_feats(const float* logz, int64_t logz_stride, const float* lidar,
                      const pmg_fit_state* state, int32_t B, int32_t H, int32_t W, int32_t h, int32_t w,
                      int32_t soft_gate, float* out, void* stream);
 
+/* The LiDAR in the network's affine log-depth frame from a solved state: MoGeModel._lidar_in_affine_frame
+ * (moge/model/v3.py:362-383) after its fit.  log_d_aff [B*H*W] = log(max(d_aff, 1e-4)) where the nearest-resized
+ * sensor value d is finite, positive and d_aff = (d - t) / max(s, 1e-6) > 1e-4, else logz; gate [B*H*W] =
+ * c * ok, or (0.15 + 0.85 c) * ok when soft_gate, with c = clamp(conf / 2, 0, 1). */
+int pmg_affine_frame(const float* logz, int64_t logz_stride, const float* lidar, const float* conf,
+                     const pmg_fit_state* state, int32_t B, int32_t H, int32_t W, int32_t h, int32_t w,
+                     int32_t soft_gate, float* log_d_aff, float* gate, void* stream);
+
 /* depth = s * depth + t per frame, in place (v3.py:777). */
 int pmg_apply_affine(float* depth, const pmg_fit_state* state, int32_t B, int64_t N, void* stream);
 
@@ -419,6 +427,14 @@ int pmg_refiner_set_frame(pmg_refiner* r, const uint16_t* encoder_feature_f16, c
  * confidence [B,1,lidar_h,lidar_w] fp32.  The pointers are recorded; their contents are read when the run executes. */
 int pmg_refiner_set_inputs(pmg_refiner* r, const float* point_coord, const float* lidar_depth, const float* lidar_conf);
 
+/* Prompt features given by the caller instead of the plan's own per-step LiDAR fit: prompt_feats [B*H*W,2] fp32
+ * device (residual, gate), read by every step while set; NULL restores the plan's own fit.  This is the argument
+ * MoGeModel._refine_logz receives (moge/model/v3.py:346-360, called from the refine loop at v3.py:556), for a
+ * caller that computes it itself (each step of a refine loop run by the reference's Python code).  With it set, the
+ * LiDAR inputs of pmg_refiner_set_inputs may be NULL and the run's fit_out is not written.  Re-capture after
+ * setting or clearing it. */
+int pmg_refiner_set_prompt(pmg_refiner* r, const float* prompt_feats);
+
 /* Enqueue K refine steps (no host synchronisation).  The refined point map is written to `point_coord_out`
  * [B,H,W,3] and the last step's per-step fit state (s, t) to `fit_out` [B] (may be NULL). */
 int pmg_refiner_enqueue(pmg_refiner* r, int32_t K, float* point_coord_out, pmg_fit_state* fit_out, void* stream);
@@ -432,7 +448,8 @@ int pmg_refiner_launch(pmg_refiner* r, void* stream);
  * level of the LAST step into counts_host[levels], and clears the word when `clear` is set. */
 int pmg_refiner_status(pmg_refiner* r, int32_t* counts_host, int32_t clear, void* stream);
 
-/* Grow capacities (e.g. after PMG_ERR_OVERFLOW) and reallocate; invalidates any captured graph. */
+/* Grow capacities (e.g. after PMG_ERR_OVERFLOW) and reallocate; invalidates any captured graph and the frame
+ * conditioning of pmg_refiner_set_frame (its token buffers are reallocated): call set_frame again before the next run. */
 int pmg_refiner_set_capacity(pmg_refiner* r, const int64_t* capacity);
 
 /* Number of kernel launches one step enqueues (for launch accounting). */

@@ -53,20 +53,25 @@ def dequant(acc: np.ndarray, s_a, s_w: np.ndarray, b: np.ndarray) -> np.ndarray:
 
 
 def conv_acc(q_in: np.ndarray, nmap: np.ndarray, q_w: np.ndarray) -> np.ndarray:
-    """int32 accumulators of a submanifold conv (_core.py:399-441 in integer form).  q_in [M, Ci] int8,
-    nmap [M, 27] int32, q_w [Co, 3, 3, 3, Ci] int8 -> [M, Co] int64."""
+    """int32 accumulators of a submanifold conv (_core.py:399-441 in integer form: per tap, gather the neighbour rows,
+    multiply by the tap's weight, add into the output rows).  q_in [M, Ci] int8, nmap [M, 27] int32,
+    q_w [Co, 3, 3, 3, Ci] int8 -> [M, Co] int64.
+
+    Each tap's product is an fp32 GEMM, which is exact here: every term is an integer of magnitude <= 127 * 127 and
+    every partial sum of one output has magnitude <= Ci * 127^2 <= 2^22 for Ci <= 256, below 2^24, so no rounding
+    happens in any summation order; the 27 taps are then summed in int64."""
     M = nmap.shape[0]
     Co, Ci = q_w.shape[0], q_w.shape[-1]
-    w = q_w.reshape(Co, 27, Ci).astype(np.float64)
-    acc = np.zeros((M, Co), np.float64)
-    qf = q_in.astype(np.float64)
+    assert Ci * 127 * 127 < 2 ** 24, "fp32 tap products are exact only for Ci <= 1040"
+    w = q_w.reshape(Co, 27, Ci).astype(np.float32)
+    acc = np.zeros((M, Co), np.int64)
     for v in range(27):
         idx = nmap[:, v]
         rows = np.nonzero(idx >= 0)[0]
         if rows.size == 0:
             continue
-        acc[rows] += qf[idx[rows]] @ w[:, v, :].T
-    return acc.astype(np.int64)
+        acc[rows] += (q_in[idx[rows]].astype(np.float32) @ w[:, v, :].T).astype(np.int64)
+    return acc
 
 
 def linear_acc(q_in: np.ndarray, q_w: np.ndarray) -> np.ndarray:

@@ -77,6 +77,7 @@ SIGNATURES = {
     "pmg_fit_prep_final": (I32, [P, P, P, P, I32, I32, I32, I32, I32, P, P, P, P]),
     "pmg_fit_solve": (I32, [P, P, P, I32, I64, I32, F32, I32, P, P, SZ, P]),
     "pmg_prompt_feats": (I32, [P, I64, P, P, P, I32, I32, I32, I32, I32, I32, P, P]),
+    "pmg_affine_frame": (I32, [P, I64, P, P, P, I32, I32, I32, I32, I32, I32, P, P, P]),
     "pmg_apply_affine": (I32, [P, P, I32, I64, P]),
     "pmg_refiner_create": (I32, [C.POINTER(RefinerConfig), C.POINTER(P)]),
     "pmg_refiner_destroy": (None, [P]),
@@ -85,6 +86,7 @@ SIGNATURES = {
     "pmg_refiner_set_proj": (I32, [P, C.c_char_p, P, P]),
     "pmg_refiner_set_frame": (I32, [P, P, P, P]),
     "pmg_refiner_set_inputs": (I32, [P, P, P, P]),
+    "pmg_refiner_set_prompt": (I32, [P, P]),
     "pmg_refiner_enqueue": (I32, [P, I32, P, P, P]),
     "pmg_refiner_capture": (I32, [P, I32, P, P, P]),
     "pmg_refiner_launch": (I32, [P, P]),

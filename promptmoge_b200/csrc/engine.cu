@@ -124,6 +124,7 @@ struct pmg_refiner {
     const float* in_pc = nullptr;
     const float* lidar = nullptr;
     const float* conf = nullptr;
+    const float* ext_prompt = nullptr;   // caller's prompt features [N][2]: the step skips its own LiDAR fit
     // graph
     cudaStream_t cap_stream = nullptr;
     // The voxel structure of a step (voxelise, pools, neighbour maps) depends only on the point map, not on the
@@ -373,7 +374,8 @@ int enqueue_step(pmg_refiner* r, cudaStream_t s) {
     PMG_CUDA_TRY(cudaEventRecord(r->ev_fork, s));
     PMG_CUDA_TRY(cudaStreamWaitEvent(r->side, r->ev_fork, 0));
     // --- per-step LiDAR fit + prompt features (v3.py:552-555) --------------------------------------------------- //
-    if (c.use_prompt) {
+    const bool own_fit = c.use_prompt && !r->ext_prompt;
+    if (own_fit) {
         LAUNCH(fit_prep_prompt(r->pc + 2, 3, r->lidar, r->conf, B, H, W, c.lidar_h, c.lidar_w, r->fz, r->fy,
                                r->fflags, s));
         size_t nclr = 0;
@@ -406,7 +408,7 @@ int enqueue_step(pmg_refiner* r, cudaStream_t s) {
     }
     PMG_CUDA_TRY(cudaEventRecord(r->ev_struct, ss));
     // --- U-Net ---------------------------------------------------------------------------------------------------- //
-    LAUNCH(input_proj(r->pc, c.use_prompt ? r->prompt : nullptr, r->N, l0.C, r->in_proj.w, r->in_proj.b,
+    LAUNCH(input_proj(r->pc, c.use_prompt ? (r->ext_prompt ? r->ext_prompt : r->prompt) : nullptr, r->N, l0.C, r->in_proj.w, r->in_proj.b,
                       r->pr_proj.w, r->pr_proj.b, l0.X, s));
     PMG_CUDA_TRY(cudaStreamWaitEvent(s, r->ev_vox, 0));      // level 0: zq / neighbour map
     for (int k = 0; k < L; ++k) {
@@ -471,12 +473,12 @@ int enqueue_step(pmg_refiner* r, cudaStream_t s) {
 }
 
 int enqueue_run(pmg_refiner* r, int K, float* pc_out, pmg_fit_state* fit_out, cudaStream_t s) {
-    if (!r->in_pc || (r->cfg.use_prompt && (!r->lidar || !r->conf))) return PMG_ERR_BAD_ARG;
+    if (!r->in_pc || (r->cfg.use_prompt && !r->ext_prompt && (!r->lidar || !r->conf))) return PMG_ERR_BAD_ARG;
     PMG_TRY(check_weights(r));
     PMG_CUDA_TRY(cudaMemcpyAsync(r->pc, r->in_pc, r->N * 3 * sizeof(float), cudaMemcpyDeviceToDevice, s));
     for (int k = 0; k < K; ++k) PMG_TRY(enqueue_step(r, s));
     if (pc_out) PMG_CUDA_TRY(cudaMemcpyAsync(pc_out, r->pc, r->N * 3 * sizeof(float), cudaMemcpyDeviceToDevice, s));
-    if (fit_out && r->cfg.use_prompt)
+    if (fit_out && r->cfg.use_prompt && !r->ext_prompt)
         PMG_CUDA_TRY(cudaMemcpyAsync(fit_out, r->fst, r->cfg.batch * sizeof(pmg_fit_state), cudaMemcpyDeviceToDevice, s));
     return PMG_OK;
 }
@@ -626,6 +628,13 @@ extern "C" int pmg_refiner_set_inputs(pmg_refiner* r, const float* point_coord, 
     r->in_pc = point_coord;
     r->lidar = lidar_depth;
     r->conf = lidar_conf;
+    return PMG_OK;
+}
+
+extern "C" int pmg_refiner_set_prompt(pmg_refiner* r, const float* prompt_feats) {
+    if (!r) return PMG_ERR_BAD_ARG;
+    if (prompt_feats && !r->cfg.use_prompt) return PMG_ERR_BAD_ARG;
+    r->ext_prompt = prompt_feats;
     return PMG_OK;
 }
 

@@ -306,7 +306,8 @@ __global__ void __launch_bounds__(kFitThreads) k_fit_select(FitArgs a, int pass)
 
 __global__ void k_prompt_feats(const float* __restrict__ logz, int64_t stride, const float* __restrict__ lidar,
                                const float* __restrict__ conf, const pmg_fit_state* __restrict__ st, int B, int H,
-                               int W, int h, int w, float sy, float sx, int soft, float* __restrict__ out) {
+                               int W, int h, int w, float sy, float sx, int soft, float* __restrict__ out,
+                               float* __restrict__ log_d_aff_out = nullptr, float* __restrict__ gate_out = nullptr) {
     pdl_begin();
     const int64_t N = (int64_t)B * H * W;
     for (int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; m < N; m += (int64_t)gridDim.x * blockDim.x) {
@@ -325,8 +326,14 @@ __global__ void k_prompt_feats(const float* __restrict__ logz, int64_t stride, c
         const float log_d_aff = ok ? logf(fmaxf(d_aff, 1e-4f)) : lz;
         const float okf = ok ? 1.0f : 0.0f;
         const float gate = soft ? __fmul_rn(__fadd_rn(0.15f, __fmul_rn(0.85f, c)), okf) : __fmul_rn(c, okf);
-        out[m * 2] = __fmul_rn(__fsub_rn(log_d_aff, lz), gate);
-        out[m * 2 + 1] = gate;
+        if (out) {
+            out[m * 2] = __fmul_rn(__fsub_rn(log_d_aff, lz), gate);
+            out[m * 2 + 1] = gate;
+        }
+        if (log_d_aff_out) {
+            log_d_aff_out[m] = log_d_aff;
+            gate_out[m] = gate;
+        }
     }
 }
 
@@ -511,6 +518,19 @@ extern "C" int pmg_fit_solve(const float* z, const float* target, const uint8_t*
     void* clr = fit_clear_region(workspace, B, N, &nclr);
     PMG_CUDA_TRY(cudaMemsetAsync(clr, 0, nclr, as_stream(stream)));
     return fit_solve(z, target, flags, B, N, iters, trim, min_points, state, workspace, as_stream(stream));
+}
+
+extern "C" int pmg_affine_frame(const float* logz, int64_t logz_stride, const float* lidar, const float* conf,
+                                const pmg_fit_state* state, int32_t B, int32_t H, int32_t W, int32_t h, int32_t w,
+                                int32_t soft_gate, float* log_d_aff, float* gate, void* stream) {
+    if (!logz || !lidar || !conf || !state || !log_d_aff || !gate || B <= 0 || H <= 0 || W <= 0 || h <= 0 || w <= 0 ||
+        logz_stride <= 0)
+        return PMG_ERR_BAD_ARG;
+    const float sy = (float)h / (float)H, sx = (float)w / (float)W;
+    k_prompt_feats<<<grid_for((int64_t)B * H * W), 256, 0, as_stream(stream)>>>(
+        logz, logz_stride, lidar, conf, state, B, H, W, h, w, sy, sx, soft_gate, nullptr, log_d_aff, gate);
+    PMG_LAUNCH_CHECK();
+    return PMG_OK;
 }
 
 extern "C" int pmg_prompt_feats(const float* logz, int64_t logz_stride, const float* lidar, const float* conf,

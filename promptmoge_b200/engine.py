@@ -84,7 +84,8 @@ class RefinerEngine:
 
     def __init__(self, weights: dict, clips: dict, geometry: Geometry, device="cuda", capacity=None,
                  use_prompt: bool = True, tensor_cores: bool = True, max_split: int = 4,
-                 output_gate_floor: float | None = None, anchor_beta: float = 0.0, pdl: bool = True):
+                 output_gate_floor: float | None = None, anchor_beta: float = 0.0, pdl: bool = True,
+                 soft_gate: bool = True):
         _lib.load()
         self.geo = geometry
         self.device = torch.device(device)
@@ -98,7 +99,7 @@ class RefinerEngine:
         cfg.enc_channels = geometry.enc_channels
         cfg.lidar_h, cfg.lidar_w = geometry.lidar_hw
         cfg.depth_resolution = geometry.depth_resolution
-        cfg.soft_gate, cfg.fit_iters, cfg.fit_trim, cfg.fit_min_points = 1, 4, 0.2, 32
+        cfg.soft_gate, cfg.fit_iters, cfg.fit_trim, cfg.fit_min_points = int(soft_gate), 4, 0.2, 32
         cfg.use_prompt = int(use_prompt)
         cfg.use_tensor_cores = int(tensor_cores)
         cfg.max_split = int(max_split)
@@ -165,6 +166,14 @@ class RefinerEngine:
         call("pmg_refiner_set_inputs", self._h, C.c_void_p(self._pc.data_ptr()),
              C.c_void_p(self._ld.data_ptr()) if self._ld is not None else None,
              C.c_void_p(self._lc.data_ptr()) if self._lc is not None else None)
+        self._graph_key = None
+
+    def set_prompt(self, prompt_feats: torch.Tensor | None):
+        """Prompt features [B*H*W, 2] fp32 on the device that every step reads instead of running its own LiDAR fit
+        (the prompt_feats argument of MoGeModel._refine_logz); None restores the plan's own fit."""
+        self._prompt = None if prompt_feats is None else \
+            prompt_feats.to(device=self.device, dtype=torch.float32).contiguous()
+        call("pmg_refiner_set_prompt", self._h, C.c_void_p(self._prompt.data_ptr()) if self._prompt is not None else None)
         self._graph_key = None
 
     def _outputs(self):

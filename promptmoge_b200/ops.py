@@ -329,6 +329,52 @@ def prompt_feats(logz, lidar, conf, state, soft_gate=True):
     return out
 
 
+def _elem_strided(t: torch.Tensor):
+    """(tensor, element stride) for a [B,H,W] tensor whose elements sit at a constant stride (a contiguous map, or
+    the logz channel of a contiguous [B,H,W,3] point map); anything else is copied to a contiguous tensor."""
+    B, H, W = t.shape
+    for st in (1, 3):
+        if t.stride() == (H * W * st, W * st, st):
+            return t, st
+    return t.contiguous(), 1
+
+
+def affine_frame(logz, lidar, conf, state, soft_gate=True):
+    """(log_d_aff [B,H,W], gate [B,H,W]) of MoGeModel._lidar_in_affine_frame (moge/model/v3.py:362-383) from a solved
+    fit state."""
+    B, H, W = logz.shape
+    h, w = lidar.shape[-2:]
+    lz, st = _elem_strided(logz)
+    log_d_aff = torch.empty((B, H, W), dtype=torch.float32, device=logz.device)
+    gate = torch.empty((B, H, W), dtype=torch.float32, device=logz.device)
+    call("pmg_affine_frame", _p(lz), st, _p(lidar), _p(conf), _p(state), B, H, W, h, w, int(soft_gate), _p(log_d_aff),
+         _p(gate), _stream())
+    return log_d_aff, gate
+
+
+def lidar_in_affine_frame(logz, lidar, conf, soft_gate=False, iters=4, trim=0.2, min_points=32):
+    """MoGeModel._lidar_in_affine_frame (moge/model/v3.py:362-383) on the device: the trimmed least-squares fit of the
+    nearest-resized confident LiDAR to exp(logz) (prompt_stem.fit_scale_shift, prompt_stem.py:211-240), then the
+    LiDAR in the affine log-depth frame.  logz [B,H,W] fp32 (a strided view of a point map's logz channel is read in
+    place), lidar / conf [B,1,h,w] fp32.  Returns (log_d_aff [B,H,W], gate [B,H,W], s [B], t [B])."""
+    if not logz.is_cuda or logz.dtype != torch.float32:
+        raise ValueError("logz must be a float32 CUDA tensor (no CPU path)")
+    _dev(lidar, torch.float32, "lidar")
+    _dev(conf, torch.float32, "conf")
+    lz, st = _elem_strided(logz)
+    B, H, W = logz.shape
+    h, w = lidar.shape[-2:]
+    dev = logz.device
+    z = torch.empty((B, H * W), dtype=torch.float32, device=dev)
+    y = torch.empty((B, H * W), dtype=torch.float32, device=dev)
+    fl = torch.empty((B, H * W), dtype=torch.uint8, device=dev)
+    call("pmg_fit_prep_prompt", _p(lz), st, _p(lidar), _p(conf), B, H, W, h, w, _p(z), _p(y), _p(fl), _stream())
+    state = fit_solve(z, y, fl, iters, trim, min_points)
+    log_d_aff, gate = affine_frame(logz, lidar, conf, state, soft_gate)
+    sv = state.view(torch.float32)[:, :2]       # pmg_fit_state starts with (s, t) fp32
+    return log_d_aff, gate, sv[:, 0].clone(), sv[:, 1].clone()
+
+
 def apply_affine(depth, state):
     B = depth.shape[0]
     call("pmg_apply_affine", _p(depth), _p(state), B, depth[0].numel(), _stream())
