@@ -608,6 +608,23 @@ static std::mutex g_noalloc_mu;
 static void* g_noalloc_addr[256] = {};
 static CUcontext g_noalloc_ctx[256] = {};
 
+// The calling thread's current CUDA context, through the driver entry point the runtime hands out (the library does
+// not link the driver library directly, so it still loads on machines without a GPU driver); nullptr if unknown.
+static CUcontext current_context() {
+    using Fn = CUresult (*)(CUcontext*);
+    static Fn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<Fn>(p);
+    }();
+    CUcontext ctx = nullptr;
+    if (!fn || fn(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+    return ctx;
+}
+
 // Device address of the table on the current device.  Host code cannot use the symbol itself (on the host it names a
 // shadow variable, not device memory), so the address is looked up once per device, with that device current.  The
 // cached address belongs to the context it was looked up in: when the device's current context is a different one
@@ -617,12 +634,11 @@ static int noalloc_table(void** out) {
     PMG_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 256) return PMG_ERR_UNSUPPORTED;
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    CUcontext ctx = nullptr;
-    if (cuCtxGetCurrent(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+    CUcontext ctx = current_context();
     if (!g_noalloc_addr[dev] || !ctx || ctx != g_noalloc_ctx[dev]) {
         void* p = nullptr;
         PMG_CUDA_TRY(cudaGetSymbolAddress(&p, g_nmap_noalloc_table));   // makes the device's context current
-        if (cuCtxGetCurrent(&ctx) != CUDA_SUCCESS) ctx = nullptr;
+        ctx = current_context();
         g_noalloc_addr[dev] = p;
         g_noalloc_ctx[dev] = ctx;
     }
