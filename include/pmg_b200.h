@@ -354,6 +354,20 @@ int pmg_affine_frame(const float* logz, int64_t logz_stride, const float* lidar,
                      const pmg_fit_state* state, int32_t B, int32_t H, int32_t W, int32_t h, int32_t w,
                      int32_t soft_gate, float* log_d_aff, float* gate, void* stream);
 
+/* The whole per-step fit in ONE launch per frame: MoGeModel._lidar_in_affine_frame (v3.py:362-383) = prep
+ * (pmg_fit_prep_prompt), the trimmed least squares (pmg_fit_solve, prompt_stem.py:211-240) and the affine-frame
+ * LiDAR, run by a 16-CTA thread-block cluster that keeps the frame's (z, target) in its shared memory and synchronises
+ * with cluster barriers.  Writes state[b] and prompt_feats [B*H*W,2] (as pmg_prompt_feats) and/or log_d_aff, gate
+ * [B*H*W] (as pmg_affine_frame; give both or neither; prompt_feats 8-byte aligned).  workspace: device, at least
+ * pmg_fit_prompt_fused_workspace_bytes (the frame's z, 4 B per pixel).  PMG_ERR_UNSUPPORTED when a frame's slice
+ * (ceil(H*W/16) pixels x 8 bytes) exceeds 180 KB of shared memory or the device cannot hold the cluster; use the
+ * multi-launch entry points then. */
+size_t pmg_fit_prompt_fused_workspace_bytes(int32_t B, int32_t H, int32_t W);
+int pmg_fit_prompt_fused(const float* logz, int64_t logz_stride, const float* lidar, const float* conf, int32_t B,
+                         int32_t H, int32_t W, int32_t h, int32_t w, int32_t iters, float trim, int32_t min_points,
+                         int32_t soft_gate, pmg_fit_state* state, float* prompt_feats, float* log_d_aff, float* gate,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
 /* depth = s * depth + t per frame, in place (v3.py:777). */
 int pmg_apply_affine(float* depth, const pmg_fit_state* state, int32_t B, int64_t N, void* stream);
 
@@ -399,6 +413,15 @@ typedef struct pmg_refiner_config {
     double output_gate_floor;   /* the gate's floor (the reference's default 0.1) */
     int32_t use_pdl;            /* 1: the captured step graph's kernel-to-kernel edges are programmatic (each kernel
                                    is scheduled while its predecessor finishes and waits for it on the device) */
+    int32_t multi_launch_fit;   /* 0: the per-step LiDAR fit runs as one 16-CTA cluster launch per frame where the
+                                   device and frame size allow (pmg_fit_prompt_fused); 1: always the multi-launch
+                                   fit (prep, sums and radix-select launches).  Same results either way up to the
+                                   summation order of the fp64 sums. */
+    int32_t multi_launch_transitions;   /* 0: each pooling transition (mean pool, pool linear) and the bottleneck's
+                                   second fuse projection run fused with the next block's LayerNorm + SiLU +
+                                   requantise in one row pass where the widths allow (32->64, 64->128, 128->256,
+                                   256->256), and level 0's first LayerNorm rides in the input projection; 1: every
+                                   step in its own launch.  Identical results. */
 } pmg_refiner_config;
 
 int pmg_refiner_create(const pmg_refiner_config* cfg, pmg_refiner** out);

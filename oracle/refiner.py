@@ -52,7 +52,48 @@ def dequant(acc: np.ndarray, s_a, s_w: np.ndarray, b: np.ndarray) -> np.ndarray:
     return ((acc.astype(f32) * f32(s_a)) * s_w[None, :] + b[None, :]).astype(f32)
 
 
+_NATIVE = None
+
+
+def _native():
+    """oracle/_build/liboracle.so (oracle/conv.c, built by oracle/build.py) when present, else None."""
+    global _NATIVE
+    if _NATIVE is None:
+        import ctypes as C
+        from pathlib import Path
+        p = Path(__file__).resolve().parent / "_build" / "liboracle.so"
+        _NATIVE = False
+        if p.exists():
+            try:
+                lib = C.CDLL(str(p))
+                lib.oracle_conv_acc.restype = C.c_int
+                lib.oracle_conv_acc.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_int64, C.c_void_p, C.c_int,
+                                                C.c_int, C.c_void_p]
+                _NATIVE = lib
+            except OSError:
+                _NATIVE = False
+    return _NATIVE or None
+
+
 def conv_acc(q_in: np.ndarray, nmap: np.ndarray, q_w: np.ndarray) -> np.ndarray:
+    """int32 accumulators of a submanifold conv (_core.py:399-441 in integer form).  q_in [M, Ci] int8,
+    nmap [M, 27] int32, q_w [Co, 3, 3, 3, Ci] int8 -> [M, Co] integers (int32 from the C restatement, oracle/conv.c:
+    exact int32 sums on all host threads, used when it is built; int64 from the numpy form below): the same values."""
+    lib = _native()
+    if lib is not None:
+        q = np.ascontiguousarray(q_in, dtype=np.int8)
+        nm = np.ascontiguousarray(nmap, dtype=np.int32)
+        w = np.ascontiguousarray(q_w, dtype=np.int8).reshape(q_w.shape[0], 27, q_w.shape[-1])
+        out = np.empty((nm.shape[0], w.shape[0]), np.int32)
+        rc = lib.oracle_conv_acc(q.ctypes.data, q.shape[0], nm.ctypes.data, nm.shape[0], w.ctypes.data, w.shape[2],
+                                 w.shape[0], out.ctypes.data)
+        if rc != 0:
+            raise ValueError("oracle_conv_acc: neighbour index out of range")
+        return out
+    return conv_acc_numpy(q_in, nmap, q_w)
+
+
+def conv_acc_numpy(q_in: np.ndarray, nmap: np.ndarray, q_w: np.ndarray) -> np.ndarray:
     """int32 accumulators of a submanifold conv (_core.py:399-441 in integer form: per tap, gather the neighbour rows,
     multiply by the tap's weight, add into the output rows).  q_in [M, Ci] int8, nmap [M, 27] int32,
     q_w [Co, 3, 3, 3, Ci] int8 -> [M, Co] int64.

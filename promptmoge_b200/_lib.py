@@ -29,7 +29,8 @@ class RefinerConfig(C.Structure):
                 ("enc_channels", I32), ("lidar_h", I32), ("lidar_w", I32), ("depth_resolution", F32),
                 ("soft_gate", I32), ("fit_iters", I32), ("fit_trim", F32), ("fit_min_points", I32),
                 ("use_prompt", I32), ("capacity", I64 * 8), ("use_tensor_cores", I32), ("max_split", I32),
-                ("output_gate", I32), ("anchor_beta", F32), ("output_gate_floor", C.c_double), ("use_pdl", I32)]
+                ("output_gate", I32), ("anchor_beta", F32), ("output_gate_floor", C.c_double), ("use_pdl", I32),
+                ("multi_launch_fit", I32), ("multi_launch_transitions", I32)]
 
 
 # name -> (restype, argtypes)
@@ -78,6 +79,8 @@ SIGNATURES = {
     "pmg_fit_solve": (I32, [P, P, P, I32, I64, I32, F32, I32, P, P, SZ, P]),
     "pmg_prompt_feats": (I32, [P, I64, P, P, P, I32, I32, I32, I32, I32, I32, P, P]),
     "pmg_affine_frame": (I32, [P, I64, P, P, P, I32, I32, I32, I32, I32, I32, P, P, P]),
+    "pmg_fit_prompt_fused_workspace_bytes": (SZ, [I32, I32, I32]),
+    "pmg_fit_prompt_fused": (I32, [P, I64, P, P, I32, I32, I32, I32, I32, I32, F32, I32, I32, P, P, P, P, P, SZ, P]),
     "pmg_apply_affine": (I32, [P, P, I32, I64, P]),
     "pmg_refiner_create": (I32, [C.POINTER(RefinerConfig), C.POINTER(P)]),
     "pmg_refiner_destroy": (None, [P]),

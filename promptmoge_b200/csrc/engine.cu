@@ -29,6 +29,11 @@ int fit_prep_prompt(const float* logz, int64_t stride, const float* lidar, const
                     int h, int w, float* z, float* y, uint8_t* flags, cudaStream_t s);
 int prompt_feats(const float* logz, int64_t stride, const float* lidar, const float* conf, const pmg_fit_state* st,
                  int B, int H, int W, int h, int w, int soft, float* out, cudaStream_t s);
+bool fit_cluster_supported(int H, int W);
+size_t fit_cluster_workspace_bytes(int B, int H, int W);
+int fit_cluster(const float* logz, int64_t stride, const float* lidar, const float* conf, int B, int H, int W, int h,
+                int w, int iters, float trim, int min_points, int soft, pmg_fit_state* st, float* prompt,
+                float* log_d_aff, float* gate, void* ws, cudaStream_t s);
 int output_gate(const float* cur, const float* refined, float* out, int64_t stride, const float* lidar,
                 const float* conf, int B, int H, int W, int h, int w, double floor_v, cudaStream_t s);
 int anchor_apply(float* logz, int64_t stride, const float* lidar, const float* conf, const pmg_fit_state* st, int B,
@@ -125,6 +130,8 @@ struct pmg_refiner {
     const float* lidar = nullptr;
     const float* conf = nullptr;
     const float* ext_prompt = nullptr;   // caller's prompt features [N][2]: the step skips its own LiDAR fit
+    bool fused_fit = false;              // the per-step fit runs as one cluster launch per frame (fit_cluster.cu)
+    void* fc_ws = nullptr;               // its (z, target) workspace
     // graph
     cudaStream_t cap_stream = nullptr;
     // The voxel structure of a step (voxelise, pools, neighbour maps) depends only on the point map, not on the
@@ -223,6 +230,8 @@ int allocate(pmg_refiner* r) {
     r->fit_ws_bytes = fit_workspace_bytes(B, (int64_t)c.height * c.width);
     PMG_TRY(alloc(r, reinterpret_cast<char**>(&r->fit_ws), r->fit_ws_bytes));
     PMG_CUDA_TRY(cudaMemset(r->fit_ws, 0, r->fit_ws_bytes));
+    if (r->fused_fit)
+        PMG_TRY(alloc(r, reinterpret_cast<char**>(&r->fc_ws), fit_cluster_workspace_bytes(B, c.height, c.width)));
     PMG_TRY(alloc(r, &r->zq, r->N));
     PMG_TRY(alloc(r, &r->lanes0, (size_t)((r->N + 127) / 128) * 27 * 4));
     // split-K for the wide (C >= 128) convs of levels with fewer tile blocks than SMs: up to max_split splits, the
@@ -358,10 +367,12 @@ int dense(const pmg_refiner* r, const int8_t* a, const int32_t* count, int64_t r
 // formed as up.uc[parent] + S (the skip) -- NearestUp + skip add -- and written to X.  When `uq` is given, conv2's
 // epilogue also writes S quantised with `uq_scale` (the input of the next up projection).
 int resblock(pmg_refiner* r, int k, const RB& b, const float* up_src, const int32_t* parent, cudaStream_t s, int& nl,
-             int8_t* uq = nullptr, float uq_scale = 0.f) {
+             int8_t* uq = nullptr, float uq_scale = 0.f, bool ln_done = false) {
     LevelBuf& l = r->lv[k];
     const int32_t* cnt = r->counts + 2 * k;
-    LAUNCH(ln_silu_q8(l.X, up_src, parent, l.S, l.X, cnt, l.cap, l.C, b.norm.g, b.norm.b, 1e-6, b.c1.sa, l.q1, s));
+    // ln_done: the producer of X already wrote LayerNorm + SiLU + requantise of X into q1
+    if (!ln_done)
+        LAUNCH(ln_silu_q8(l.X, up_src, parent, l.S, l.X, cnt, l.cap, l.C, b.norm.g, b.norm.b, 1e-6, b.c1.sa, l.q1, s));
     LAUNCH(conv(r, k, l, l.q1, b.c1, PMG_EPI_SILU_Q8, b.c2.sa, nullptr, l.q2, cnt, s));
     LAUNCH(conv(r, k, l, l.q2, b.c2, PMG_EPI_F32_RESID, 0.f, l.X, l.S, cnt, s, uq, uq_scale));
     return PMG_OK;
@@ -375,7 +386,11 @@ int enqueue_step(pmg_refiner* r, cudaStream_t s) {
     PMG_CUDA_TRY(cudaStreamWaitEvent(r->side, r->ev_fork, 0));
     // --- per-step LiDAR fit + prompt features (v3.py:552-555) --------------------------------------------------- //
     const bool own_fit = c.use_prompt && !r->ext_prompt;
-    if (own_fit) {
+    if (own_fit && r->fused_fit) {
+        // one 16-CTA cluster per frame: prep, the trimmed least squares and the prompt features in one launch
+        LAUNCH(fit_cluster(r->pc + 2, 3, r->lidar, r->conf, B, H, W, c.lidar_h, c.lidar_w, c.fit_iters, c.fit_trim,
+                           c.fit_min_points, c.soft_gate, r->fst, r->prompt, nullptr, nullptr, r->fc_ws, s));
+    } else if (own_fit) {
         LAUNCH(fit_prep_prompt(r->pc + 2, 3, r->lidar, r->conf, B, H, W, c.lidar_h, c.lidar_w, r->fz, r->fy,
                                r->fflags, s));
         size_t nclr = 0;
@@ -408,18 +423,31 @@ int enqueue_step(pmg_refiner* r, cudaStream_t s) {
     }
     PMG_CUDA_TRY(cudaEventRecord(r->ev_struct, ss));
     // --- U-Net ---------------------------------------------------------------------------------------------------- //
-    LAUNCH(input_proj(r->pc, c.use_prompt ? (r->ext_prompt ? r->ext_prompt : r->prompt) : nullptr, r->N, l0.C, r->in_proj.w, r->in_proj.b,
-                      r->pr_proj.w, r->pr_proj.b, l0.X, s));
+    // level 0's first LayerNorm + SiLU + requantise rides in the input projection (row-parallel widths)
+    const bool ln0 = !c.multi_launch_transitions && (l0.C == 32 || l0.C == 64 || l0.C == 128 || l0.C == 256);
+    LAUNCH(input_proj(r->pc, c.use_prompt ? (r->ext_prompt ? r->ext_prompt : r->prompt) : nullptr, r->N, l0.C,
+                      r->in_proj.w, r->in_proj.b, r->pr_proj.w, r->pr_proj.b, l0.X, s, r->down[0].norm.g,
+                      r->down[0].norm.b, 1e-6, r->down[0].c1.sa, ln0 ? l0.q1 : nullptr));
     PMG_CUDA_TRY(cudaStreamWaitEvent(s, r->ev_vox, 0));      // level 0: zq / neighbour map
+    bool ln_done = ln0;
     for (int k = 0; k < L; ++k) {
-        PMG_TRY(resblock(r, k, r->down[k], nullptr, nullptr, s, nl));
+        PMG_TRY(resblock(r, k, r->down[k], nullptr, nullptr, s, nl, nullptr, 0.f, ln_done));
         if (k + 1 < L) {
             LevelBuf& f = r->lv[k];
             LevelBuf& n = r->lv[k + 1];
             const int32_t* ncnt = r->counts + 2 * (k + 1);
             if (k == 0) PMG_CUDA_TRY(cudaStreamWaitEvent(s, r->ev_struct, 0));   // pools and coarser levels
-            LAUNCH(pool_mean(f.S, f.seg_idx, f.seg_off, ncnt, n.cap, f.C, r->pool[k].sa, f.pq, nullptr, s));
-            LAUNCH(dense(r, f.pq, ncnt, n.cap, f.C, n.C, r->pool[k], PMG_EPI_F32, 0.f, nullptr, n.X, s));
+            ln_done = !r->cfg.multi_launch_transitions && transition_supported(f.C, n.C);
+            if (ln_done) {
+                // pool + linear + the next block's norm1 / SiLU / requantise in one row pass
+                LAUNCH(transition(f.S, f.seg_idx, f.seg_off, r->pool[k].sa, nullptr, ncnt, n.cap, f.C, n.C,
+                                  r->pool[k].w, r->pool[k].ws, r->pool[k].b, r->pool[k].sa, n.X,
+                                  r->down[k + 1].norm.g, r->down[k + 1].norm.b, 1e-6, r->down[k + 1].c1.sa, n.q1,
+                                  s));
+            } else {
+                LAUNCH(pool_mean(f.S, f.seg_idx, f.seg_off, ncnt, n.cap, f.C, r->pool[k].sa, f.pq, nullptr, s));
+                LAUNCH(dense(r, f.pq, ncnt, n.cap, f.C, n.C, r->pool[k], PMG_EPI_F32, 0.f, nullptr, n.X, s));
+            }
         }
     }
     {
@@ -437,8 +465,14 @@ int enqueue_step(pmg_refiner* r, cudaStream_t s) {
         PMG_CUDA_TRY(cudaStreamWaitEvent(s, r->ev_frame, capturing && !same_capture ? cudaEventWaitExternal : 0));
         LAUNCH(concat_q8(l.S, r->enc_tok, l.col ? l.col : nullptr, cnt, l.cap, l.C, r->fuse0.sa, r->aq, s));
         LAUNCH(dense(r, r->aq, cnt, l.cap, 2 * l.C, l.C, r->fuse0, PMG_EPI_SILU_Q8, r->fuse2.sa, nullptr, r->g8, s));
-        LAUNCH(dense(r, r->g8, cnt, l.cap, l.C, l.C, r->fuse2, PMG_EPI_F32, 0.f, nullptr, l.X, s));
-        PMG_TRY(resblock(r, L - 1, r->bott, nullptr, nullptr, s, nl, l.uq, r->upl[0].sa));
+        const bool fuse_ln = !r->cfg.multi_launch_transitions && transition_supported(l.C, l.C);
+        if (fuse_ln)   // fuse_proj.2 + the bottleneck block's norm1 / SiLU / requantise in one row pass
+            LAUNCH(transition(nullptr, nullptr, nullptr, 0.f, r->g8, cnt, l.cap, l.C, l.C, r->fuse2.w, r->fuse2.ws,
+                              r->fuse2.b, r->fuse2.sa, l.X, r->bott.norm.g, r->bott.norm.b, 1e-6, r->bott.c1.sa, l.q1,
+                              s));
+        else
+            LAUNCH(dense(r, r->g8, cnt, l.cap, l.C, l.C, r->fuse2, PMG_EPI_F32, 0.f, nullptr, l.X, s));
+        PMG_TRY(resblock(r, L - 1, r->bott, nullptr, nullptr, s, nl, l.uq, r->upl[0].sa, fuse_ln));
     }
     for (int i = 0; i + 1 < L; ++i) {
         const int src = L - 1 - i, t = src - 1;
@@ -512,6 +546,7 @@ extern "C" int pmg_refiner_create(const pmg_refiner_config* cfg, pmg_refiner** o
     if (cfg->enc_channels % 64) return PMG_ERR_UNSUPPORTED;
     auto* r = new pmg_refiner();
     r->cfg = *cfg;
+    r->fused_fit = !cfg->multi_launch_fit && fit_cluster_supported(cfg->height, cfg->width);
     int rc = allocate(r);
     if (rc == PMG_OK) {
         cudaError_t e = cudaStreamCreateWithFlags(&r->cap_stream, cudaStreamNonBlocking);

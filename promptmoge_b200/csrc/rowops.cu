@@ -250,6 +250,37 @@ __device__ __forceinline__ double group_sum(double v) {
     return v;
 }
 
+// LayerNorm (statistics in fp64, rounded once) + SiLU + requantise of one row held as 8 values per lane of its G-lane
+// group; every lane of the warp calls it (the statistics are shuffle trees), `live` marks lanes whose row exists.
+template <int C>
+__device__ __forceinline__ void ln_silu_q8_row(const float (&v)[8], int sub, bool live, const float* sg,
+                                               const float* sb, double eps, float scale, float inv_s,
+                                               int8_t* __restrict__ qrow) {
+    constexpr int G = RowMap<C>::G;
+    double s = 0.0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s += (double)v[k];
+    const double mean = group_sum<G>(s) / C;
+    double ss = 0.0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const double d = (double)v[k] - mean;
+        ss += d * d;
+    }
+    ss = group_sum<G>(ss);
+    if (!live) return;
+    const float rstd = __double2float_rn(1.0 / sqrt(ss / C + eps));
+    const float shift = __fmul_rn(-rstd, __double2float_rn(mean));
+    int qv[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const int c = chan8<C>(sub, k);
+        const float y = __fadd_rn(__fmul_rn(__fadd_rn(__fmul_rn(v[k], rstd), shift), sg[c]), sb[c]);
+        qv[k] = silu_quant8_fast(y, scale, inv_s);
+    }
+    store8_q8<C>(qrow, sub, qv);
+}
+
 template <int C>
 __global__ void __launch_bounds__(256) k_ln_silu_rows(const float* __restrict__ x, const float* __restrict__ up_src,
                                                       const int32_t* __restrict__ parent,
@@ -287,28 +318,7 @@ __global__ void __launch_bounds__(256) k_ln_silu_rows(const float* __restrict__ 
 #pragma unroll
             for (int k = 0; k < 8; ++k) v[k] = 0.f;
         }
-        double s = 0.0;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) s += (double)v[k];
-        const double mean = group_sum<G>(s) / C;
-        double ss = 0.0;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const double d = (double)v[k] - mean;
-            ss += d * d;
-        }
-        ss = group_sum<G>(ss);
-        if (!live) continue;
-        const float rstd = __double2float_rn(1.0 / sqrt(ss / C + eps));
-        const float shift = __fmul_rn(-rstd, __double2float_rn(mean));
-        int qv[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const int c = chan8<C>(sub, k);
-            const float y = __fadd_rn(__fmul_rn(__fadd_rn(__fmul_rn(v[k], rstd), shift), sg[c]), sb[c]);
-            qv[k] = silu_quant8_fast(y, scale, inv_s);
-        }
-        store8_q8<C>(q + m * C, sub, qv);
+        ln_silu_q8_row<C>(v, sub, live, sg, sb, eps, scale, inv_s, q + m * C);
     }
 }
 
@@ -366,14 +376,18 @@ __global__ void __launch_bounds__(256) k_pool_mean_rows_f(const float* __restric
     pool_mean_rows<C, false>(x, seg_idx, seg_off, count, max_rows, scale, q, out, mean);
 }
 
+// Input + prompt projections of level 0 (sparse_unet.py:189-192), and when `q` is given the first residual block's
+// LayerNorm + SiLU + requantise of the result in the same pass (the row is already in registers).
 template <int C>
 __global__ void __launch_bounds__(256) k_input_proj_rows(const float* __restrict__ pc, const float* __restrict__ prompt,
                                                          int64_t N, const float* __restrict__ wi,
                                                          const float* __restrict__ bi, const float* __restrict__ wp,
-                                                         const float* __restrict__ bp, float* __restrict__ x0) {
+                                                         const float* __restrict__ bp, float* __restrict__ x0,
+                                                         const float* __restrict__ gamma, const float* __restrict__ beta,
+                                                         double eps, float scale, int8_t* __restrict__ q) {
     pdl_begin();
     constexpr int G = RowMap<C>::G, RPB = RowMap<C>::RPB;
-    __shared__ float s_wi[3 * C], s_bi[C], s_wp[2 * C], s_bp[C];
+    __shared__ float s_wi[3 * C], s_bi[C], s_wp[2 * C], s_bp[C], sg[C], sb[C];
     for (int i = threadIdx.x; i < C; i += blockDim.x) {
         s_wi[3 * i] = wi[3 * i];
         s_wi[3 * i + 1] = wi[3 * i + 1];
@@ -384,32 +398,45 @@ __global__ void __launch_bounds__(256) k_input_proj_rows(const float* __restrict
             s_wp[2 * i + 1] = wp[2 * i + 1];
             s_bp[i] = bp[i];
         }
+        if (q) {
+            sg[i] = gamma[i];
+            sb[i] = beta[i];
+        }
     }
     __syncthreads();
+    const float inv_s = q ? 1.0f / scale : 0.f;
     const int sub = threadIdx.x % G;
-    for (int64_t m = (int64_t)blockIdx.x * RPB + threadIdx.x / G; m < N; m += (int64_t)gridDim.x * RPB) {
-        const double p0 = pc[m * 3], p1 = pc[m * 3 + 1], p2 = pc[m * 3 + 2];
-        double r0 = 0.0, r1 = 0.0;
-        if (prompt) {
-            r0 = prompt[m * 2];
-            r1 = prompt[m * 2 + 1];
-        }
+    for (int64_t base = (int64_t)blockIdx.x * RPB; base < N; base += (int64_t)gridDim.x * RPB) {
+        const int64_t m = base + threadIdx.x / G;
+        const bool live = m < N;
         float y[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-            const int n = chan8<C>(sub, k);
-            double a = p0 * (double)s_wi[n * 3];
-            a = fma(p1, (double)s_wi[n * 3 + 1], a);
-            a = fma(p2, (double)s_wi[n * 3 + 2], a);
-            float v = __double2float_rn(a + (double)s_bi[n]);
+        if (live) {
+            const double p0 = pc[m * 3], p1 = pc[m * 3 + 1], p2 = pc[m * 3 + 2];
+            double r0 = 0.0, r1 = 0.0;
             if (prompt) {
-                double b2 = r0 * (double)s_wp[n * 2];
-                b2 = fma(r1, (double)s_wp[n * 2 + 1], b2);
-                v = __fadd_rn(v, __double2float_rn(b2 + (double)s_bp[n]));
+                r0 = prompt[m * 2];
+                r1 = prompt[m * 2 + 1];
             }
-            y[k] = v;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const int n = chan8<C>(sub, k);
+                double a = p0 * (double)s_wi[n * 3];
+                a = fma(p1, (double)s_wi[n * 3 + 1], a);
+                a = fma(p2, (double)s_wi[n * 3 + 2], a);
+                float v = __double2float_rn(a + (double)s_bi[n]);
+                if (prompt) {
+                    double b2 = r0 * (double)s_wp[n * 2];
+                    b2 = fma(r1, (double)s_wp[n * 2 + 1], b2);
+                    v = __fadd_rn(v, __double2float_rn(b2 + (double)s_bp[n]));
+                }
+                y[k] = v;
+            }
+            store8<C>(x0 + m * C, sub, y);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) y[k] = 0.f;
         }
-        store8<C>(x0 + m * C, sub, y);
+        if (q) ln_silu_q8_row<C>(y, sub, live, sg, sb, eps, scale, inv_s, q + m * C);
     }
 }
 
@@ -444,6 +471,101 @@ __global__ void __launch_bounds__(256) k_out_apply_rows(const float* __restrict_
             pc_out[m * 3 + 1] = pc_in[m * 3 + 1];
             pc_out[m * 3 + 2] = __fadd_rn(lz, d);
         }
+    }
+}
+
+// One U-Net transition into level k+1 as a single row-parallel pass (sparse_unet.py:217-225 + flex_sparse_blocks.py
+// PoolDown and the next SparseResBlock3d's norm1): per output row, the mean of its children's fp32 rows quantised
+// with the pool linear's input scale (the pool_mean_rows arithmetic), the int8 linear by dp4a (exact int32 sums, the
+// same integers the tensor-core GEMM accumulates), dequant + bias -> the level's fp32 input X, then LayerNorm + SiLU +
+// requantise of X into the first conv's int8 input.  With `a8` given instead of pooling inputs, the int8 input rows
+// are read directly (the bottleneck's second fuse projection).  K -> N in {32->64, 64->128, 128->256, 256->256}.
+// Layout: RowMap<N> (G = N/8 lanes per output row, 8 output channels per lane); the quantised input row goes through
+// shared memory; the weight sits in shared memory as [K/4][N] 32-bit words (4 input channels of one output).
+template <int K, int N>
+__global__ void __launch_bounds__(256) k_transition_rows(
+    const float* __restrict__ x, const int32_t* __restrict__ seg_idx, const int32_t* __restrict__ seg_off,
+    float pool_scale, const int8_t* __restrict__ a8, const int32_t* __restrict__ count, int64_t max_rows,
+    const int8_t* __restrict__ w, const float* __restrict__ w_scale, const float* __restrict__ bias, float sa,
+    float* __restrict__ x_out, const float* __restrict__ gamma, const float* __restrict__ beta, double eps,
+    float q_scale, int8_t* __restrict__ q) {
+    pdl_begin();
+    constexpr int G = RowMap<N>::G, RPB = RowMap<N>::RPB;
+    constexpr int GK = K / 8;                   // lanes that pool one input row (RowMap<K> layout)
+    static_assert(GK <= G, "input row wider than its output lane group");
+    extern __shared__ __align__(16) uint32_t w4[];           // [K / 4][N + 4] (rows padded against bank conflicts)
+    __shared__ __align__(16) int8_t qin[RPB][K];
+    __shared__ float s_ws[N], s_b[N], sg[N], sb[N];
+    constexpr int WS = N + 4;                   // padded row stride of w4 in words
+    for (int i = threadIdx.x; i < (K / 4) * N; i += blockDim.x) {
+        const int n = i / (K / 4), j = i - (i / (K / 4)) * (K / 4);     // consecutive threads: one weight row
+        w4[j * WS + n] = reinterpret_cast<const uint32_t*>(w)[i];
+    }
+    for (int i = threadIdx.x; i < N; i += blockDim.x) {
+        s_ws[i] = w_scale[i];
+        s_b[i] = bias[i];
+        sg[i] = gamma[i];
+        sb[i] = beta[i];
+    }
+    __syncthreads();
+    const float inv_s = 1.0f / q_scale;
+    const int64_t M = rows_of(count, max_rows);
+    const int sub = threadIdx.x % G, slot = threadIdx.x / G;
+    int8_t* qrow = qin[slot];
+    for (int64_t base = (int64_t)blockIdx.x * RPB; base < M; base += (int64_t)gridDim.x * RPB) {
+        const int64_t o = base + slot;
+        const bool live = o < M;
+        // ---- the row's int8 input into shared memory
+        if (live && sub < GK) {
+            if (a8) {
+                *reinterpret_cast<uint2*>(qrow + 8 * sub) = reinterpret_cast<const uint2*>(a8 + o * K)[sub];
+            } else {
+                const int lo = seg_off[o], hi = seg_off[o + 1];
+                float acc[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+                for (int j = lo; j < hi; ++j) {
+                    float v[8];
+                    load8<K>(x + (int64_t)seg_idx[j] * K, sub, v);
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) acc[k] = __fadd_rn(acc[k], v[k]);
+                }
+                const float n = (float)max(hi - lo, 1);
+#pragma unroll
+                for (int k = 0; k < 8; ++k) qrow[chan8<K>(sub, k)] = (int8_t)quant8(__fdiv_rn(acc[k], n), pool_scale);
+            }
+        }
+        __syncwarp();
+        // ---- int8 linear: outputs 4*sub + 0..3 and 4*(sub + G) + 0..3
+        int acc[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[k] = 0;
+        if (live) {
+            const uint32_t* qw = reinterpret_cast<const uint32_t*>(qrow);
+#pragma unroll 4
+            for (int j = 0; j < K / 4; ++j) {
+                const int a = (int)qw[j];
+                const uint4 lo4 = reinterpret_cast<const uint4*>(w4 + j * WS)[sub];
+                const uint4 hi4 = reinterpret_cast<const uint4*>(w4 + j * WS)[sub + G];
+                acc[0] = __dp4a(a, (int)lo4.x, acc[0]);
+                acc[1] = __dp4a(a, (int)lo4.y, acc[1]);
+                acc[2] = __dp4a(a, (int)lo4.z, acc[2]);
+                acc[3] = __dp4a(a, (int)lo4.w, acc[3]);
+                acc[4] = __dp4a(a, (int)hi4.x, acc[4]);
+                acc[5] = __dp4a(a, (int)hi4.y, acc[5]);
+                acc[6] = __dp4a(a, (int)hi4.z, acc[6]);
+                acc[7] = __dp4a(a, (int)hi4.w, acc[7]);
+            }
+        }
+        __syncwarp();           // the row buffer is rewritten by the next iteration
+        float y[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int c = chan8<N>(sub, k);
+            y[k] = live ? dequant(acc[k], sa, s_ws[c], s_b[c]) : 0.f;
+        }
+        if (live) store8<N>(x_out + o * N, sub, y);
+        ln_silu_q8_row<N>(y, sub, live, sg, sb, eps, q_scale, inv_s, q + o * N);
     }
 }
 
@@ -548,16 +670,55 @@ int planar_to_rows(const float* f, int B, int C, int T, float* out, cudaStream_t
 }
 
 int input_proj(const float* pc, const float* prompt, int64_t N, int C, const float* wi, const float* bi,
-               const float* wp, const float* bp, float* x0, cudaStream_t st) {
+               const float* wp, const float* bp, float* x0, cudaStream_t st, const float* gamma, const float* beta,
+               double eps, float scale, int8_t* q) {
     if (N == 0) return PMG_OK;
-    if (rows_ok(C, {x0})) {
-        PMG_ROWS_DISPATCH(C, k_input_proj_rows, N, pc, prompt, N, wi, bi, wp, bp, x0)
+    if (rows_ok(C, {x0, q})) {
+        PMG_ROWS_DISPATCH(C, k_input_proj_rows, N, pc, prompt, N, wi, bi, wp, bp, x0, gamma, beta, eps, scale, q)
         PMG_LAUNCH_CHECK();
         return PMG_OK;
     }
+    if (q) return PMG_ERR_UNSUPPORTED;
     k_input_proj<<<grid_for(N * C, 256), 256, 0, st>>>(pc, prompt, N, C, wi, bi, wp, bp, x0);
     PMG_LAUNCH_CHECK();
     return PMG_OK;
+}
+
+// Transition into level k+1 (pool + linear + norm1 + SiLU + requantise) in one pass; PMG_ERR_UNSUPPORTED for
+// widths it does not cover.  Either the pooling inputs (x, seg_idx, seg_off, pool_scale) or a8 are given.
+int transition(const float* x, const int32_t* seg_idx, const int32_t* seg_off, float pool_scale, const int8_t* a8,
+               const int32_t* count, int64_t max_rows, int K, int N, const int8_t* w, const float* w_scale,
+               const float* bias, float sa, float* x_out, const float* gamma, const float* beta, double eps,
+               float q_scale, int8_t* q, cudaStream_t st) {
+    if (max_rows == 0) return PMG_OK;
+    if (!rows_ok(N, {x_out, q}) || (x && (reinterpret_cast<uintptr_t>(x) & 15)) ||
+        (a8 && (reinterpret_cast<uintptr_t>(a8) & 7)) || (reinterpret_cast<uintptr_t>(w) & 3))
+        return PMG_ERR_UNSUPPORTED;
+    // every CTA stages the whole weight in shared memory: few enough CTAs that each serves many rows with it
+    const int64_t rpb = 256 / (N / 8);
+    const int64_t cap = (int64_t)kNumSMs * ((int64_t)K * N <= 8192 ? 8 : 2);
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((max_rows + rpb - 1) / rpb, cap));
+    const size_t smem = (size_t)K / 4 * (N + 4) * sizeof(uint32_t);
+#define PMG_TRANSITION(KK, NN)                                                                                    \
+    if (K == KK && N == NN) {                                                                                    \
+        PMG_CUDA_TRY(cudaFuncSetAttribute(k_transition_rows<KK, NN>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
+                                          (int)smem));                                                           \
+        k_transition_rows<KK, NN><<<grid, 256, smem, st>>>(x, seg_idx, seg_off, pool_scale, a8, count, max_rows, \
+                                                           w, w_scale, bias, sa, x_out, gamma, beta, eps,        \
+                                                           q_scale, q);                                          \
+        PMG_LAUNCH_CHECK();                                                                                      \
+        return PMG_OK;                                                                                           \
+    }
+    PMG_TRANSITION(32, 64)
+    PMG_TRANSITION(64, 128)
+    PMG_TRANSITION(128, 256)
+    PMG_TRANSITION(256, 256)
+#undef PMG_TRANSITION
+    return PMG_ERR_UNSUPPORTED;
+}
+
+bool transition_supported(int K, int N) {
+    return (K == 32 && N == 64) || (K == 64 && N == 128) || (K == 128 && N == 256) || (K == 256 && N == 256);
 }
 
 int out_apply(const float* x, int64_t N, int C, const float* wo, const float* bo, const float* pc_in, float* pc_out,

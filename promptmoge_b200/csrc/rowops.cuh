@@ -56,9 +56,19 @@ int concat_q8(const float* x, const float* enc_tok, const int32_t* col, const in
               float scale, int8_t* q, cudaStream_t st);
 int tokens_q8(const void* f16, int B, int K, int T, float scale, int8_t* q, cudaStream_t st);
 int planar_to_rows(const float* f, int B, int C, int T, float* out, cudaStream_t st);
+// Input + prompt projections; with `q`, also the LayerNorm (gamma, beta, eps) + SiLU + requantise (scale) of the
+// result into q (the first residual block's conv1 input).
 int input_proj(const float* pc, const float* prompt, int64_t N, int C, const float* wi, const float* bi,
-               const float* wp, const float* bp, float* x0, cudaStream_t st);
+               const float* wp, const float* bp, float* x0, cudaStream_t st, const float* gamma = nullptr,
+               const float* beta = nullptr, double eps = 0.0, float scale = 0.f, int8_t* q = nullptr);
 int out_apply(const float* x, int64_t N, int C, const float* wo, const float* bo, const float* pc_in, float* pc_out,
               float* delta, cudaStream_t st);
+// A U-Net transition into level k+1 in one row pass: mean pool of x's children (or the int8 rows a8) -> int8 linear
+// [N][K] -> fp32 x_out -> LayerNorm + SiLU + requantise into q.  PMG_ERR_UNSUPPORTED outside the covered widths.
+int transition(const float* x, const int32_t* seg_idx, const int32_t* seg_off, float pool_scale, const int8_t* a8,
+               const int32_t* count, int64_t max_rows, int K, int N, const int8_t* w, const float* w_scale,
+               const float* bias, float sa, float* x_out, const float* gamma, const float* beta, double eps,
+               float q_scale, int8_t* q, cudaStream_t st);
+bool transition_supported(int K, int N);
 
 }  // namespace pmg

@@ -57,15 +57,20 @@ class ShardedRefiner:
         rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.begin, self.end = frame_range(n_frames, rank, world)
 
-    def run(self, frames, K: int = 1):
+    def run(self, frames, K: int = 1, batch_frames=None):
         """Returns (refined point maps of this rank's frames [n_local,H,W,3] host, all frames' fit states
-        [n_frames, 18] int32 on this rank's device)."""
+        [n_frames, 18] int32 on this rank's device).  batch_frames(ids), when given, returns the five inputs of a
+        whole batch of frames at once (already concatenated, e.g. pinned host tensors), instead of frames(i) per
+        frame."""
         B = self.refiner.geo.batch
         outs, fits = [], []
         for f0 in range(self.begin, self.end, B):
             ids = [min(f, self.end - 1) for f in range(f0, f0 + B)]      # the last batch repeats its final frame
-            parts = [frames(i) for i in ids]
-            cat = [np.concatenate([p[k] for p in parts]) if parts[0][k] is not None else None for k in range(5)]
+            if batch_frames is not None:
+                cat = list(batch_frames(ids))
+            else:
+                parts = [frames(i) for i in ids]
+                cat = [np.concatenate([p[k] for p in parts]) if parts[0][k] is not None else None for k in range(5)]
             pc, fit = self.refiner.refine(*cat[:4], uv_bias=cat[4], K=K)
             n = min(B, self.end - f0)
             outs.append(pc[:n].clone())

@@ -85,7 +85,7 @@ class RefinerEngine:
     def __init__(self, weights: dict, clips: dict, geometry: Geometry, device="cuda", capacity=None,
                  use_prompt: bool = True, tensor_cores: bool = True, max_split: int = 4,
                  output_gate_floor: float | None = None, anchor_beta: float = 0.0, pdl: bool = True,
-                 soft_gate: bool = True):
+                 soft_gate: bool = True, multi_launch_fit: bool = False, multi_launch_transitions: bool = False):
         _lib.load()
         self.geo = geometry
         self.device = torch.device(device)
@@ -109,6 +109,8 @@ class RefinerEngine:
         cfg.output_gate_floor = float(output_gate_floor) if output_gate_floor is not None else 0.1
         cfg.anchor_beta = float(anchor_beta)
         cfg.use_pdl = int(pdl)
+        cfg.multi_launch_fit = int(multi_launch_fit)
+        cfg.multi_launch_transitions = int(multi_launch_transitions)
         for k in range(L):
             cfg.capacity[k] = int(capacity[k]) if capacity is not None else 0
         self._cfg = cfg

@@ -320,6 +320,21 @@ def fit_prep_final(depth, lidar, conf, mask01=None):
     return z, y, fl
 
 
+def fit_prompt_fused(logz, lidar, conf, soft_gate=True, iters=4, trim=0.2, min_points=32):
+    """The one-launch per-step fit (pmg_fit_prompt_fused): (state [B,18] int32 view of pmg_fit_state, prompt
+    features [B*H*W,2]) from logz [B,H,W] (contiguous or a point map's logz channel) and the LiDAR."""
+    lz, st = _elem_strided(logz)
+    B, H, W = logz.shape
+    h, w = lidar.shape[-2:]
+    state = _fit_state(B, logz.device)
+    out = torch.empty((B * H * W, 2), dtype=torch.float32, device=logz.device)
+    nbytes = _lib.load().pmg_fit_prompt_fused_workspace_bytes(B, H, W)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=logz.device)
+    call("pmg_fit_prompt_fused", _p(lz), st, _p(lidar), _p(conf), B, H, W, h, w, iters, float(trim), min_points,
+         int(soft_gate), _p(state), _p(out), None, None, _p(ws), nbytes, _stream())
+    return state, out
+
+
 def prompt_feats(logz, lidar, conf, state, soft_gate=True):
     B, H, W = logz.shape
     h, w = lidar.shape[-2:]
@@ -352,11 +367,12 @@ def affine_frame(logz, lidar, conf, state, soft_gate=True):
     return log_d_aff, gate
 
 
-def lidar_in_affine_frame(logz, lidar, conf, soft_gate=False, iters=4, trim=0.2, min_points=32):
+def lidar_in_affine_frame(logz, lidar, conf, soft_gate=False, iters=4, trim=0.2, min_points=32, fused=True):
     """MoGeModel._lidar_in_affine_frame (moge/model/v3.py:362-383) on the device: the trimmed least-squares fit of the
     nearest-resized confident LiDAR to exp(logz) (prompt_stem.fit_scale_shift, prompt_stem.py:211-240), then the
     LiDAR in the affine log-depth frame.  logz [B,H,W] fp32 (a strided view of a point map's logz channel is read in
-    place), lidar / conf [B,1,h,w] fp32.  Returns (log_d_aff [B,H,W], gate [B,H,W], s [B], t [B])."""
+    place), lidar / conf [B,1,h,w] fp32.  Returns (log_d_aff [B,H,W], gate [B,H,W], s [B], t [B]).  fused: one
+    cluster launch per frame (pmg_fit_prompt_fused) where the frame size allows, else the multi-launch kernels."""
     if not logz.is_cuda or logz.dtype != torch.float32:
         raise ValueError("logz must be a float32 CUDA tensor (no CPU path)")
     _dev(lidar, torch.float32, "lidar")
@@ -365,6 +381,20 @@ def lidar_in_affine_frame(logz, lidar, conf, soft_gate=False, iters=4, trim=0.2,
     B, H, W = logz.shape
     h, w = lidar.shape[-2:]
     dev = logz.device
+    if fused:
+        state = _fit_state(B, dev)
+        log_d_aff = torch.empty((B, H, W), dtype=torch.float32, device=dev)
+        gate = torch.empty((B, H, W), dtype=torch.float32, device=dev)
+        nbytes = _lib.load().pmg_fit_prompt_fused_workspace_bytes(B, H, W)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        rc = _lib.load().pmg_fit_prompt_fused(_p(lz), st, _p(lidar), _p(conf), B, H, W, h, w, iters, float(trim),
+                                               min_points, int(soft_gate), _p(state), None, _p(log_d_aff), _p(gate),
+                                               _p(ws), nbytes, _stream())
+        if rc == 0:
+            sv = state.view(torch.float32)[:, :2]
+            return log_d_aff, gate, sv[:, 0].clone(), sv[:, 1].clone()
+        if rc != 5:          # PMG_ERR_UNSUPPORTED: this frame size / device takes the multi-launch fit below
+            raise _lib.PmgError("pmg_fit_prompt_fused", rc)
     z = torch.empty((B, H * W), dtype=torch.float32, device=dev)
     y = torch.empty((B, H * W), dtype=torch.float32, device=dev)
     fl = torch.empty((B, H * W), dtype=torch.uint8, device=dev)

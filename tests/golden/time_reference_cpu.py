@@ -104,7 +104,7 @@ def main():
                           "torch.inference_mode, torch.set_num_threads(os.cpu_count())",
         "port_s_per_step": round(float(np.median(port_t)), 4),
         "port_steps": [round(x, 4) for x in port_t],
-        "port_path": "oracle.refiner.refine_step + oracle.fit.final_fit (numpy; this repository's CPU restatement)",
+        "port_path": "oracle.refiner.refine_step + oracle.fit.final_fit (this repository's CPU restatement: int8 convs in C with OpenMP, oracle/conv.c; the rest numpy)",
     }
     res["port_over_reference"] = round(res["port_s_per_step"] / res["reference_s_per_step"], 3)
     (HERE / "reference_cpu_timing.json").write_text(json.dumps(res, indent=1) + "\n")

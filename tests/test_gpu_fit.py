@@ -85,3 +85,66 @@ def test_fit_edge_cases():
     for b in range(B):
         assert got[b]["s"] == so[b] and got[b]["t"] == to[b], b
     assert got[0]["s"] == 1.0 and got[0]["t"] == 0.0 and got[0]["ok"] == 0
+
+
+def _fused_vs_multi(pc, ld, lc, soft=True):
+    from promptmoge_b200 import ops
+    st_f, pf_f = ops.fit_prompt_fused(pc[..., 2], ld, lc, soft_gate=soft)
+    z, y, fl = ops.fit_prep_prompt(pc, ld, lc)
+    st_m = ops.fit_solve(z, y, fl)
+    pf_m = ops.prompt_feats(pc[..., 2].contiguous(), ld, lc, st_m, soft_gate=soft)
+    torch.cuda.synchronize()
+    return ops.fit_state_view(st_f), pf_f, ops.fit_state_view(st_m), pf_m
+
+
+@pytest.mark.parametrize("name", ["B_small", "A_small", "B_full", "A_full"])
+def test_one_launch_fit_equals_multi_launch_fit(golden, name):
+    """The 16-CTA cluster fit (one launch: prep, 4 trimmed iterations, prompt features) reaches the multi-launch
+    fit's state and prompt features bit for bit, and the reference's (s, t)."""
+    g = golden(name)
+    sc = g.scene()
+    pc = torch.from_numpy(sc.point_coord).cuda()
+    ld = torch.from_numpy(sc.lidar_depth).cuda()
+    lc = torch.from_numpy(sc.lidar_conf).cuda()
+    f, pf_f, m, pf_m = _fused_vs_multi(pc, ld, lc)
+    for key in ("s", "t", "thr", "count", "k", "ok"):
+        assert f[0][key] == m[0][key], key
+    assert f[0]["sums"] == m[0]["sums"]
+    assert torch.equal(pf_f, pf_m)
+    st_ref = g["s0_fit_st"][0]
+    assert abs(f[0]["s"] - st_ref[0]) <= 1e-4 * abs(st_ref[0]) and abs(f[0]["t"] - st_ref[1]) <= 1e-4
+
+
+def test_one_launch_fit_batch_and_edge_cases():
+    """Three frames in one launch (three clusters): an ordinary frame, one with fewer than 32 confident pixels
+    (no fit: s = 1, t = 0), and one where every pixel is confident; each equals the multi-launch fit, hard and soft
+    gate."""
+    from promptmoge_b200 import synth
+    scs = [synth.make_scene(s, 120, 160, 8, 256) for s in (51, 52, 53)]
+    pc = torch.from_numpy(np.concatenate([s.point_coord for s in scs])).cuda()
+    ld = np.concatenate([s.lidar_depth for s in scs])
+    lc = np.concatenate([s.lidar_conf for s in scs])
+    lc[1] = 0.0
+    lc[1, 0, 0, :10] = 2.0
+    lc[2] = 2.0
+    ld[2] = np.where(ld[2] > 0, ld[2], 1.5)
+    ld, lc = torch.from_numpy(ld).cuda(), torch.from_numpy(lc).cuda()
+    for soft in (True, False):
+        f, pf_f, m, pf_m = _fused_vs_multi(pc, ld, lc, soft)
+        for b in range(3):
+            for key in ("s", "t", "thr", "count", "k", "ok"):
+                assert f[b][key] == m[b][key], (b, key)
+        assert f[1]["ok"] == 0 and f[1]["s"] == 1.0 and f[1]["t"] == 0.0
+        assert torch.equal(pf_f, pf_m)
+
+
+def test_one_launch_fit_refuses_frames_beyond_its_shared_memory():
+    from promptmoge_b200 import _lib
+    lib = _lib.load()
+    t = torch.zeros(8, dtype=torch.float32, device="cuda")
+    st = torch.zeros((1, 18), dtype=torch.int32, device="cuda")
+    # 4096 x 4096 pixels: a 1,048,576-pixel slice per CTA (4 MB of residuals) cannot sit in shared memory
+    ws = torch.empty(lib.pmg_fit_prompt_fused_workspace_bytes(1, 4096, 4096), dtype=torch.uint8, device="cuda")
+    rc = lib.pmg_fit_prompt_fused(t.data_ptr(), 1, t.data_ptr(), t.data_ptr(), 1, 4096, 4096, 192, 256, 4, 0.2, 32, 1,
+                                  st.data_ptr(), t.data_ptr(), None, None, ws.data_ptr(), ws.numel(), None)
+    assert rc == 5      # PMG_ERR_UNSUPPORTED, nothing launched

@@ -272,3 +272,56 @@ def test_set_frame_captured_with_the_steps():
         del g
     finally:
         eng.close()
+
+
+@pytest.mark.parametrize("name", ["A_full", "B_small"])
+def test_one_launch_fit_plan_equals_multi_launch_fit_plan(golden, name):
+    """The step with its LiDAR fit as one cluster launch refines to the same bits as the step with the
+    multi-launch fit."""
+    from promptmoge_b200 import synth
+    from promptmoge_b200.engine import Geometry, RefinerEngine
+    g = golden(name)
+    sc = g.scene()
+    c = g.config
+    geo = Geometry(channels=synth.MODELS[c["model"]]["model_channels"], height=c["H"], width=c["W"])
+    outs = []
+    for multi in (True, False):
+        eng = RefinerEngine(g.weights(), g.clips, geo, multi_launch_fit=multi)
+        _inputs(eng, sc)
+        eng.capture(1)
+        out, fit = eng.replay()
+        outs.append((out.clone(), fit.clone(), eng.launches_per_step()))
+        assert eng.status()[0] == 0
+        eng.close()
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+    assert outs[1][2] < outs[0][2]          # the one-launch fit is in use where supported
+
+
+@pytest.mark.parametrize("name", ["A_full", "B_full", "A_small"])
+def test_fused_transitions_plan_equals_multi_launch_plan(golden, name):
+    """Pool + linear + the next block's LayerNorm / SiLU / requantise in one row pass (every pooling transition, the
+    bottleneck's second fuse projection) and the level-0 LayerNorm inside the input projection refine to the same bits
+    as the plan that runs each of those steps as its own launch (the int8 linear by dp4a sums the same integers the
+    tensor-core GEMM does)."""
+    from promptmoge_b200 import synth
+    from promptmoge_b200.engine import Geometry, RefinerEngine
+    g = golden(name)
+    sc = g.scene()
+    c = g.config
+    geo = Geometry(channels=synth.MODELS[c["model"]]["model_channels"], height=c["H"], width=c["W"])
+    outs = []
+    for multi in (True, False):
+        eng = RefinerEngine(g.weights(), g.clips, geo, multi_launch_transitions=multi)
+        _inputs(eng, sc)
+        eng.capture(1)
+        out, fit = eng.replay()
+        L = geo.levels
+        qs = [eng.debug_tensor("q1", k, (eng.level_info(k)["cap"], geo.channels[k]), torch.int8)[:eng.status(False)[1][k]].clone()
+              for k in range(L)]
+        outs.append((out.clone(), qs, eng.launches_per_step()))
+        assert eng.status()[0] == 0
+        eng.close()
+    assert torch.equal(outs[0][0], outs[1][0])
+    for a, b in zip(outs[0][1], outs[1][1]):
+        assert torch.equal(a, b)
+    assert outs[1][2] < outs[0][2]
