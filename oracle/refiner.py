@@ -80,7 +80,7 @@ def conv_acc(q_in: np.ndarray, nmap: np.ndarray, q_w: np.ndarray) -> np.ndarray:
     nmap [M, 27] int32, q_w [Co, 3, 3, 3, Ci] int8 -> [M, Co] integers (int32 from the C restatement, oracle/conv.c:
     exact int32 sums on all host threads, used when it is built; int64 from the numpy form below): the same values."""
     lib = _native()
-    if lib is not None:
+    if lib is not None and q_w.shape[0] % 16 == 0 and q_w.shape[-1] % 2 == 0:
         q = np.ascontiguousarray(q_in, dtype=np.int8)
         nm = np.ascontiguousarray(nmap, dtype=np.int32)
         w = np.ascontiguousarray(q_w, dtype=np.int8).reshape(q_w.shape[0], 27, q_w.shape[-1])
