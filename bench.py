@@ -510,6 +510,40 @@ def cpu_baseline(batch=1, steps=1):
             "reference_measured": reference_cpu_record()}
 
 
+def profile_step(args):
+    """Profiling driver (run under ncu, one kernel family per capture with -k): the 480x640 Model A refine step of
+    the benchmark frame replayed --steps times after one sizing run (every structure, fit, row and conv kernel of the
+    step), then one hash neighbour map over a 2M-voxel surface-shell set (the generic-voxel-set builder of
+    configuration 3) and one output path of the refined frame (the gauge fit).  Not a bench value."""
+    import torch
+    from promptmoge_b200 import ops, post, synth
+    from promptmoge_b200.refine import Refiner, pinned, synthetic_model
+    torch.cuda.set_device(0)
+    weights, clips = synthetic_model("A", 0)
+    sc = synth.make_scene(0, 480, 640, 16, 256)
+    ref = Refiner(weights, clips, "A")
+    h = [pinned(x) for x in (sc.point_coord, sc.lidar_depth, sc.lidar_conf, sc.encoder_feature, sc.uv_bias)]
+    ref.refine(*h[:4], uv_bias=h[4])
+    rc, counts = ref.engine.status()
+    ref.engine.fit_to(counts)
+    ref._K = None
+    flush = torch.empty(256 << 18, dtype=torch.float32, device="cuda")
+    for _ in range(max(1, args.steps)):
+        flush.zero_()
+        out, _ = ref.refine(*h[:4], uv_bias=h[4])
+    coords = torch.from_numpy(synth.make_surface_voxels(2_000_000, seed=5)).cuda()
+    nmap, mask, st = ops.nmap_hash(coords, [1, 1 << 21, 1 << 21, 1 << 21])
+    torch.cuda.synchronize()
+    coords_out = out.cuda()
+    ld, lc = torch.from_numpy(sc.lidar_depth).cuda(), torch.from_numpy(sc.lidar_conf).cuda()
+    pg = post.PostGraph(1, (480, 640), (480, 640), (192, 256), device="cuda")
+    pg.run(coords_out, ld, lc)
+    torch.cuda.synchronize()
+    ref.close()
+    return {"profile_step": True, "steps": args.steps, "levels_voxels": counts, "hash_voxels": int(coords.shape[0]),
+            "hash_status": int(st.item())}
+
+
 def profile_conv(args):
     """Profiling driver (run under ncu): the real 480x640 level structure of the benchmark frame, random int8
     activations and weights, `--steps` launches of that level's conv (fused SiLU + requantise epilogue).  Only the
@@ -750,6 +784,8 @@ def main():
     ap.add_argument("--ncu", action="store_true", help="profiling mode: warm-up + timed replays only, no extras")
     ap.add_argument("--profile-conv", type=int, default=None, metavar="LEVEL",
                     help="profiling driver: launch one level's conv --steps times on the benchmark frame's structure")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="profiling driver: --steps refine steps, a 2M-voxel hash neighbour map and one output path")
     ap.add_argument("--simt", action="store_true", help="with --profile-conv: the SIMT kernel instead of tcgen05")
     ap.add_argument("--model", choices=["A", "B"], default="A",
                     help="A: the headline config (480x640); B: config 1 (Model B, 240x320)")
@@ -765,6 +801,9 @@ def main():
     args = ap.parse_args()
     if args.profile_conv is not None:
         print(json.dumps(profile_conv(args)), flush=True)
+        return
+    if args.profile_step:
+        print(json.dumps(profile_step(args)), flush=True)
         return
     if args.conv_sweep:
         conv_sweep(args)

@@ -417,11 +417,10 @@ typedef struct pmg_refiner_config {
                                    device and frame size allow (pmg_fit_prompt_fused); 1: always the multi-launch
                                    fit (prep, sums and radix-select launches).  Same results either way up to the
                                    summation order of the fp64 sums. */
-    int32_t multi_launch_transitions;   /* 0: each pooling transition (mean pool, pool linear) and the bottleneck's
-                                   second fuse projection run fused with the next block's LayerNorm + SiLU +
-                                   requantise in one row pass where the widths allow (32->64, 64->128, 128->256,
-                                   256->256), and level 0's first LayerNorm rides in the input projection; 1: every
-                                   step in its own launch.  Identical results. */
+    int32_t multi_launch_transitions;   /* 0: the pooling transitions into widths up to 128 (mean pool, pool linear:
+                                   32->64, 64->128) run fused with the next block's LayerNorm + SiLU + requantise in
+                                   one row pass, and level 0's first LayerNorm rides in the input projection; 1:
+                                   every step in its own launch.  Identical results. */
 } pmg_refiner_config;
 
 int pmg_refiner_create(const pmg_refiner_config* cfg, pmg_refiner** out);

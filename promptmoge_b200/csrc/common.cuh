@@ -71,6 +71,26 @@ __device__ __forceinline__ float rcp_approx(float x) {
     return r;
 }
 
+// quant8(x, s) for inv_s = 1 / s (IEEE), identical for every x: t = fl(x * inv_s) differs from x / s by at most
+// (2^-24 + 2^-24 + 2^-48) |x / s| < 2e-5 for |x / s| < 160, and the exact chain's fl(x / s) by at most 2^-24 |x / s|;
+// when t is more than 2^-12 from every half-integer both round to the same integer (|t| >= 160 clamps either way).
+// Otherwise, and for NaN, the exact chain runs.
+__device__ __forceinline__ int quant8_fast(float x, float s, float inv_s) {
+    const float t = __fmul_rn(x, inv_s);
+    const float a = fabsf(t);
+    const float f = a - truncf(a);
+    const bool sure = a >= 160.0f || fabsf(f - 0.5f) > (1.0f / 4096.0f);
+    if (__builtin_expect(sure, 1)) return static_cast<int>(fminf(fmaxf(rintf(t), -127.0f), 127.0f));
+    return quant8(x, s);
+}
+
+// x / n for a voxel count n >= 1: a multiply by the exact reciprocal when n is a power of two (the same correctly
+// rounded quotient), the IEEE divide otherwise.
+__device__ __forceinline__ float div_count(float x, int n) {
+    if ((n & (n - 1)) == 0) return __fmul_rn(x, __int_as_float((127 - (__ffs(n) - 1)) << 23));
+    return __fdiv_rn(x, (float)n);
+}
+
 __device__ __forceinline__ int silu_quant8_fast(float x, float s, float inv_s) {
     const float d = __fadd_rn(1.0f, expf(-x));
     const float t = __fmul_rn(__fmul_rn(x, rcp_approx(d)), inv_s);

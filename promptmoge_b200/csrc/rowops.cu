@@ -17,8 +17,9 @@ namespace pmg {
 
 __global__ void k_quantize(const float* __restrict__ x, int64_t n, float s, int8_t* __restrict__ q) {
     pdl_begin();
+    const float inv_s = 1.0f / s;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-        q[i] = (int8_t)quant8(x[i], s);
+        q[i] = (int8_t)quant8_fast(x[i], s, inv_s);
 }
 
 // One warp per row.  C <= 256: lane l holds channels l, l+32, ...
@@ -341,14 +342,15 @@ __device__ __forceinline__ void pool_mean_rows(const float* __restrict__ x, cons
 #pragma unroll
             for (int k = 0; k < 8; ++k) acc[k] = __fadd_rn(acc[k], v[k]);
         }
-        const float n = (float)max(hi - lo, 1);
+        const int n = max(hi - lo, 1);
         if (mean)
 #pragma unroll
-            for (int k = 0; k < 8; ++k) acc[k] = __fdiv_rn(acc[k], n);
+            for (int k = 0; k < 8; ++k) acc[k] = div_count(acc[k], n);
         if (QUANT) {
+            const float inv_s = 1.0f / scale;
             int qv[8];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) qv[k] = quant8(acc[k], scale);
+            for (int k = 0; k < 8; ++k) qv[k] = quant8_fast(acc[k], scale, inv_s);
             store8_q8<C>(q + o * C, sub, qv);
         } else {
             store8<C>(out + o * C, sub, acc);
@@ -479,7 +481,7 @@ __global__ void __launch_bounds__(256) k_out_apply_rows(const float* __restrict_
 // with the pool linear's input scale (the pool_mean_rows arithmetic), the int8 linear by dp4a (exact int32 sums, the
 // same integers the tensor-core GEMM accumulates), dequant + bias -> the level's fp32 input X, then LayerNorm + SiLU +
 // requantise of X into the first conv's int8 input.  With `a8` given instead of pooling inputs, the int8 input rows
-// are read directly (the bottleneck's second fuse projection).  K -> N in {32->64, 64->128, 128->256, 256->256}.
+// are read directly (the bottleneck's second fuse projection).  K -> N in {32->64, 64->128}.
 // Layout: RowMap<N> (G = N/8 lanes per output row, 8 output channels per lane); the quantised input row goes through
 // shared memory; the weight sits in shared memory as [K/4][N] 32-bit words (4 input channels of one output).
 template <int K, int N>
@@ -508,7 +510,7 @@ __global__ void __launch_bounds__(256) k_transition_rows(
         sb[i] = beta[i];
     }
     __syncthreads();
-    const float inv_s = 1.0f / q_scale;
+    const float inv_s = 1.0f / q_scale, inv_ps = 1.0f / pool_scale;
     const int64_t M = rows_of(count, max_rows);
     const int sub = threadIdx.x % G, slot = threadIdx.x / G;
     int8_t* qrow = qin[slot];
@@ -530,9 +532,10 @@ __global__ void __launch_bounds__(256) k_transition_rows(
 #pragma unroll
                     for (int k = 0; k < 8; ++k) acc[k] = __fadd_rn(acc[k], v[k]);
                 }
-                const float n = (float)max(hi - lo, 1);
+                const int n = max(hi - lo, 1);
 #pragma unroll
-                for (int k = 0; k < 8; ++k) qrow[chan8<K>(sub, k)] = (int8_t)quant8(__fdiv_rn(acc[k], n), pool_scale);
+                for (int k = 0; k < 8; ++k)
+                    qrow[chan8<K>(sub, k)] = (int8_t)quant8_fast(div_count(acc[k], n), pool_scale, inv_ps);
             }
         }
         __syncwarp();
@@ -711,15 +714,15 @@ int transition(const float* x, const int32_t* seg_idx, const int32_t* seg_off, f
     }
     PMG_TRANSITION(32, 64)
     PMG_TRANSITION(64, 128)
-    PMG_TRANSITION(128, 256)
-    PMG_TRANSITION(256, 256)
 #undef PMG_TRANSITION
     return PMG_ERR_UNSUPPORTED;
 }
 
-bool transition_supported(int K, int N) {
-    return (K == 32 && N == 64) || (K == 64 && N == 128) || (K == 128 && N == 256) || (K == 256 && N == 256);
-}
+// The plan fuses the transitions whose output is at most 128 wide: there the fused pass measured faster than pool +
+// GEMM + LayerNorm launches (B200, 480x640: 32->64 71 vs 94 us, 64->128 61 vs 67 us of serialised kernel time); the
+// 256-wide ones (levels 3 and 4, 12.8k and 2.6k rows) run too few rows per CTA to amortise staging the weight and
+// measured slower fused (50 vs 34 us, 31 vs 30 us), so they keep the separate launches.
+bool transition_supported(int K, int N) { return (K == 32 && N == 64) || (K == 64 && N == 128); }
 
 int out_apply(const float* x, int64_t N, int C, const float* wo, const float* bo, const float* pc_in, float* pc_out,
               float* delta, cudaStream_t st) {

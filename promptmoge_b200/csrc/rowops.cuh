@@ -64,7 +64,8 @@ int input_proj(const float* pc, const float* prompt, int64_t N, int C, const flo
 int out_apply(const float* x, int64_t N, int C, const float* wo, const float* bo, const float* pc_in, float* pc_out,
               float* delta, cudaStream_t st);
 // A U-Net transition into level k+1 in one row pass: mean pool of x's children (or the int8 rows a8) -> int8 linear
-// [N][K] -> fp32 x_out -> LayerNorm + SiLU + requantise into q.  PMG_ERR_UNSUPPORTED outside the covered widths.
+// [N][K] -> fp32 x_out -> LayerNorm + SiLU + requantise into q.  PMG_ERR_UNSUPPORTED outside the covered widths
+// (32->64, 64->128).
 int transition(const float* x, const int32_t* seg_idx, const int32_t* seg_off, float pool_scale, const int8_t* a8,
                const int32_t* count, int64_t max_rows, int K, int N, const int8_t* w, const float* w_scale,
                const float* bias, float sa, float* x_out, const float* gamma, const float* beta, double eps,

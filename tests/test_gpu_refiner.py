@@ -299,8 +299,8 @@ def test_one_launch_fit_plan_equals_multi_launch_fit_plan(golden, name):
 
 @pytest.mark.parametrize("name", ["A_full", "B_full", "A_small"])
 def test_fused_transitions_plan_equals_multi_launch_plan(golden, name):
-    """Pool + linear + the next block's LayerNorm / SiLU / requantise in one row pass (every pooling transition, the
-    bottleneck's second fuse projection) and the level-0 LayerNorm inside the input projection refine to the same bits
+    """Pool + linear + the next block's LayerNorm / SiLU / requantise in one row pass (the pooling transitions into
+    widths up to 128) and the level-0 LayerNorm inside the input projection refine to the same bits
     as the plan that runs each of those steps as its own launch (the int8 linear by dp4a sums the same integers the
     tensor-core GEMM does)."""
     from promptmoge_b200 import synth
