@@ -285,6 +285,40 @@ def submanifold_conv(feats: Tensor, coords: Tensor, shape: torch.Size, weight: T
     return out.to(feats.dtype), neighbor_cache
 
 
+def submanifold_conv_int8(feats: Tensor, coords: Tensor, shape: torch.Size, weight: Tensor, bias: Tensor | None,
+                          clip: float, *, dilation: Sequence[int] | None = None,
+                          neighbor_cache: NeighborCache | None = None) -> tuple[Tensor, NeighborCache]:
+    """The QAT conv as the deployed int8 layer (moge/model/modules/qat.py:28-57, promptmoge/export/refiner.py:40-46):
+    q = clamp(rint(feats / s_a), +-127) with s_a = clip / 127, q_w = clamp(rint(w / s_w), +-127) with
+    s_w = amax|w[n]| / 127 per output channel, exact int32 accumulation on the tcgen05 kernel, y = acc * s_a * s_w + b.
+    weight is the fp32 master (Co, 3, 3, 3, Ci).  Returns (out [M, Co] in feats' dtype, the cache)."""
+    kernel_size = tuple(weight.shape[1:-1])
+    sparse_shape = tuple(shape[: coords.shape[1]])
+    if neighbor_cache is None:
+        neighbor_cache = build_submanifold_cache(coords, sparse_shape, kernel_size, dilation)
+    else:
+        neighbor_cache.assert_match(input_coords=coords, output_coords=coords, is_transposed=False)
+    _require_cuda(feats, "feats")
+    Co, Ci = int(weight.shape[0]), int(weight.shape[-1])
+    V = int(neighbor_cache.nmap_tm.shape[0])
+    if V != 27 or not ops.tc_supported(Ci, Co):
+        raise NotImplementedError(f"int8 tensor-core conv for a {V}-tap {Ci}->{Co} layer")
+    from ..engine import act_scale
+    s_a = act_scale(clip)
+    q_in = ops.quantize(feats.detach().float().contiguous(), s_a)
+    w = weight.detach().float()
+    # IEEE divides throughout (a tensor divisor: torch turns a division by a Python scalar into a multiply by its
+    # reciprocal, which can differ in the last bit)
+    amax = w.abs().reshape(Co, -1).amax(dim=1)
+    s_w = (amax / torch.full_like(amax, 127.0)).clamp_min(1e-12)
+    q_w = torch.clamp(torch.round(w / s_w.view(-1, 1, 1, 1, 1)), -127, 127).to(torch.int8)
+    w_tm = q_w.reshape(Co, V, Ci).permute(1, 0, 2).contiguous()
+    b = bias.detach().float().contiguous() if bias is not None else torch.zeros(Co, device=feats.device)
+    out = ops.spconv_i8(q_in, neighbor_cache.nmap_tm, neighbor_cache.tile_mask, w_tm, s_w.contiguous(), b, s_a,
+                        ops.EPI_F32, rows=feats.shape[0])
+    return out.to(feats.dtype), neighbor_cache
+
+
 def sparse_pool(feats: Tensor, coords: Tensor, shape: torch.Size, kernel_size, stride=None, padding=None,
                 reduce: str = "mean", output_coords: Tensor | None = None, output_shape: torch.Size | None = None,
                 neighbor_cache: NeighborCache | None = None) -> tuple[Tensor, Tensor, torch.Size, NeighborCache]:

@@ -1,7 +1,9 @@
 """nn.Module wrappers with the signatures the refiner's blocks construct (reference: promptmoge/_fallback/flex_gemm/
 nn/__init__.py:20-110; upstream FlexGEMM's module names).  Parameters are plain ``nn.Parameter``s in the reference's
 shapes (weight (Co, k, k, k, Ci), bias (Co,)) with the same initialisation, so QAT parametrisations and state dicts
-carry over unchanged."""
+carry over unchanged.  A conv wrapped by the reference's int8 QAT (moge/model/modules/qat.py:101-138) runs, in eval
+mode, as the deployed int8 layer on the tcgen05 kernel (exact int32 accumulators, dequantised once); without QAT
+it runs the fp32 kernel."""
 from __future__ import annotations
 
 import math
@@ -9,7 +11,7 @@ import math
 import torch
 from torch import nn
 
-from ._core import _broadcast, sparse_pool, sparse_upsample, submanifold_conv
+from ._core import _broadcast, sparse_pool, sparse_upsample, submanifold_conv, submanifold_conv_int8
 
 __all__ = ["SubmanifoldConv", "SubmanifoldConv3d", "SparsePool", "SparsePool3d", "SparseUpsample",
            "SparseUpsample3d"]
@@ -39,7 +41,30 @@ class SubmanifoldConv(nn.Module):
             bound = 1.0 / math.sqrt(fan_in) if fan_in > 0 else 0.0
             nn.init.uniform_(self.bias, -bound, bound)
 
+    def _int8_quantizers(self):
+        """(activation clip module, weight parametrisation) when the reference's int8 QAT wraps this conv
+        (moge/model/modules/qat.py:101-115: a per-output-channel WeightFakeQuant parametrisation of `weight` and an
+        ActFakeQuant forward pre-hook on the input), else None."""
+        params = getattr(self, "parametrizations", None)
+        if params is None or "weight" not in params or len(params.weight) != 1:
+            return None
+        wq = params.weight[0]
+        if not getattr(wq, "enabled", False) or getattr(wq, "ch_dim", None) != 0:
+            return None
+        for hook in self._forward_pre_hooks.values():
+            for cell in getattr(hook, "__closure__", None) or ():
+                aq = cell.cell_contents
+                if hasattr(aq, "clip") and hasattr(aq, "observed") and getattr(aq, "enabled", False):
+                    return aq, wq
+        return None
+
     def forward(self, feats, coords, shape, neighbor_cache=None):
+        qat = None if self.training else self._int8_quantizers()
+        if qat is not None and int(qat[0].observed) > 0:
+            # the deployed int8 arithmetic on the tensor cores: the pre-hook already fake-quantised feats with the
+            # clip, so requantising them gives the int8 input exactly; the weight is quantised from its fp32 master
+            return submanifold_conv_int8(feats, coords, shape, self.parametrizations.weight.original, self.bias,
+                                         float(qat[0].clip), dilation=self.dilation, neighbor_cache=neighbor_cache)
         return submanifold_conv(feats, coords, shape, self.weight, self.bias, dilation=self.dilation,
                                 neighbor_cache=neighbor_cache)
 

@@ -103,3 +103,43 @@ def stub_model(model: str = "B", seed: int = 0, qat: bool = True, blocks: int = 
     if qat:
         unet.attach_clips(clips)
     return StubMoGe(unet.eval())
+
+
+# ---- stand-ins for the reference's QAT wrappers (moge/model/modules/qat.py:40-115), for the flex_gemm drop-in's
+# int8 routing: a per-output-channel weight parametrisation and a per-tensor input quantiser attached as a forward
+# pre-hook, with the attribute names the reference's classes carry (ch_dim / enabled, clip / observed / enabled).
+class StubWeightFakeQuant(nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.ch_dim, self.enabled = 0, True
+
+    def forward(self, w):
+        dims = [d for d in range(w.ndim) if d != 0]
+        s = (w.detach().abs().amax(dim=dims, keepdim=True) / 127.0).float().clamp_min(1e-12)
+        return torch.clamp(torch.round(w.float() / s), -127, 127) * s
+
+
+class StubActFakeQuant(nn.Module):
+    def __init__(self, clip: float):
+        super().__init__()
+        self.enabled = True
+        self.register_buffer("clip", torch.tensor(float(clip)))
+        self.register_buffer("observed", torch.ones((), dtype=torch.long))
+
+    def forward(self, x):
+        s = (self.clip / 127.0).float().clamp_min(1e-12)
+        return torch.clamp(torch.round(x.float() / s), -127, 127) * s
+
+
+def stub_qat(module: nn.Module, clip: float) -> StubActFakeQuant:
+    """Wrap one conv / linear the way enable_refiner_qat does (parametrisation + input pre-hook)."""
+    import torch.nn.utils.parametrize as P
+    P.register_parametrization(module, "weight", StubWeightFakeQuant())
+    aq = StubActFakeQuant(clip)
+
+    def make_hook(q):
+        def hook(mod, args):
+            return (q(args[0]), *args[1:])
+        return hook
+    module.register_forward_pre_hook(make_hook(aq))
+    return aq

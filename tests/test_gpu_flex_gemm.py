@@ -154,3 +154,39 @@ def test_unsorted_pool_input_is_an_error(golden):
     coords = torch.from_numpy(g["s0_L1_coords"][::-1].copy()).cuda()
     with pytest.raises(ValueError):
         build_pool_cache(coords, _level_shapes(g, 4)[1], (2, 2, 2), (2, 2, 2), (0, 0, 0))
+
+
+@pytest.mark.parametrize("name,level", [("A_small", 1), ("A_small", 2), ("B_small", 3), ("A_small", 0)])
+def test_qat_conv_runs_int8_on_tensor_cores(golden, name, level):
+    """A drop-in SubmanifoldConv3d wrapped by the reference's QAT (weight parametrisation + input quantiser pre-hook)
+    runs the deployed int8 layer on the tcgen05 kernel: its output is the oracle's dequantised exact int32
+    accumulators bit for bit, and within 1e-3 (relative to the output's range) of the fake-quantised fp32 conv."""
+    from oracle import refiner as oref
+    from promptmoge_b200 import flex_gemm
+    from stub_moge import stub_qat
+    flex_gemm.install()
+    from flex_gemm.nn import SubmanifoldConv3d
+    g = golden(name)
+    widths = _widths(g)
+    C = widths[level]
+    coords = torch.from_numpy(g[f"s0_L{level}_coords"]).cuda()
+    shape = torch.Size(list(_level_shapes(g, len(widths))[level]) + [C])
+    torch.manual_seed(level)
+    conv = SubmanifoldConv3d(C, C, 3).cuda().eval()
+    x = torch.randn(coords.shape[0], C, device="cuda") * 2.0
+    with torch.no_grad():
+        y_float, cache = conv(x, coords, shape)                        # no QAT: the fp32 kernel
+        aq = stub_qat(conv, clip=5.0)
+        y_int8, _ = conv(x, coords, shape, neighbor_cache=cache)       # QAT: the int8 tensor-core kernel
+        fq_x = aq(x)
+        y_fq, _ = flex_gemm.ops.submanifold_conv(fq_x, coords, shape, conv.weight, conv.bias, neighbor_cache=cache)
+    del y_float
+    # exact: dequant(oracle int32 accumulators of the quantised input and weight)
+    s_a = np.float32(np.float32(5.0) / np.float32(127.0))
+    q = np.clip(np.rint(x.cpu().numpy() / s_a), -127, 127).astype(np.int8)
+    qw, sw = oref.quant_weight(conv.parametrizations.weight.original.detach().cpu().numpy())
+    acc = oref.conv_acc(q, g[f"s0_L{level}_nmap"], qw)
+    want = oref.dequant(acc.astype(np.int64), s_a, sw, conv.bias.detach().cpu().numpy())
+    np.testing.assert_array_equal(y_int8.cpu().numpy(), want)
+    ref = y_fq.cpu().numpy()
+    assert np.abs(y_int8.cpu().numpy() - ref).max() <= 1e-3 * np.abs(ref).max()
