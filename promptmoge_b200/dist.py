@@ -57,11 +57,11 @@ class ShardedRefiner:
         rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.begin, self.end = frame_range(n_frames, rank, world)
 
-    def run(self, frames, K: int = 1, batch_frames=None):
+    def run(self, frames, K: int = 1, batch_frames=None, out: torch.Tensor | None = None):
         """Returns (refined point maps of this rank's frames [n_local,H,W,3] host, all frames' fit states
         [n_frames, 18] int32 on this rank's device).  batch_frames(ids), when given, returns the five inputs of a
         whole batch of frames at once (already concatenated, e.g. pinned host tensors), instead of frames(i) per
-        frame."""
+        frame.  out: a host tensor [n_local,H,W,3] (pinned: the refined maps are copied into it directly)."""
         B = self.refiner.geo.batch
         outs, fits = [], []
         for f0 in range(self.begin, self.end, B):
@@ -71,12 +71,23 @@ class ShardedRefiner:
             else:
                 parts = [frames(i) for i in ids]
                 cat = [np.concatenate([p[k] for p in parts]) if parts[0][k] is not None else None for k in range(5)]
-            pc, fit = self.refiner.refine(*cat[:4], uv_bias=cat[4], K=K)
             n = min(B, self.end - f0)
-            outs.append(pc[:n].clone())
-            fits.append(self.refiner.h_fit[:n].clone())
-        local_pc = torch.cat(outs) if outs else torch.empty(0)
-        local_fit = torch.cat(fits) if fits else torch.empty((0, 18), dtype=torch.int32)
+            whole = out is not None and n == B
+            dst = out[f0 - self.begin:f0 - self.begin + B] if whole else None
+            # with a whole batch copied straight into `out`, nothing on the host waits for the batch: the next
+            # batch's copies and graph queue up behind it (the plan's buffers are stream-ordered)
+            pc, _ = self.refiner.refine(*cat[:4], uv_bias=cat[4], K=K, out=dst, sync=not whole)
+            if out is not None and not whole:
+                out[f0 - self.begin:f0 - self.begin + n] = pc[:n]
+            elif out is None:
+                outs.append(pc[:n].clone())
+            fits.append(self.refiner.engine._fit[:n].clone())          # device copy, stream-ordered
+        torch.cuda.current_stream(self.refiner.device).synchronize()
+        if out is not None:
+            local_pc = out
+        else:
+            local_pc = torch.cat(outs) if outs else torch.empty(0)
+        local_fit = torch.cat(fits).cpu() if fits else torch.empty((0, 18), dtype=torch.int32)
         if dist.is_initialized() and dist.get_world_size(self.group) > 1:
             dev = self.refiner.device if dist.get_backend(self.group) == "nccl" else torch.device("cpu")
             all_fit = gather_frame_states(local_fit.to(dev), self.n_frames, self.group)

@@ -74,12 +74,13 @@ class Refiner:
             self._K = K
 
     def refine(self, point_coord, lidar_depth, lidar_conf, encoder_feature, uv_bias=None, K: int = 1,
-               sync: bool = True, fill: bool = False):
+               sync: bool = True, fill: bool = False, out: torch.Tensor | None = None):
         """Refine a batch of frames.  Host arrays/tensors (pinned CPU tensors copy asynchronously):
         point_coord [B,H,W,3] fp32, lidar_depth/lidar_conf [B,1,192,256] fp32, encoder_feature [B,1024,h,w] fp16,
         uv_bias [B,C,h,w] fp32 or None.  fill=True first applies promptmoge.nearest_fill to the sensor frames on the
         device (promptmoge.infer does so by default before the model sees them, promptmoge/model.py:93-94).
-        Returns (refined point map [B,H,W,3] host tensor, fit list)."""
+        out: a host tensor [B,H,W,3] (pinned for an asynchronous copy) the refined point map is copied into instead of
+        the Refiner's own staging buffer.  Returns (refined point map [B,H,W,3] host tensor, fit list)."""
         self._ensure_graph(K)
         s = torch.cuda.current_stream(self.device)
         if fill:
@@ -112,13 +113,14 @@ class Refiner:
             elif uv_bias is not None:
                 self.d_uv.copy_(torch.as_tensor(uv_bias), non_blocking=True)
             self.engine.set_frame(self.d_enc, self.d_uv if uv_bias is not None else None)
-        out, fit = self.engine.replay()
-        self.h_out.copy_(out, non_blocking=True)
+        res, fit = self.engine.replay()
+        dst = self.h_out if out is None else out
+        dst.copy_(res, non_blocking=True)
         self.h_fit.copy_(fit, non_blocking=True)
         if sync:
             s.synchronize()
-            return self.h_out, fit_state_view(self.h_fit)
-        return self.h_out, None
+            return dst, fit_state_view(self.h_fit)
+        return dst, None
 
     @classmethod
     def from_refiner_dir(cls, path, batch: int = 1, device="cuda", capacity=None):

@@ -325,3 +325,36 @@ def test_fused_transitions_plan_equals_multi_launch_plan(golden, name):
     for a, b in zip(outs[0][1], outs[1][1]):
         assert torch.equal(a, b)
     assert outs[1][2] < outs[0][2]
+
+
+def test_sharded_refiner_pipelined_batches_equal_single_frames():
+    """ShardedRefiner on one process: 6 frames, 4 per graph replay (the last batch partial), copied straight into a
+    pinned output without a host wait per batch, and through the Refiner's own staging buffer: every frame equals its
+    single-frame refinement, and every frame's fit state is returned."""
+    from promptmoge_b200 import synth
+    from promptmoge_b200.dist import ShardedRefiner
+    from promptmoge_b200.refine import Refiner, pinned, synthetic_model
+    m = synth.MODELS["B"]
+    weights, clips = synthetic_model("B", 0)
+    scenes = [synth.make_scene(60 + i, m["H"], m["W"], m["encoder_downsample"], m["model_channels"][-1])
+              for i in range(6)]
+    keys = ("point_coord", "lidar_depth", "lidar_conf", "encoder_feature", "uv_bias")
+    single = Refiner(weights, clips, "B", batch=1)
+    try:
+        want = [single.refine(*[pinned(getattr(sc, k)) for k in keys[:4]], uv_bias=pinned(sc.uv_bias), K=2)[0].clone()
+                for sc in scenes]
+    finally:
+        single.close()
+    ref = Refiner(weights, clips, "B", batch=4)
+    try:
+        def batch_frames(ids):
+            return tuple(pinned(np.concatenate([getattr(scenes[i], k) for i in ids])) for k in keys)
+        sharded = ShardedRefiner(ref, 6)
+        out = torch.empty((6, m["H"], m["W"], 3), dtype=torch.float32).pin_memory()
+        for o in (out, None):
+            got, fits = sharded.run(None, K=2, batch_frames=batch_frames, out=o)
+            assert fits.shape == (6, 18)
+            for i in range(6):
+                assert torch.equal(got[i:i + 1], want[i]), i
+    finally:
+        ref.close()
