@@ -628,86 +628,120 @@ def conv_sweep(args):
         del nmap, mask
 
 
+def _rows_of_index(idx, C: int):
+    """Seeded int8 rows [n, C] as a function of the voxels' global indices (the same rows whichever rank holds them)."""
+    import torch
+    ch = torch.arange(C, device=idx.device, dtype=torch.int64)
+    h = (idx.to(torch.int64)[:, None] * 2654435761 + ch[None, :] * 40503 + 12345) & 0xFFFFFFFF
+    h = (h ^ (h >> 15)) * 2246822519 & 0xFFFFFFFF
+    return ((h >> 13) % 255 - 127).to(torch.int8)
+
+
 def fused_scene(args, ws, rank, local):
-    """Benchmark configuration 5: one synthetic 12 x 12 x 3 m room seen from 200 poses (480 x 640, random walk), fused into a
-    1 cm voxel grid, Morton-range sharded over the ranks; a stack of --fused-layers int8 submanifold convs (C = 32,
-    Model A's level-0 width, SiLU + requantise epilogue) with a one-voxel halo exchange (NCCL all-to-all of int8
-    rows) before every layer.  value = voxel-layers/s of the whole job (strong scaling: the scene is fixed);
-    the sharded result is checked against a single-device run over the whole grid."""
+    """Benchmark configuration 5: one synthetic 12 x 12 x 3 m room seen from --fused-poses poses (480 x 640, random walk),
+    fused into a 1 cm voxel grid and sharded by Morton ranges WITHOUT a global view: each rank back-projects its own
+    contiguous share of the poses, voxels go to the owners of their code ranges (count-balanced splitters from one
+    all-gather of code samples), neighbours across a range boundary are looked up at their owner, and every coarser
+    level is the parents (code >> 3) of the level below, each level with its own count-balanced ranges
+    (promptmoge_b200.fused.build_levels).
+    The timed step is a sharded U-Net encoder with Model A's widths (32, 64, 128, 256, 256), two int8 submanifold
+    convs per level (tcgen05, SiLU + requantise epilogue), each after a one-voxel halo exchange (NCCL all-to-all of
+    int8 rows), and between levels the mean pool into parents (children moved to their parent's owner, summed in code
+    order) plus the transition's int8 linear.  value = voxel-layers/s of the whole job (strong scaling: the scene is fixed).  Rank
+    0 also runs the same pipeline as the only rank over the whole scene and every level's output is compared."""
+    import hashlib
     import torch
     import torch.distributed as dist
     from promptmoge_b200 import fused, ops
+    from promptmoge_b200.dist import frame_range
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    widths = [32, 64, 128, 256, 256]
+    convs, links = fused.encoder_layers(widths, 2, seed=7, device=dev)
+
+    def nmap_fn(coords, ext):
+        nm, _, st = ops.nmap_hash(coords, ext)
+        if int(st.item()) != 0:
+            raise RuntimeError("hash neighbour map failed")
+        return nm
+
+    group = None if ws > 1 else fused.LOCAL
+    layout = fused.scene_layout(0, args.fused_poses)
+    b, e = frame_range(args.fused_poses, rank, ws)
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
     t0 = time.perf_counter()
-    coords, info = fused.make_fused_scene(0, n_poses=args.fused_poses, device=dev)
-    M = coords.shape[0]
-    ext = [1, 1 << 21, 1 << 21, 1 << 21]
-    bounds = fused.shard_bounds(M, ws)
-    lo, hi = bounds[rank]
-    nm, _, st = ops.nmap_hash(coords, ext)
-    if int(st.item()) != 0:
-        raise RuntimeError("hash neighbour map failed")
-    nm_own = nm[:, lo:hi].contiguous()
-    plan = fused.ShardPlan(nm_own, bounds, rank)
-    setup_s = time.perf_counter() - t0
-    C, L = 32, args.fused_layers
-    layers = fused.random_layers(L, C, seed=7, device=dev)
-    q_all = torch.randint(-127, 128, (M, C), dtype=torch.int8, generator=torch.Generator().manual_seed(3)).to(dev)
-    q_own = q_all[lo:hi].contiguous()
-    buf = plan.local_buffer(C)
+    local_codes = fused.scene_codes(0, layout, range(b, e), device=dev)
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    levels = fused.build_levels(local_codes, len(widths), nmap_fn, group)
+    pools = [fused.PoolPlan(levels[k], levels[k + 1], group) for k in range(len(widths) - 1)]
+    torch.cuda.synchronize()
+    t2 = time.perf_counter()
+    q0 = _rows_of_index(torch.arange(levels[0].offset, levels[0].offset + levels[0].plan.n_own, device=dev),
+                        widths[0])
 
     def step():
-        buf[:plan.n_own] = q_own
-        for layer in layers:
-            plan.exchange(buf)
-            buf[:plan.n_own] = fused.gpu_conv(buf, plan.nmap, plan.mask, layer)
+        return fused.encoder_forward(levels, q0, convs, links, fused.gpu_conv, fused.gpu_link, group, pools=pools)
 
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     if ws > 1:
         dist.barrier()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
-        s.record()
+        s0.record()
         for _ in range(args.steps):
-            step()
-        e.record()
+            outs = step()
+        s1.record()
         torch.cuda.synchronize()
     if ws > 1:
         dist.barrier()
-    ms = s.elapsed_time(e)
+    ms = s0.elapsed_time(s1)
+    build = [t1 - t0, t2 - t1]
+    counts = [[l.plan.n_own for l in levels]]
+    halos = [[l.plan.n_halo for l in levels]]
+    digests = [hashlib.sha256(o.cpu().numpy().tobytes()).hexdigest() for o in outs]
     if ws > 1:
-        t = torch.tensor([ms], device=dev)
+        t = torch.tensor([ms] + build, device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    out = buf[:plan.n_own].clone()
+        ms, build = float(t[0]), [float(x) for x in t[1:]]
+        gathered = [None] * ws
+        dist.all_gather_object(gathered, (counts[0], halos[0], [o.cpu() for o in outs]))
+        counts = [g[0] for g in gathered]
+        halos = [g[1] for g in gathered]
     verified = None
-    if ws > 1:
-        sizes = [b - a for a, b in bounds]
-        mx = max(sizes)
-        pad = torch.zeros((mx, C), dtype=torch.int8, device=dev)
-        pad[:plan.n_own] = out
-        allp = [torch.empty_like(pad) for _ in range(ws)]
-        dist.all_gather(allp, pad)
-        if rank == 0:
-            got = torch.cat([allp[r][:sizes[r]] for r in range(ws)])
-            full = fused.plans_in_process(nm[:, :M].contiguous(), fused.shard_bounds(M, 1))[0]
-            want = fused.run_layers(full, q_all, layers, fused.gpu_conv)
-            verified = bool(torch.equal(got, want))
+    if rank == 0:
+        # the same pipeline as the only rank over the whole scene
+        whole = fused.scene_codes(0, layout, range(args.fused_poses), device=dev)
+        ref_levels = fused.build_levels(whole, len(widths), nmap_fn, fused.LOCAL)
+        ref_q0 = _rows_of_index(torch.arange(ref_levels[0].plan.n_own, device=dev), widths[0])
+        ref = fused.encoder_forward(ref_levels, ref_q0, convs, links, fused.gpu_conv, fused.gpu_link, fused.LOCAL)
+        if ws > 1:
+            got = [torch.cat([g[2][k] for g in gathered]) for k in range(len(widths))]
+        else:
+            got = [o.cpu() for o in outs]
+        verified = all(torch.equal(a, r.cpu()) for a, r in zip(got, ref))
+        M = [sum(c[k] for c in counts) for k in range(len(widths))]
     if rank != 0:
         return None
-    value = M * L * args.steps / (ms * 1e-3)
+    vl = sum(M[k] * len(convs[k]) for k in range(len(widths)))
+    value = vl * args.steps / (ms * 1e-3)
     return {"metric": "fused-scene voxel-layers/s (C5)", "value": round(value, 1), "unit": "voxel-layers/s",
             "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": f"C5: fused scene, {info['poses']} poses 480x640 into a 1 cm grid "
-                                   f"({M} voxels), {L} int8 submanifold convs C=32 with a halo exchange each",
-                       "voxels": M, "voxels_per_rank": [b - a for a, b in bounds], "layers": L,
-                       "halo_rows_rank0": plan.n_halo, "halo_bytes_per_layer_rank0": plan.halo_bytes(C),
-                       "setup_s_rank0": round(setup_s, 2), "sharding": "Morton ranges", "exchange": "NCCL all-to-all"},
-            "verified_vs_single_device": verified, "clocks": clk.summary()}
+            "config": {"workload": f"C5: fused scene, {args.fused_poses} poses 480x640 into a 1 cm grid ({M[0]} voxels), "
+                                   "sharded U-Net encoder with Model A widths: 2 int8 submanifold convs per level, "
+                                   "halo exchange before each, mean pool + int8 linear between levels",
+                       "voxels_per_level": M, "voxels_per_rank_per_level": counts, "halo_rows_per_rank_per_level": halos,
+                       "convs_per_level": 2, "widths": widths,
+                       "build_s": {"backproject_own_poses": round(build[0], 3),
+                                   "levels_sharded_structure": round(build[1], 3)},
+                       "sharding": "Morton ranges, count-balanced per level; coarser levels are parent codes",
+                       "exchange": "NCCL all-to-all (halo rows; children to their parent's owner)"},
+            "verified_vs_single_device": verified, "level_output_sha256_rank0": digests, "clocks": clk.summary()}
 
 
 def _port_step(steps: int, warm: int):
@@ -798,7 +832,6 @@ def main():
     ap.add_argument("--sweep-n", default="100000,500000,2000000,8000000")
     ap.add_argument("--fused-scene", action="store_true", help="config 5: fused multi-pose scene over Morton shards")
     ap.add_argument("--fused-poses", type=int, default=200)
-    ap.add_argument("--fused-layers", type=int, default=4)
     ap.add_argument("--c4-frames", type=int, default=256,
                     help="config 4 sub-record: frames of the batched sharded run (0 = skip)")
     ap.add_argument("--c4-K", type=int, default=3)

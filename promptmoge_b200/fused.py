@@ -96,16 +96,12 @@ def _raycast(origin: torch.Tensor, dirs: torch.Tensor, boxes: torch.Tensor, sphe
     return t
 
 
-def make_fused_scene(seed: int, n_poses: int = 200, H: int = 480, W: int = 640, voxel: float = 0.01,
-                     room_size=(12.0, 12.0, 3.0), device: str | torch.device = "cpu", chunk: int = 16):
-    """Voxels (b = 0, x, y, z) int32 [M, 4] of one synthetic room seen from `n_poses` camera poses along a seeded random
-    walk, back-projected with 1 %-of-depth noise into a `voxel`-metre grid, unique and sorted by Morton code.
-
-    Room: `room_size` metres with one axis-aligned box per 3.6 m^2 of floor (40 in the 12 x 12 m room; 60 % standing
-    on the floor) and one sphere per 18 m^2; pinhole camera fx = fy = 0.8 W at 1.2-1.8 m height, 0.15 m steps with a
-    drifting heading.  Returns (coords, info)."""
+def scene_layout(seed: int, n_poses: int = 200, room_size=(12.0, 12.0, 3.0)):
+    """The seeded room and camera walk of a fused scene: (room [2,3], boxes [(lo, hi)], spheres [[c, r]], poses
+    [(position, rotation)]).  Room: `room_size` metres with one axis-aligned box per 3.6 m^2 of floor (40 in the
+    12 x 12 m room; 60 % standing on the floor) and one sphere per 18 m^2; camera at 1.2-1.8 m height, 0.15 m steps
+    with a drifting heading.  Plain numpy from the seed: every rank derives the same layout."""
     rng = np.random.default_rng(seed)
-    dev = torch.device(device)
     room = np.array([[0.0, 0.0, 0.0], list(room_size)])
     area = room_size[0] * room_size[1]
     n_boxes, n_spheres = max(2, round(area / 3.6)), max(1, round(area / 18.0))
@@ -152,7 +148,16 @@ def make_fused_scene(seed: int, n_poses: int = 200, H: int = 480, W: int = 640, 
         blocked = 0
         pos = cand
         poses.append((pos.copy(), _rotation(heading + rng.normal(0.0, 0.2), rng.uniform(-0.3, 0.3))))
+    return room, boxes, spheres, poses
 
+
+def scene_codes(seed: int, layout, pose_ids, H: int = 480, W: int = 640, voxel: float = 0.01,
+                device: str | torch.device = "cpu", chunk: int = 16) -> torch.Tensor:
+    """Sorted unique Morton codes (int64) of the voxels the poses `pose_ids` of `layout` back-project into: pinhole
+    fx = fy = 0.8 W, analytic ray cast, 1 %-of-depth noise drawn from a generator seeded by (seed, pose index), so a
+    pose gives the same voxels whichever rank casts it."""
+    room, boxes, spheres, poses = layout
+    dev = torch.device(device)
     dt = torch.float32
     t_room = torch.tensor(room, dtype=dt, device=dev)
     t_boxes = torch.tensor(np.array([[lo, hi] for lo, hi in boxes]), dtype=dt, device=dev)
@@ -161,24 +166,40 @@ def make_fused_scene(seed: int, n_poses: int = 200, H: int = 480, W: int = 640, 
     v, u = torch.meshgrid(torch.arange(H, dtype=dt, device=dev) + 0.5, torch.arange(W, dtype=dt, device=dev) + 0.5,
                           indexing="ij")
     d_cam = torch.stack([(u - W / 2.0) / fx, (v - H / 2.0) / fx, torch.ones_like(u)], dim=-1).reshape(-1, 3)
-    noise_gen = torch.Generator(device=dev).manual_seed(seed)
     limit = (1 << MORTON_BITS) - 1
-    codes = []
-    pending = []
-    for i, (o, R) in enumerate(poses):
+    codes, pending = [], []
+    pose_ids = list(pose_ids)
+    for n, i in enumerate(pose_ids):
+        o, R = poses[i]
         origin = torch.tensor(o, dtype=dt, device=dev)
         dirs = d_cam @ torch.tensor(R.T, dtype=dt, device=dev)
         t = _raycast(origin, dirs, t_boxes, t_spheres, t_room)
-        t = t * (1.0 + 0.01 * torch.randn(t.shape, generator=noise_gen, device=dev, dtype=dt))
+        gen = torch.Generator(device=dev).manual_seed(seed * 1_000_003 + i)
+        t = t * (1.0 + 0.01 * torch.randn(t.shape, generator=gen, device=dev, dtype=dt))
         p = origin + t[:, None] * dirs
         q = torch.floor(p / voxel).to(torch.int64).clamp(0, limit)
         pending.append(morton3(q[:, 0], q[:, 1], q[:, 2]))
-        if len(pending) == chunk or i == len(poses) - 1:
+        if len(pending) == chunk or n == len(pose_ids) - 1:
             codes.append(torch.unique(torch.cat(pending)))
             pending = []
-    code = torch.unique(torch.cat(codes))                 # sorted ascending = Morton order
+    if not codes:
+        return torch.empty(0, dtype=torch.int64, device=dev)
+    return torch.unique(torch.cat(codes))                 # sorted ascending = Morton order
+
+
+def coords_of_codes(code: torch.Tensor) -> torch.Tensor:
+    """[M, 4] int32 (b = 0, x, y, z) of Morton codes."""
     x, y, z = demorton3(code)
-    coords = torch.stack([torch.zeros_like(x), x, y, z], dim=1).to(torch.int32)
+    return torch.stack([torch.zeros_like(x), x, y, z], dim=1).to(torch.int32)
+
+
+def make_fused_scene(seed: int, n_poses: int = 200, H: int = 480, W: int = 640, voxel: float = 0.01,
+                     room_size=(12.0, 12.0, 3.0), device: str | torch.device = "cpu", chunk: int = 16):
+    """Voxels (b = 0, x, y, z) int32 [M, 4] of one synthetic room (scene_layout) seen from `n_poses` camera poses,
+    back-projected (scene_codes) into a `voxel`-metre grid, unique and sorted by Morton code.  Returns (coords, info)."""
+    layout = scene_layout(seed, n_poses, room_size)
+    code = scene_codes(seed, layout, range(n_poses), H, W, voxel, device, chunk)
+    coords = coords_of_codes(code)
     info = dict(seed=seed, poses=n_poses, H=H, W=W, voxel=voxel, room=list(room_size), voxels=int(coords.shape[0]))
     return coords, info
 
@@ -264,6 +285,24 @@ class ShardPlan:
         self.send_idx = (wanted.to(torch.int64) - self.lo).contiguous()
         self.group = group
 
+    @classmethod
+    def from_parts(cls, nmap_local: torch.Tensor, n_own: int, n_halo: int, recv_splits, send_idx: torch.Tensor,
+                   send_splits, rank: int, world: int, group=None) -> "ShardPlan":
+        """A plan from an already local neighbour map (owned rows, indices in [owned | halo] row space) and the
+        exchange lists, for a voxel set sharded without a global view (LevelShard)."""
+        self = cls.__new__(cls)
+        self.rank, self.world = rank, world
+        self.lo, self.hi = 0, n_own
+        self.n_own, self.n_halo = n_own, n_halo
+        self.halo = None
+        self.nmap = nmap_local.contiguous()
+        self.mask = tile_mask_of(self.nmap)
+        self.recv_splits = [int(c) for c in recv_splits]
+        self.send_splits = [int(c) for c in send_splits]
+        self.send_idx = send_idx.to(torch.int64).contiguous()
+        self.group = group
+        return self
+
     def local_buffer(self, C: int, dtype=torch.int8) -> torch.Tensor:
         """[n_own + n_halo, C] rows: owned first, halo rows after (filled by `exchange`)."""
         return torch.empty((self.n_own + self.n_halo, C), dtype=dtype, device=self.nmap.device)
@@ -336,3 +375,294 @@ def random_layers(n: int, C: int, seed: int, device):
         b = torch.randn(C, generator=g) * 0.1
         layers.append((w.to(device), ws.to(device), b.to(device), 0.05, 0.04))
     return layers
+
+
+# --------------------------------------------------------------------------------------------------------------- #
+# Sharded structure without a global view: every rank back-projects its own poses, voxels go to the owners of their
+# Morton code ranges (balanced per level), neighbours across a range boundary are looked up at their owner, and each
+# coarser level is the set of parents (code >> 3) of the level below, with its own balanced ranges.
+# --------------------------------------------------------------------------------------------------------------- #
+
+LOCAL = "local"   # pass as `group` to run a sharded routine as the only rank (a single-device run), collectives off
+
+
+def _world(group):
+    import torch.distributed as dist
+    if group is LOCAL or not dist.is_available() or not dist.is_initialized():
+        return 1, 0
+    return dist.get_world_size(group), dist.get_rank(group)
+
+
+def _alltoallv(send: torch.Tensor, send_counts, group):
+    """Variable all-to-all of rows grouped by destination rank: (received rows grouped by source, counts)."""
+    import torch.distributed as dist
+    world, _ = _world(group)
+    if world == 1:
+        return send.clone(), [int(c) for c in send_counts]
+    dev = send.device
+    sc = torch.tensor([int(c) for c in send_counts], dtype=torch.int64, device=dev)
+    rc = torch.empty_like(sc)
+    dist.all_to_all_single(rc, sc, group=group)
+    recv_counts = [int(c) for c in rc.tolist()]
+    recv = torch.empty((sum(recv_counts),) + tuple(send.shape[1:]), dtype=send.dtype, device=dev)
+    dist.all_to_all_single(recv, send.contiguous(), recv_counts, [int(c) for c in send_counts], group=group)
+    return recv, recv_counts
+
+
+def _owner_of(codes: torch.Tensor, splitters: torch.Tensor) -> torch.Tensor:
+    """Rank whose code range [splitters[r], splitters[r + 1]) holds each code."""
+    return torch.searchsorted(splitters[1:-1].contiguous(), codes, right=True)
+
+
+CODE_END = (1 << 63) - 1      # end of the last code range (the all-ones 63-bit code, a voxel at 2^21 - 1 on every axis,
+                              # is not used: scene coordinates stay far below it)
+
+
+def morton_splitters(local_codes: torch.Tensor, group=None, samples: int = 1024) -> torch.Tensor:
+    """Code-range boundaries [world + 1] (int64) balancing the voxel counts over the ranks: every rank contributes
+    `samples` codes at evenly spaced quantiles of its sorted codes, weighted by its count (one all-gather), and the
+    ranges are cut at equal cumulative weight.  Codes several ranks back-project are counted once per rank here,
+    which only perturbs the balance."""
+    import torch.distributed as dist
+    world, _ = _world(group)
+    dev = local_codes.device
+    if world == 1:
+        return torch.tensor([0, CODE_END], dtype=torch.int64, device=dev)
+    srt = torch.sort(local_codes).values
+    n = int(srt.numel())
+    if n:
+        pick = srt[(torch.arange(samples, device=dev) * n) // samples]
+    else:
+        pick = torch.full((samples,), CODE_END, dtype=torch.int64, device=dev)
+    meta = torch.tensor([n], dtype=torch.int64, device=dev)
+    picks = [torch.empty_like(pick) for _ in range(world)]
+    metas = [torch.empty_like(meta) for _ in range(world)]
+    dist.all_gather(picks, pick, group=group)
+    dist.all_gather(metas, meta, group=group)
+    vals = torch.cat(picks)
+    wts = torch.cat([torch.full((samples,), float(m.item()) / samples, dtype=torch.float64, device=dev)
+                     for m in metas])
+    order = torch.argsort(vals, stable=True)
+    vals, cum = vals[order], torch.cumsum(wts[order], 0)
+    total = float(cum[-1]) if cum.numel() else 0.0
+    cuts = [0]
+    for r in range(1, world):
+        k = int(torch.searchsorted(cum, torch.tensor(total * r / world, dtype=torch.float64, device=dev)))
+        cuts.append(max(int(vals[min(k, vals.numel() - 1)]), cuts[-1]))
+    cuts.append(CODE_END)
+    return torch.tensor(cuts, dtype=torch.int64, device=dev)
+
+
+def distribute_codes(local_codes: torch.Tensor, splitters: torch.Tensor, group=None) -> torch.Tensor:
+    """This rank's owned voxels: every rank's codes sent to their owners (one all-to-all), merged and uniqued."""
+    world, _ = _world(group)
+    owner = _owner_of(local_codes, splitters)
+    order = torch.argsort(owner, stable=True)
+    counts = torch.bincount(owner, minlength=world)
+    recv, _ = _alltoallv(local_codes[order], counts.tolist(), group)
+    return torch.unique(recv)
+
+
+NEIGHBOUR_OFFSETS = [(dx, dy, dz) for dx in (-1, 0, 1) for dy in (-1, 0, 1) for dz in (-1, 0, 1)
+                     if (dx, dy, dz) != (0, 0, 0)]
+
+
+class LevelShard:
+    """One level of a Morton-sharded voxel set, built from this rank's owned codes alone.
+
+    owned_codes: this rank's voxels, sorted unique Morton codes inside [splitters[rank], splitters[rank + 1]).
+    nmap_fn(coords [M, 4] int32, extents) -> tap-major [27, M] int32 neighbour map of a voxel set (the library's hash
+    builder on GPUs, the oracle in the CPU tests).  The plan (`self.plan`, a ShardPlan) has the local row space
+    [owned rows | halo rows], the owned rows' neighbour map in it, and the halo exchange lists; `offset` is the global
+    index of the first owned voxel (global indices follow Morton order over all ranks)."""
+
+    def __init__(self, owned_codes: torch.Tensor, splitters: torch.Tensor, nmap_fn, group=None):
+        import torch.distributed as dist
+        world, rank = _world(group)
+        dev = owned_codes.device
+        self.codes = owned_codes
+        self.splitters = splitters
+        n_own = int(owned_codes.numel())
+        counts = torch.tensor([n_own], dtype=torch.int64, device=dev)
+        if world > 1:
+            parts = [torch.empty_like(counts) for _ in range(world)]
+            dist.all_gather(parts, counts, group=group)
+            allc = torch.cat(parts)
+        else:
+            allc = counts
+        self.counts = [int(c) for c in allc.tolist()]
+        self.offset = sum(self.counts[:rank])
+        lo, hi = int(splitters[rank]), int(splitters[rank + 1])
+        # neighbour candidates outside this rank's code range, each once, asked of their owners
+        x, y, z = demorton3(owned_codes)
+        limit = (1 << MORTON_BITS) - 1
+        cand = []
+        for dx, dy, dz in NEIGHBOUR_OFFSETS:
+            nx, ny, nz = x + dx, y + dy, z + dz
+            ok = (nx >= 0) & (ny >= 0) & (nz >= 0) & (nx <= limit) & (ny <= limit) & (nz <= limit)
+            c = morton3(nx[ok], ny[ok], nz[ok])
+            cand.append(c[(c < lo) | (c >= hi)])
+        ask = torch.unique(torch.cat(cand)) if cand else owned_codes[:0]
+        owner = _owner_of(ask, splitters)
+        ask_counts = torch.bincount(owner, minlength=world).tolist()
+        asked, asked_counts = _alltoallv(ask, ask_counts, group)          # codes other ranks ask this rank about
+        pos = torch.searchsorted(owned_codes, asked)
+        found = (pos < n_own) & (owned_codes[pos.clamp(max=max(n_own - 1, 0))] == asked) if n_own else \
+            torch.zeros_like(asked, dtype=torch.bool)
+        reply = torch.where(found, pos, torch.full_like(pos, -1))
+        back, _ = _alltoallv(reply, asked_counts, group)                  # for each of this rank's questions
+        exists = back >= 0
+        halo_codes = ask[exists]                                          # sorted by code = by owner, global order
+        self.halo_codes = halo_codes
+        # send lists: the owned rows each peer found, in the peer's (sorted) halo order
+        send_idx, send_splits, off = [], [], 0
+        for c in asked_counts:
+            r = reply[off:off + c]
+            r = r[r >= 0]
+            send_idx.append(r)
+            send_splits.append(int(r.numel()))
+            off += c
+        recv_splits = torch.bincount(owner[exists], minlength=world).tolist()
+        # the owned rows' neighbour map over owned + halo voxels, in the local row space
+        local_codes = torch.cat([owned_codes, halo_codes])
+        if local_codes.numel():
+            nm = nmap_fn(coords_of_codes(local_codes), [1, 1 << MORTON_BITS, 1 << MORTON_BITS, 1 << MORTON_BITS])
+        else:
+            nm = torch.empty((27, 0), dtype=torch.int32, device=dev)
+        self.plan = ShardPlan.from_parts(nm[:, :n_own].contiguous(), n_own, int(halo_codes.numel()), recv_splits,
+                                         torch.cat(send_idx).to(torch.int64) if send_idx else reply[:0],
+                                         send_splits, rank, world, group)
+
+
+class PoolPlan:
+    """The mean pool of level k's owned rows into the parents level k + 1 owns (code >> 3; flex_gemm's mean pool,
+    children summed in code order), planned once per structure: which owned rows go to which parent owner
+    (`send_idx`, `send_splits`), how many arrive (`recv_splits`), and the segments (`seg_idx`, `seg_off`) over the
+    pool buffer [owned rows | received rows] that list every owned parent's children in code order."""
+
+    def __init__(self, level: "LevelShard", next_level: "LevelShard", group=None):
+        world, rank = _world(group)
+        self.group = group
+        parents = level.codes >> 3
+        powner = _owner_of(parents, next_level.splitters)
+        away = powner != rank
+        away_idx = torch.nonzero(away).flatten()
+        order = torch.argsort(powner[away], stable=True)
+        self.send_idx = away_idx[order].contiguous()
+        self.send_splits = torch.bincount(powner[away], minlength=world).tolist()
+        got_codes, self.recv_splits = _alltoallv(level.codes[self.send_idx], self.send_splits, group)
+        self.n_own = int(level.codes.numel())
+        self.n_recv = int(got_codes.numel())
+        keep_idx = torch.nonzero(~away).flatten()
+        cand_idx = torch.cat([keep_idx, self.n_own + torch.arange(self.n_recv, device=keep_idx.device)])
+        cand_codes = torch.cat([level.codes[keep_idx], got_codes])
+        srt = torch.argsort(cand_codes, stable=True)                 # children in code order
+        codes = cand_codes[srt]
+        self.seg_idx = cand_idx[srt].to(torch.int32).contiguous()
+        pc, cnt = torch.unique_consecutive(codes >> 3, return_counts=True)
+        if not torch.equal(pc, next_level.codes):
+            raise RuntimeError("pooled parents differ from the next level's owned voxels")
+        self.n_parents = int(pc.numel())
+        self.seg_off = torch.zeros(self.n_parents + 1, dtype=torch.int32, device=codes.device)
+        self.seg_off[1:] = torch.cumsum(cnt, 0).to(torch.int32)
+
+    def buffer(self, C: int, device) -> torch.Tensor:
+        """[n_own + n_recv, C] fp32: the owned rows, then the rows other ranks send."""
+        return torch.empty((self.n_own + self.n_recv, C), dtype=torch.float32, device=device)
+
+    def apply(self, buf: torch.Tensor) -> torch.Tensor:
+        """Pool `buf` (owned rows written by the caller) into the owned parents' means [n_parents, C] fp32."""
+        from . import ops
+        import torch.distributed as dist
+        world, _ = _world(self.group)
+        if world > 1 and (sum(self.send_splits) or self.n_recv):
+            send = buf[:self.n_own].index_select(0, self.send_idx)
+            dist.all_to_all_single(buf[self.n_own:], send, self.recv_splits, self.send_splits, group=self.group)
+        if buf.is_cuda:
+            return ops.pool_mean(buf, self.seg_idx, self.seg_off, self.n_parents)
+        rows = buf[self.seg_idx.long()]
+        return torch.stack([_mean_in_order(rows[int(a):int(b)]) for a, b in zip(self.seg_off[:-1], self.seg_off[1:])]) \
+            if self.n_parents else buf[:0]
+
+
+def _mean_in_order(rows: torch.Tensor) -> torch.Tensor:
+    """fl(sum in row order / n) in fp32 (the pooling kernels' arithmetic), on the CPU."""
+    acc = torch.zeros(rows.shape[1], dtype=torch.float32)
+    for r in rows:
+        acc = acc + r
+    return acc / torch.tensor(float(rows.shape[0]), dtype=torch.float32)
+
+
+def build_levels(local_codes: torch.Tensor, levels: int, nmap_fn, group=None) -> list:
+    """Every level of a fused scene sharded by Morton ranges, from this rank's own back-projected codes.  Level 0:
+    codes to the owners of sample-balanced ranges, then once more to ranges balanced on the now unique owned voxels;
+    each coarser level: the parents (code >> 3) of the level below, balanced on their own counts and sent to their
+    owners.  Every level's ranges are balanced by that level's voxel count.  Returns [LevelShard] per level."""
+    owned = distribute_codes(local_codes, morton_splitters(local_codes, group), group)
+    splitters = morton_splitters(owned, group)
+    owned = distribute_codes(owned, splitters, group)
+    lv = [LevelShard(owned, splitters, nmap_fn, group)]
+    for _ in range(1, levels):
+        cand = torch.unique(lv[-1].codes >> 3)
+        splitters = morton_splitters(cand, group)
+        lv.append(LevelShard(distribute_codes(cand, splitters, group), splitters, nmap_fn, group))
+    return lv
+
+
+def encoder_layers(widths, convs_per_level: int, seed: int, device):
+    """Seeded int8 layers of a sharded U-Net encoder with the given level widths: per level `convs_per_level`
+    submanifold convs (weights [27, C, C]) and, between levels, a pooling transition's int8 linear ([C', C])."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    convs, links = [], []
+    for k, C in enumerate(widths):
+        lv = []
+        for _ in range(convs_per_level):
+            w = torch.randint(-127, 128, (27, C, C), generator=g, dtype=torch.int8)
+            ws = torch.rand(C, generator=g) * (4e-4 * 32 / C) + 1e-5
+            b = torch.randn(C, generator=g) * 0.1
+            lv.append((w.to(device), ws.to(device), b.to(device), 0.05, 0.04))
+        convs.append(lv)
+        if k + 1 < len(widths):
+            Cn = widths[k + 1]
+            w = torch.randint(-127, 128, (Cn, C), generator=g, dtype=torch.int8)
+            ws = torch.rand(Cn, generator=g) * (4e-3 * 32 / C) + 1e-4
+            b = torch.randn(Cn, generator=g) * 0.1
+            links.append((w.to(device), ws.to(device), b.to(device), 0.02, 0.04))
+    return convs, links
+
+
+def encoder_forward(levels: list, q0: torch.Tensor, convs, links, conv, link, group=None, out_scale: float = 0.04,
+                    pools=None):
+    """The sharded encoder pass: at every level its convs, each after a halo exchange of the int8 input rows, then
+    (between levels) the mean pool into parents (rows dequantised with the last conv's output scale, children moved
+    to their parent's owner and summed in code order, PoolPlan) and the transition's int8 linear.  conv(q_local,
+    nmap, mask, layer) and link(pooled fp32, layer) give the next int8 rows.  `pools`: the PoolPlans of the
+    transitions (built here when not given).  Returns the int8 rows of every level's owned voxels after its convs."""
+    if pools is None:
+        pools = [PoolPlan(levels[k], levels[k + 1], group) for k in range(len(levels) - 1)]
+    scale = torch.tensor(out_scale, dtype=torch.float32)
+    outs = []
+    q = q0
+    for k, lvl in enumerate(levels):
+        plan = lvl.plan
+        buf = plan.local_buffer(q.shape[1], q.dtype)
+        buf[:plan.n_own] = q
+        for layer in convs[k]:
+            plan.exchange(buf)
+            buf[:plan.n_own] = conv(buf, plan.nmap, plan.mask, layer)
+        q = buf[:plan.n_own]
+        outs.append(q)
+        if k + 1 < len(levels):
+            pb = pools[k].buffer(q.shape[1], q.device)
+            torch.mul(q, scale.to(q.device), out=pb[:plan.n_own])     # dequantise into the pool buffer
+            q = link(pools[k].apply(pb), links[k])
+    return outs
+
+
+def gpu_link(pooled: torch.Tensor, layer):
+    """A pooling transition on the device: quantise the pooled means with the linear's input scale, then the dense
+    int8 layer with the SiLU + requantise epilogue."""
+    from . import ops
+    w, ws, b, sa, s_out = layer
+    qp = ops.quantize(pooled.contiguous(), sa)
+    return ops.dense_i8(qp, w, ws, b, sa, ops.EPI_SILU_Q8, s_out)

@@ -56,3 +56,41 @@ def test_sharded_gpu_layers_equal_single_device(world):
     torch.cuda.synchronize()
     assert sum(p.n_halo for p in plans) > 0
     assert torch.equal(got, want)
+
+
+def test_sharded_levels_on_device_equal_oracle_structure():
+    """The sharded level build as the only rank on the GPU (hash neighbour maps): every level's voxels are the parents
+    of the level below, every neighbour map equals the oracle's over that level, and the encoder's level-0 output
+    equals the oracle's conv arithmetic (up to one-step SiLU requantise flips from CUDA's exp)."""
+    import numpy as np
+    from oracle import structure as ost
+    from promptmoge_b200 import fused, ops
+    from test_fused_levels import conv_cpu
+    layout = fused.scene_layout(11, 6)
+    codes = fused.scene_codes(11, layout, range(6), H=60, W=80, voxel=0.02, device="cuda")
+
+    def nmap_fn(coords, ext):
+        nm, _, st = ops.nmap_hash(coords, ext)
+        assert int(st.item()) == 0
+        return nm
+
+    widths = [32, 64, 128]
+    levels = fused.build_levels(codes, len(widths), nmap_fn, fused.LOCAL)
+    ext = [1, 1 << 21, 1 << 21, 1 << 21]
+    for k, lv in enumerate(levels):
+        if k:
+            assert torch.equal(lv.codes, torch.unique(levels[k - 1].codes >> 3))
+        want = ost.nmap_sorted(fused.coords_of_codes(lv.codes).cpu().numpy(), ext)
+        np.testing.assert_array_equal(lv.plan.nmap.t().cpu().numpy(), want)
+    convs, links = fused.encoder_layers(widths, 2, seed=3, device="cuda")
+    q0 = torch.randint(-127, 128, (levels[0].plan.n_own, widths[0]), dtype=torch.int8,
+                       generator=torch.Generator().manual_seed(1)).cuda()
+    outs = fused.encoder_forward(levels, q0, convs, links, fused.gpu_conv, fused.gpu_link, fused.LOCAL)
+    assert [o.shape[0] for o in outs] == [lv.plan.n_own for lv in levels]
+    cpu_layers = [tuple(t.cpu() if torch.is_tensor(t) else t for t in layer) for layer in convs[0]]
+    q = q0.cpu()
+    nm = levels[0].plan.nmap.cpu()
+    for layer in cpu_layers:
+        q = conv_cpu(q, nm, None, layer)
+    d = (outs[0].cpu().to(torch.int32) - q.to(torch.int32)).abs()
+    assert int(d.max()) <= 1 and float((d > 0).float().mean()) < 1e-3
