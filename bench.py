@@ -747,10 +747,12 @@ def fused_scene(args, ws, rank, local):
 def _port_step(steps: int, warm: int):
     """Time the CPU port of one refine step (the oracle: exact int8 convs in C on all host threads, oracle/conv.c, the
     rest in numpy), Model A at 480x640 plus the final metric fit; returns (seconds per step, description)."""
+    from oracle import build as obuild
     from oracle import fit as ofit
     from oracle import refiner as oref
     from promptmoge_b200 import synth
     from promptmoge_b200.refine import synthetic_model
+    obuild.build()           # the C restatement, if this host did not receive it prebuilt (gcc, seconds)
     weights, clips = synthetic_model("A", 0)
     ch = synth.MODELS["A"]["model_channels"]
     qr = oref.QuantRefiner(weights, clips, ch, [2] * (len(ch) - 1))
