@@ -333,6 +333,14 @@ def run_ours(args, ws, rank, local):
         c4 = c4_batched(torch, args, ws, rank, dev, weights, clips)
         if line is not None:
             line["c4"] = c4
+    if args.c5_poses > 0 and args.model == "A":
+        # config 5 sub-record: the fused scene over the same ranks (strong scaling), its own steps and warm-up
+        import copy
+        a5 = copy.copy(args)
+        a5.fused_poses, a5.steps, a5.warmup = args.c5_poses, args.c5_steps, 3
+        c5 = fused_scene(a5, ws, rank, local)
+        if line is not None:
+            line["c5"] = c5
     return line
 
 
@@ -682,36 +690,44 @@ def fused_scene(args, ws, rank, local):
     q0 = _rows_of_index(torch.arange(levels[0].offset, levels[0].offset + levels[0].plan.n_own, device=dev),
                         widths[0])
 
-    def step():
-        return fused.encoder_forward(levels, q0, convs, links, fused.gpu_conv, fused.gpu_link, group, pools=pools)
+    def step(overlap=True):
+        return fused.encoder_forward(levels, q0, convs, links, fused.gpu_conv, fused.gpu_link, group, pools=pools,
+                                     overlap=overlap)
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    if ws > 1:
-        dist.barrier()
-    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with Clocks(local) as clk:
-        s0.record()
-        for _ in range(args.steps):
-            outs = step()
-        s1.record()
+    def timed(overlap):
+        for _ in range(args.warmup):
+            step(overlap)
         torch.cuda.synchronize()
-    if ws > 1:
-        dist.barrier()
-    ms = s0.elapsed_time(s1)
+        if ws > 1:
+            dist.barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with Clocks(local) as clk:
+            s0.record()
+            for _ in range(args.steps):
+                o = step(overlap)
+            s1.record()
+            torch.cuda.synchronize()
+        if ws > 1:
+            dist.barrier()
+        return s0.elapsed_time(s1), o, clk
+
+    # every exchange beside the interior rows' conv (the headline); with several ranks also exchange-then-conv
+    ms_plain = timed(False)[0] if ws > 1 else None
+    ms, outs, clk = timed(True)
     build = [t1 - t0, t2 - t1]
     counts = [[l.plan.n_own for l in levels]]
     halos = [[l.plan.n_halo for l in levels]]
     digests = [hashlib.sha256(o.cpu().numpy().tobytes()).hexdigest() for o in outs]
+    all_digests = [digests]
     if ws > 1:
-        t = torch.tensor([ms] + build, device=dev, dtype=torch.float64)
+        t = torch.tensor([ms, ms_plain] + build, device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, build = float(t[0]), [float(x) for x in t[1:]]
+        ms, ms_plain, build = float(t[0]), float(t[1]), [float(x) for x in t[2:]]
         gathered = [None] * ws
-        dist.all_gather_object(gathered, (counts[0], halos[0], [o.cpu() for o in outs]))
+        dist.all_gather_object(gathered, (counts[0], halos[0], digests))
         counts = [g[0] for g in gathered]
         halos = [g[1] for g in gathered]
+        all_digests = [g[2] for g in gathered]
     verified = None
     if rank == 0:
         # the same pipeline as the only rank over the whole scene
@@ -719,11 +735,16 @@ def fused_scene(args, ws, rank, local):
         ref_levels = fused.build_levels(whole, len(widths), nmap_fn, fused.LOCAL)
         ref_q0 = _rows_of_index(torch.arange(ref_levels[0].plan.n_own, device=dev), widths[0])
         ref = fused.encoder_forward(ref_levels, ref_q0, convs, links, fused.gpu_conv, fused.gpu_link, fused.LOCAL)
-        if ws > 1:
-            got = [torch.cat([g[2][k] for g in gathered]) for k in range(len(widths))]
-        else:
-            got = [o.cpu() for o in outs]
-        verified = all(torch.equal(a, r.cpu()) for a, r in zip(got, ref))
+        # each rank's rows of a level are one contiguous Morton range of the whole level: compare their digests
+        verified = True
+        for k in range(len(widths)):
+            off = 0
+            for r in range(ws):
+                n = counts[r][k]
+                d = hashlib.sha256(ref[k][off:off + n].cpu().numpy().tobytes()).hexdigest()
+                verified = verified and d == all_digests[r][k]
+                off += n
+            verified = verified and off == ref[k].shape[0]
         M = [sum(c[k] for c in counts) for k in range(len(widths))]
     if rank != 0:
         return None
@@ -731,6 +752,7 @@ def fused_scene(args, ws, rank, local):
     value = vl * args.steps / (ms * 1e-3)
     return {"metric": "fused-scene voxel-layers/s (C5)", "value": round(value, 1), "unit": "voxel-layers/s",
             "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+            "ms_per_step_exchange_then_conv": round(ms_plain / args.steps, 4) if ms_plain is not None else None,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": f"C5: fused scene, {args.fused_poses} poses 480x640 into a 1 cm grid ({M[0]} voxels), "
                                    "sharded U-Net encoder with Model A widths: 2 int8 submanifold convs per level, "
@@ -740,7 +762,9 @@ def fused_scene(args, ws, rank, local):
                        "build_s": {"backproject_own_poses": round(build[0], 3),
                                    "levels_sharded_structure": round(build[1], 3)},
                        "sharding": "Morton ranges, count-balanced per level; coarser levels are parent codes",
-                       "exchange": "NCCL all-to-all (halo rows; children to their parent's owner)"},
+                       "exchange": "NCCL all-to-all (halo rows; children to their parent's owner); each halo "
+                                   "exchange runs beside the conv of the rows with no halo neighbour, the boundary "
+                                   "rows' conv after it lands"},
             "verified_vs_single_device": verified, "level_output_sha256_rank0": digests, "clocks": clk.summary()}
 
 
@@ -838,6 +862,9 @@ def main():
                     help="config 4 sub-record: frames of the batched sharded run (0 = skip)")
     ap.add_argument("--c4-K", type=int, default=3)
     ap.add_argument("--c4-batch", type=int, default=4, help="config 4: frames per graph replay")
+    ap.add_argument("--c5-poses", type=int, default=200,
+                    help="config 5 sub-record: poses of the fused scene run after the main line (0 = skip)")
+    ap.add_argument("--c5-steps", type=int, default=10, help="config 5 sub-record: timed encoder steps")
     args = ap.parse_args()
     if args.profile_conv is not None:
         print(json.dumps(profile_conv(args)), flush=True)

@@ -284,6 +284,7 @@ class ShardPlan:
             raise RuntimeError("halo request outside this rank's range")
         self.send_idx = (wanted.to(torch.int64) - self.lo).contiguous()
         self.group = group
+        self._split_boundary()
 
     @classmethod
     def from_parts(cls, nmap_local: torch.Tensor, n_own: int, n_halo: int, recv_splits, send_idx: torch.Tensor,
@@ -301,7 +302,23 @@ class ShardPlan:
         self.send_splits = [int(c) for c in send_splits]
         self.send_idx = send_idx.to(torch.int64).contiguous()
         self.group = group
+        self._split_boundary()
         return self
+
+    def _split_boundary(self):
+        """Interior rows (every neighbour owned) and boundary rows (some neighbour in the halo), for the conv that
+        overlaps the exchange: `perm` lists the owned rows interior first (each part in row order), `nmap_int` /
+        `nmap_bnd` are the two parts' columns of the neighbour map (indices still in the [owned | halo] row space)."""
+        bnd = (self.nmap >= self.n_own).any(dim=0) if self.n_own else torch.zeros(0, dtype=torch.bool,
+                                                                                    device=self.nmap.device)
+        inner = torch.nonzero(~bnd).flatten()
+        edge = torch.nonzero(bnd).flatten()
+        self.n_int = int(inner.numel())
+        self.perm = torch.cat([inner, edge])
+        self.nmap_int = self.nmap[:, inner].contiguous()
+        self.nmap_bnd = self.nmap[:, edge].contiguous()
+        self.mask_int = tile_mask_of(self.nmap_int)
+        self.mask_bnd = tile_mask_of(self.nmap_bnd)
 
     def local_buffer(self, C: int, dtype=torch.int8) -> torch.Tensor:
         """[n_own + n_halo, C] rows: owned first, halo rows after (filled by `exchange`)."""
@@ -315,6 +332,28 @@ class ShardPlan:
         send = buf.index_select(0, self.send_idx)
         dist.all_to_all_single(buf[self.n_own:], send, self.recv_splits, self.send_splits, group=self.group)
         return buf
+
+    def conv(self, buf: torch.Tensor, layer, conv, overlap: bool = True) -> None:
+        """One conv layer in place on the owned rows of `buf`: exchange the halo rows, then
+        `conv(q_local, nmap, mask, layer)`.  overlap: the interior rows' conv runs while the all-to-all is in flight
+        (it reads owned rows only) and the boundary rows' conv after it lands; both parts write their rows back in
+        row order, so the result equals the plain exchange-then-conv bit for bit."""
+        import torch.distributed as dist
+        exchanging = self.world > 1 and (self.n_halo or self.send_idx.numel())
+        if not (overlap and exchanging):
+            self.exchange(buf)
+            buf[:self.n_own] = conv(buf, self.nmap, self.mask, layer)
+            return
+        send = buf.index_select(0, self.send_idx)
+        work = dist.all_to_all_single(buf[self.n_own:], send, self.recv_splits, self.send_splits, group=self.group,
+                                      async_op=True)
+        parts = []
+        if self.n_int:
+            parts.append(conv(buf, self.nmap_int, self.mask_int, layer))
+        work.wait()
+        if self.n_own - self.n_int:
+            parts.append(conv(buf, self.nmap_bnd, self.mask_bnd, layer))
+        buf[:self.n_own].index_copy_(0, self.perm, torch.cat(parts) if len(parts) > 1 else parts[0])
 
     def halo_bytes(self, C: int) -> int:
         """int8 bytes this rank receives per conv layer."""
@@ -346,15 +385,13 @@ def exchange_in_process(plans, bufs):
             off += n
 
 
-def run_layers(plan: ShardPlan, q_own: torch.Tensor, layers, conv) -> torch.Tensor:
+def run_layers(plan: ShardPlan, q_own: torch.Tensor, layers, conv, overlap: bool = True) -> torch.Tensor:
     """A stack of int8 submanifold convs over the sharded voxels: before each layer the halo rows are exchanged, then
-    `conv(q_local, nmap, mask, layer)` returns the next int8 features of the owned rows."""
+    `conv(q_local, nmap, mask, layer)` returns the next int8 features of the owned rows (ShardPlan.conv)."""
     buf = plan.local_buffer(q_own.shape[1], q_own.dtype)
     buf[:plan.n_own] = q_own
     for layer in layers:
-        plan.exchange(buf)
-        out = conv(buf, plan.nmap, plan.mask, layer)
-        buf[:plan.n_own] = out
+        plan.conv(buf, layer, conv, overlap)
     return buf[:plan.n_own].clone()
 
 
@@ -632,12 +669,13 @@ def encoder_layers(widths, convs_per_level: int, seed: int, device):
 
 
 def encoder_forward(levels: list, q0: torch.Tensor, convs, links, conv, link, group=None, out_scale: float = 0.04,
-                    pools=None):
+                    pools=None, overlap: bool = True):
     """The sharded encoder pass: at every level its convs, each after a halo exchange of the int8 input rows, then
     (between levels) the mean pool into parents (rows dequantised with the last conv's output scale, children moved
     to their parent's owner and summed in code order, PoolPlan) and the transition's int8 linear.  conv(q_local,
     nmap, mask, layer) and link(pooled fp32, layer) give the next int8 rows.  `pools`: the PoolPlans of the
-    transitions (built here when not given).  Returns the int8 rows of every level's owned voxels after its convs."""
+    transitions (built here when not given).  overlap: each exchange runs beside the interior rows' conv
+    (ShardPlan.conv).  Returns the int8 rows of every level's owned voxels after its convs."""
     if pools is None:
         pools = [PoolPlan(levels[k], levels[k + 1], group) for k in range(len(levels) - 1)]
     scale = torch.tensor(out_scale, dtype=torch.float32)
@@ -648,8 +686,7 @@ def encoder_forward(levels: list, q0: torch.Tensor, convs, links, conv, link, gr
         buf = plan.local_buffer(q.shape[1], q.dtype)
         buf[:plan.n_own] = q
         for layer in convs[k]:
-            plan.exchange(buf)
-            buf[:plan.n_own] = conv(buf, plan.nmap, plan.mask, layer)
+            plan.conv(buf, layer, conv, overlap)
         q = buf[:plan.n_own]
         outs.append(q)
         if k + 1 < len(levels):

@@ -51,7 +51,7 @@ def link_cpu(pooled, layer):
     return torch.from_numpy(np.clip(np.rint(oref.silu(y) / np.float32(s_out)), -127, 127).astype(np.int8))
 
 
-def _run(local_codes, group):
+def _run(local_codes, group, overlap=True):
     levels = fused.build_levels(local_codes, len(WIDTHS), nmap_cpu, group)
     convs, links = fused.encoder_layers(WIDTHS, 2, seed=9, device="cpu")
     rng = np.random.default_rng(17)
@@ -59,7 +59,7 @@ def _run(local_codes, group):
     # level-0 input: a deterministic function of the voxel's global index
     g_all = torch.from_numpy(rng.integers(-127, 128, (200000, WIDTHS[0])).astype(np.int8))
     q0 = g_all[n0:n0 + levels[0].plan.n_own]
-    outs = fused.encoder_forward(levels, q0, convs, links, conv_cpu, link_cpu, group)
+    outs = fused.encoder_forward(levels, q0, convs, links, conv_cpu, link_cpu, group, overlap=overlap)
     return levels, outs
 
 
@@ -76,8 +76,10 @@ def _worker(rank, world, port, q):
     try:
         b, e = frame_range(POSES, rank, world)
         levels, outs = _run(_codes(range(b, e)), None)
+        _, plain = _run(_codes(range(b, e)), None, overlap=False)     # exchange first, then the whole conv
+        assert all(torch.equal(a, p) for a, p in zip(outs, plain))
         q.put((rank, [l.codes for l in levels], [l.offset for l in levels], outs,
-               [l.plan.n_halo for l in levels]))
+               [l.plan.n_halo for l in levels], [l.plan.n_int for l in levels]))
     finally:
         dist.destroy_process_group()
 
@@ -98,6 +100,7 @@ def test_sharded_levels_and_encoder_equal_single_rank(world):
         p.join(timeout=60)
         assert p.exitcode == 0
     assert sum(r[4][0] for r in res) > 0                      # the shards really exchanged halo rows
+    assert all(0 < r[5][0] < r[1][0].numel() for r in res)     # level 0 has interior and boundary rows on every rank
     for k in range(len(WIDTHS)):
         codes = torch.cat([r[1][k] for r in res])
         assert torch.equal(codes, ref_levels[k].codes), k     # ranges partition the level in Morton order

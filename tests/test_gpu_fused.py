@@ -47,14 +47,21 @@ def test_sharded_gpu_layers_equal_single_device(world):
     bufs = [p.local_buffer(C) for p in plans]
     for p, b, (lo, hi) in zip(plans, bufs, bounds):
         b[:p.n_own] = q0[lo:hi]
-    for layer in layers:
+    for i, layer in enumerate(layers):
         fused.exchange_in_process(plans, bufs)
         outs = [fused.gpu_conv(b, p.nmap, p.mask, layer) for p, b in zip(plans, bufs)]
+        # the overlapped form (ShardPlan.conv): interior rows, then boundary rows, written back in row order
+        for p, b, o in zip(plans, bufs, outs):
+            parts = [fused.gpu_conv(b, p.nmap_int, p.mask_int, layer), fused.gpu_conv(b, p.nmap_bnd, p.mask_bnd, layer)]
+            split = torch.empty_like(o)
+            split.index_copy_(0, p.perm, torch.cat(parts))
+            assert torch.equal(split, o), i
         for p, b, o in zip(plans, bufs, outs):
             b[:p.n_own] = o
     got = torch.cat([b[:p.n_own] for p, b in zip(plans, bufs)])
     torch.cuda.synchronize()
     assert sum(p.n_halo for p in plans) > 0
+    assert all(0 < p.n_int < p.n_own for p in plans)
     assert torch.equal(got, want)
 
 
