@@ -333,7 +333,7 @@ class ShardPlan:
         dist.all_to_all_single(buf[self.n_own:], send, self.recv_splits, self.send_splits, group=self.group)
         return buf
 
-    def conv(self, buf: torch.Tensor, layer, conv, overlap: bool = True) -> None:
+    def conv(self, buf: torch.Tensor, layer, conv, overlap: bool = False) -> None:
         """One conv layer in place on the owned rows of `buf`: exchange the halo rows, then
         `conv(q_local, nmap, mask, layer)`.  overlap: the interior rows' conv runs while the all-to-all is in flight
         (it reads owned rows only) and the boundary rows' conv after it lands; both parts write their rows back in
@@ -385,7 +385,7 @@ def exchange_in_process(plans, bufs):
             off += n
 
 
-def run_layers(plan: ShardPlan, q_own: torch.Tensor, layers, conv, overlap: bool = True) -> torch.Tensor:
+def run_layers(plan: ShardPlan, q_own: torch.Tensor, layers, conv, overlap: bool = False) -> torch.Tensor:
     """A stack of int8 submanifold convs over the sharded voxels: before each layer the halo rows are exchanged, then
     `conv(q_local, nmap, mask, layer)` returns the next int8 features of the owned rows (ShardPlan.conv)."""
     buf = plan.local_buffer(q_own.shape[1], q_own.dtype)
@@ -668,17 +668,30 @@ def encoder_layers(widths, convs_per_level: int, seed: int, device):
     return convs, links
 
 
+_SCALARS = {}
+
+
+def _device_scalar(v: float, device) -> torch.Tensor:
+    """A 0-dim fp32 tensor of v on `device`, made once (a step captured in a CUDA graph may not copy from the host)."""
+    key = (float(v), str(device))
+    t = _SCALARS.get(key)
+    if t is None:
+        t = _SCALARS[key] = torch.tensor(float(v), dtype=torch.float32, device=device)
+    return t
+
+
 def encoder_forward(levels: list, q0: torch.Tensor, convs, links, conv, link, group=None, out_scale: float = 0.04,
-                    pools=None, overlap: bool = True):
+                    pools=None, overlap: bool = False):
     """The sharded encoder pass: at every level its convs, each after a halo exchange of the int8 input rows, then
     (between levels) the mean pool into parents (rows dequantised with the last conv's output scale, children moved
     to their parent's owner and summed in code order, PoolPlan) and the transition's int8 linear.  conv(q_local,
     nmap, mask, layer) and link(pooled fp32, layer) give the next int8 rows.  `pools`: the PoolPlans of the
     transitions (built here when not given).  overlap: each exchange runs beside the interior rows' conv
-    (ShardPlan.conv).  Returns the int8 rows of every level's owned voxels after its convs."""
+    (ShardPlan.conv; measured slower on B200 at 2 and 4 GPUs, where the halo is a few percent of the rows, so off by
+    default).  Returns the int8 rows of every level's owned voxels after its convs."""
     if pools is None:
         pools = [PoolPlan(levels[k], levels[k + 1], group) for k in range(len(levels) - 1)]
-    scale = torch.tensor(out_scale, dtype=torch.float32)
+    scale = _device_scalar(out_scale, q0.device)
     outs = []
     q = q0
     for k, lvl in enumerate(levels):
@@ -691,7 +704,7 @@ def encoder_forward(levels: list, q0: torch.Tensor, convs, links, conv, link, gr
         outs.append(q)
         if k + 1 < len(levels):
             pb = pools[k].buffer(q.shape[1], q.device)
-            torch.mul(q, scale.to(q.device), out=pb[:plan.n_own])     # dequantise into the pool buffer
+            torch.mul(q, scale, out=pb[:plan.n_own])                  # dequantise into the pool buffer
             q = link(pools[k].apply(pb), links[k])
     return outs
 

@@ -51,7 +51,7 @@ def link_cpu(pooled, layer):
     return torch.from_numpy(np.clip(np.rint(oref.silu(y) / np.float32(s_out)), -127, 127).astype(np.int8))
 
 
-def _run(local_codes, group, overlap=True):
+def _run(local_codes, group, overlap=False):
     levels = fused.build_levels(local_codes, len(WIDTHS), nmap_cpu, group)
     convs, links = fused.encoder_layers(WIDTHS, 2, seed=9, device="cpu")
     rng = np.random.default_rng(17)
@@ -76,9 +76,10 @@ def _worker(rank, world, port, q):
     try:
         b, e = frame_range(POSES, rank, world)
         levels, outs = _run(_codes(range(b, e)), None)
-        _, plain = _run(_codes(range(b, e)), None, overlap=False)     # exchange first, then the whole conv
+        _, plain = _run(_codes(range(b, e)), None, overlap=True)      # exchanges beside the interior rows' conv
         assert all(torch.equal(a, p) for a, p in zip(outs, plain))
-        q.put((rank, [l.codes for l in levels], [l.offset for l in levels], outs,
+        # numpy arrays travel by value: shared-memory tensors would need this process alive while the parent reads
+        q.put((rank, [l.codes.numpy() for l in levels], [l.offset for l in levels], [o.numpy() for o in outs],
                [l.plan.n_halo for l in levels], [l.plan.n_int for l in levels]))
     finally:
         dist.destroy_process_group()
@@ -95,7 +96,9 @@ def test_sharded_levels_and_encoder_equal_single_rank(world):
     procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    res = sorted(q.get(timeout=300) for _ in range(world))
+    res = sorted((q.get(timeout=300) for _ in range(world)), key=lambda r: r[0])
+    res = [(r[0], [torch.from_numpy(c) for c in r[1]], r[2], [torch.from_numpy(o) for o in r[3]], r[4], r[5])
+           for r in res]
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
