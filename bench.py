@@ -311,6 +311,8 @@ def run_ours(args, ws, rank, local):
             "vs_baseline_basis": f"the reference's published int8 Metal time for one refine step of Model "
                                  f"{args.model} on an iPad Pro M5 ({PUBLISHED_MS[args.model]} ms, docs/index.html:453)",
             "dtype": "int8", "data": "synthetic",
+            "reference_arm": "bench.py --impl reference times one frame's step on the host cores of one machine "
+                             "(rank 0 only at any N), so against this line's N-GPU aggregate its ratio grows with N",
             "config": {"workload": (f"C2: Model A refiner (widths 32-64-128-256-256), 1 refine step, 480x640, "
                                     if args.model == "A" else
                                     "C1: Model B refiner (widths 32-64-128-256), 1 refine step, 240x320, ")
@@ -883,6 +885,7 @@ def run_reference(args, ws, rank):
             "warmup": warm, "ms_per_step": round(dt * 1e3, 1), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "steps_note": "CPU steps take seconds: at most 3 timed steps (the GPU arm times --steps)",
+            "scope": "one frame at a time on the host cores of one machine, whatever --gpus says",
             "config": {"workload": "C2: Model A refiner, 1 refine step, 480x640, batch 1 (synthetic room, seed 0)",
                        "K": 1},
             "cpu_baseline": {"value": v, "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": sample,
