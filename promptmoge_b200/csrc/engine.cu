@@ -242,7 +242,7 @@ int allocate(pmg_refiner* r) {
         const LevelBuf& l = r->lv[k];
         r->lsplit[k] = 1;
         if (!c.use_tensor_cores || l.C < 128 || max_split < 2) continue;
-        const int64_t units = l.cap / 128 * (l.C / 128);
+        const int64_t units = l.cap / 128 * (l.C == 256 ? 1 : l.C / 128);   // N blocks as the gather kernel cuts them
         if (units >= kNumSMs) continue;       // a level that fills the SMs never splits
         const int sp = max_split;
         r->lsplit[k] = sp;

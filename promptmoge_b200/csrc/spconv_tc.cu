@@ -1,6 +1,7 @@
 // tcgen05 (5th-generation tensor core) int8 implicit-GEMM kernels: the refiner's submanifold convs and dense layers.
 //
-// One persistent CTA per SM walks work units = (128-row output tile, N block of NT <= 128 output channels).  A unit's
+// One persistent CTA per SM walks work units = (128-row output tile, N block of NT output channels: NT = Co up to 128,
+// and NT = 256 for the 256-channel convs, whose neighbour rows are then gathered once rather than twice).  A unit's
 // reduction is a stream of items through an NST-stage shared-memory ring; an item is K = 128 bytes: 128 / Ci taps of
 // a narrow conv (4 taps at Ci = 32, 2 at Ci = 64), or one 128-byte K-block of a wide layer.  Warp roles:
 //   warps 0-7   producers:
@@ -15,7 +16,7 @@
 //   thread 0    also publishes unit records {first row, rows, tap mask, items} three units ahead into an 8-deep ring
 //               (tap masks prefetched from the per-tile mask array), read by producers, MMA and epilogue warps.
 //   warps 8-9   MMA issue: each owns one partial accumulator per TMEM buffer (two buffers, 128 lanes x NT int32
-//               columns each) and issues alternate items of every unit (tcgen05.mma.cta_group::1.kind::i8, K = 32
+//               columns each; one buffer at NT = 256, all 512 columns) and issues alternate items of every unit (tcgen05.mma.cta_group::1.kind::i8, K = 32
 //               bytes per instruction), tcgen05.commit releasing stages and publishing its finished partial.  Two
 //               issuing threads halve the per-item issue latency that bounds a single thread.
 //   warps 10-17 epilogue, two warps per TMEM lane quarter (each half of the columns): tcgen05.ld 32x32b.x16 of both
@@ -135,6 +136,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     using C = Cfg<KIND, NT, W, RES>;
     constexpr int NST = C::kStages;
     constexpr int NCOLS = tmem_cols<NT>();
+    // accumulator buffers: two (the next unit accumulates while the epilogue drains this one) while both MMA warps'
+    // partials of both fit the SM's 512 TMEM columns; one at NT = 256 (those convs run at most a unit or two per CTA)
+    constexpr int NBUF = 4 * NCOLS <= 512 ? 2 : 1;
+    static_assert(2 * NBUF * NCOLS <= 512, "TMEM columns");
     constexpr uint32_t IDESC = instr_desc(kM, NT);
     constexpr int TPI = W < kItemK ? kItemK / W : 1;  // most taps per item
     constexpr int CPR = W / 16;                      // 16-byte chunks of one tap row in an item
@@ -192,7 +197,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             s_ws[n] = e.ws[n];
             s_bias[n] = e.bias[n];
         }
-    if (warp == kMma0) tmem_alloc(tmem_slot, 4 * NCOLS);
+    if (warp == kMma0) tmem_alloc(tmem_slot, 2 * NBUF * NCOLS);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -500,8 +505,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tile_of(u / nblk, m0, mc, mk);
                 }
                 const int nitems = ((__popc(mk) + tpi - 1) / tpi) * nkb;
-                const uint32_t b = k & 1u;
-                if (!mbar_wait(&acc_empty[b], ((k >> 1) & 1u) ^ 1u, &s_abort)) { ok = false; break; }
+                const uint32_t b = k % NBUF;
+                if (!mbar_wait(&acc_empty[b], ((k / NBUF) & 1u) ^ 1u, &s_abort)) { ok = false; break; }
                 tc_fence_after();
                 const uint32_t d = tmem + (2 * b + (uint32_t)mw) * NCOLS;
                 uint32_t accumulate = 0;
@@ -593,8 +598,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool two = ((__popc(mk) + tpi - 1) / tpi) * nkb > 1;
             const uint32_t tb = (uint32_t)u / (uint32_t)S;
             const int n0 = (int)(tb % (uint32_t)nblk) * NT;
-            const uint32_t b = k & 1u;
-            if (!mbar_wait(&acc_full[b], (k >> 1) & 1u, &s_abort)) { ok = false; break; }
+            const uint32_t b = k % NBUF;
+            if (!mbar_wait(&acc_full[b], (k / NBUF) & 1u, &s_abort)) { ok = false; break; }
             tc_fence_after();
             const int rr = 32 * q + lane;
             const bool live = rr < mc;
@@ -667,7 +672,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (warp == kMma0) {
         tc_fence_after();
-        tmem_dealloc(tmem, 4 * NCOLS);
+        tmem_dealloc(tmem, 2 * NBUF * NCOLS);
     }
 }
 
@@ -762,7 +767,7 @@ int launch(const TcArgs& a, const Epi& e, cudaStream_t s) {
 template <int KIND, int NT, int W>
 int launch_res(const TcArgs& a, const Epi& e, cudaStream_t s) {
     // split-K variant: the wide gather convs (the coarse levels, whose tile counts can leave SMs idle)
-    if constexpr (KIND == tc::GATHER && NT == 128 && W == 128) {
+    if constexpr (KIND == tc::GATHER && NT >= 128 && W == 128) {
         if (e.nsplit > 1 && e.part) return launch<KIND, NT, W, false, true>(a, e, s);
     }
     // whole 27-tap weight resident in shared memory when it is one N block and leaves a ring of >= 4 stages
@@ -776,13 +781,17 @@ int launch_res(const TcArgs& a, const Epi& e, cudaStream_t s) {
 
 template <int KIND>
 int dispatch(const TcArgs& a, const Epi& e, cudaStream_t s) {
-    const int NTv = a.Co < 128 ? a.Co : 128;
+    // a 256-channel conv is one N block (its neighbour rows are gathered once, not once per 128 channels)
+    const int NTv = a.Co < 128 ? a.Co : ((KIND == tc::GATHER && a.Co == 256 && a.Ci >= 128) ? 256 : 128);
     const int Wv = a.Ci < 128 ? a.Ci : 128;
 #define PMG_TC_CASE(NT_, W_) \
     if (NTv == NT_ && Wv == W_) return launch_res<KIND, NT_, W_>(a, e, s);
     PMG_TC_CASE(32, 32) PMG_TC_CASE(32, 64) PMG_TC_CASE(32, 128)
     PMG_TC_CASE(64, 32) PMG_TC_CASE(64, 64) PMG_TC_CASE(64, 128)
     PMG_TC_CASE(128, 32) PMG_TC_CASE(128, 64) PMG_TC_CASE(128, 128)
+    if constexpr (KIND == tc::GATHER) {
+        PMG_TC_CASE(256, 128)
+    }
 #undef PMG_TC_CASE
     return PMG_ERR_UNSUPPORTED;
 }
