@@ -243,7 +243,7 @@ int allocate(pmg_refiner* r) {
         r->lsplit[k] = 1;
         if (!c.use_tensor_cores || l.C < 128 || max_split < 2) continue;
         const int64_t units = l.cap / 128 * (l.C == 256 ? 1 : l.C / 128);   // N blocks as the gather kernel cuts them
-        if (units >= kNumSMs) continue;       // a level that fills the SMs never splits
+        if (2 * units > kNumSMs) continue;    // a level that cannot split at least twice at capacity never splits
         const int sp = max_split;
         r->lsplit[k] = sp;
         part_elems = std::max(part_elems, (size_t)(sp * l.cap * l.C));
