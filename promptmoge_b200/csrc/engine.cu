@@ -375,6 +375,7 @@ int resblock(pmg_refiner* r, int k, const RB& b, const float* up_src, const int3
         LAUNCH(ln_silu_q8(l.X, up_src, parent, l.S, l.X, cnt, l.cap, l.C, b.norm.g, b.norm.b, 1e-6, b.c1.sa, l.q1, s));
     LAUNCH(conv(r, k, l, l.q1, b.c1, PMG_EPI_SILU_Q8, b.c2.sa, nullptr, l.q2, cnt, s));
     LAUNCH(conv(r, k, l, l.q2, b.c2, PMG_EPI_F32_RESID, 0.f, l.X, l.S, cnt, s, uq, uq_scale));
+    if (r->lsplit[k] > 1 && r->split_part && r->cfg.use_tensor_cores) nl += 2;   // each conv's split-K epilogue
     return PMG_OK;
 }
 
