@@ -91,12 +91,13 @@ class Refiner:
             ld, lc = self.d_ld, self.d_lc
         # the step's own inputs on the step's stream; the per-frame conditioning (encoder feature, UV planes,
         # encoder_fuse) on a side stream that the step waits for only before its encoder fusion, so its copy and
-        # kernels overlap the finer levels.  The side stream first waits for the previous call's step.
+        # kernels overlap the finer levels.  The side stream waits for the step's input copies (and so for the
+        # previous call's step): its host copies then follow them on the bus instead of sharing it with them.
         if self._side is None:
             self._side = torch.cuda.Stream(self.device)
-        self._side.wait_stream(s)
         for dst, src in ((self.d_pc, point_coord), (ld, lidar_depth), (lc, lidar_conf)):
             dst.copy_(torch.as_tensor(src), non_blocking=True)
+        self._side.wait_stream(s)
         if fill:
             ops.nearest_fill(ld, lc, out=(self.d_ld, self.d_lc))
         with torch.cuda.stream(self._side):
