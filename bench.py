@@ -685,7 +685,7 @@ def fused_scene(args, ws, rank, local):
     local_codes = fused.scene_codes(0, layout, range(b, e), device=dev)
     torch.cuda.synchronize()
     t1 = time.perf_counter()
-    levels = fused.build_levels(local_codes, len(widths), nmap_fn, group)
+    levels = fused.build_levels(local_codes, len(widths), nmap_fn, group, aligned=args.fused_ranges == "aligned")
     pools = [fused.PoolPlan(levels[k], levels[k + 1], group) for k in range(len(widths) - 1)]
     torch.cuda.synchronize()
     t2 = time.perf_counter()
@@ -818,7 +818,11 @@ def fused_scene(args, ws, rank, local):
                        "convs_per_level": 2, "widths": widths,
                        "build_s": {"backproject_own_poses": round(build[0], 3),
                                    "levels_sharded_structure": round(build[1], 3)},
-                       "sharding": "Morton ranges, count-balanced per level; coarser levels are parent codes",
+                       "sharding": ("Morton ranges: level 0 cut to balance the whole encoder's work, every coarser "
+                                    "level's ranges the parent codes of the level-0 boundaries (a parent's children "
+                                    "stay on its rank)") if args.fused_ranges == "aligned" else
+                                   ("Morton ranges balanced on every level's own count; parents whose children all "
+                                    "sit on one rank are pooled there and only the pooled row moves"),
                        "exchange": "NCCL all-to-all (halo rows; children to their parent's owner) before each "
                                    "conv; eager_overlapped: each halo exchange beside the conv of the rows with no "
                                    "halo neighbour, the boundary rows' conv after it lands",
@@ -918,6 +922,8 @@ def main():
     ap.add_argument("--sweep-n", default="100000,500000,2000000,8000000")
     ap.add_argument("--fused-scene", action="store_true", help="config 5: fused multi-pose scene over Morton shards")
     ap.add_argument("--fused-poses", type=int, default=200)
+    ap.add_argument("--fused-ranges", choices=["aligned", "balanced"], default="balanced",
+                    help="config 5: coarser levels' ranges the parents of level 0's (aligned) or balanced per level")
     ap.add_argument("--c4-frames", type=int, default=256,
                     help="config 4 sub-record: frames of the batched sharded run (0 = skip)")
     ap.add_argument("--c4-K", type=int, default=3)

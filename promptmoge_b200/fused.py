@@ -325,9 +325,10 @@ class ShardPlan:
         return torch.empty((self.n_own + self.n_halo, C), dtype=dtype, device=self.nmap.device)
 
     def exchange(self, buf: torch.Tensor) -> torch.Tensor:
-        """Fill the halo rows of `buf` from their owners (one all-to-all of int8 rows)."""
+        """Fill the halo rows of `buf` from their owners (one all-to-all of int8 rows).  Every rank of the group takes
+        part, also one that neither sends nor receives (a collective must be entered by all of them)."""
         import torch.distributed as dist
-        if self.world == 1 or (not self.n_halo and not self.send_idx.numel()):
+        if self.world == 1:
             return buf
         send = buf.index_select(0, self.send_idx)
         dist.all_to_all_single(buf[self.n_own:], send, self.recv_splits, self.send_splits, group=self.group)
@@ -339,8 +340,7 @@ class ShardPlan:
         (it reads owned rows only) and the boundary rows' conv after it lands; both parts write their rows back in
         row order, so the result equals the plain exchange-then-conv bit for bit."""
         import torch.distributed as dist
-        exchanging = self.world > 1 and (self.n_halo or self.send_idx.numel())
-        if not (overlap and exchanging):
+        if not (overlap and self.world > 1):
             self.exchange(buf)
             buf[:self.n_own] = conv(buf, self.nmap, self.mask, layer)
             return
@@ -455,23 +455,31 @@ CODE_END = (1 << 63) - 1      # end of the last code range (the all-ones 63-bit 
                               # is not used: scene coordinates stay far below it)
 
 
-def morton_splitters(local_codes: torch.Tensor, group=None, samples: int = 1024) -> torch.Tensor:
-    """Code-range boundaries [world + 1] (int64) balancing the voxel counts over the ranks: every rank contributes
-    `samples` codes at evenly spaced quantiles of its sorted codes, weighted by its count (one all-gather), and the
-    ranges are cut at equal cumulative weight.  Codes several ranks back-project are counted once per rank here,
-    which only perturbs the balance."""
+def morton_splitters(local_codes: torch.Tensor, group=None, samples: int = 1024, weights=None) -> torch.Tensor:
+    """Code-range boundaries [world + 1] (int64) balancing the voxel counts (or the per-voxel `weights`, aligned with
+    `local_codes`) over the ranks: every rank contributes `samples` codes at evenly spaced quantiles of the cumulative
+    weight of its sorted codes, each carrying 1/samples of its total (one all-gather), and the ranges are cut at equal
+    cumulative weight.  Codes several ranks back-project are counted once per rank here, which only perturbs the
+    balance."""
     import torch.distributed as dist
     world, _ = _world(group)
     dev = local_codes.device
     if world == 1:
         return torch.tensor([0, CODE_END], dtype=torch.int64, device=dev)
-    srt = torch.sort(local_codes).values
+    srt, order = torch.sort(local_codes)
     n = int(srt.numel())
-    if n:
+    if n and weights is not None:
+        cw = torch.cumsum(weights.to(torch.float64)[order], 0)
+        tot = float(cw[-1])
+        at = torch.arange(samples, device=dev, dtype=torch.float64) * (tot / samples)
+        pick = srt[torch.searchsorted(cw, at, right=True).clamp(max=n - 1)]
+    elif n:
+        tot = float(n)
         pick = srt[(torch.arange(samples, device=dev) * n) // samples]
     else:
+        tot = 0.0
         pick = torch.full((samples,), CODE_END, dtype=torch.int64, device=dev)
-    meta = torch.tensor([n], dtype=torch.int64, device=dev)
+    meta = torch.tensor([tot], dtype=torch.float64, device=dev)
     picks = [torch.empty_like(pick) for _ in range(world)]
     metas = [torch.empty_like(meta) for _ in range(world)]
     dist.all_gather(picks, pick, group=group)
@@ -573,35 +581,85 @@ class LevelShard:
 
 class PoolPlan:
     """The mean pool of level k's owned rows into the parents level k + 1 owns (code >> 3; flex_gemm's mean pool,
-    children summed in code order), planned once per structure: which owned rows go to which parent owner
-    (`send_idx`, `send_splits`), how many arrive (`recv_splits`), and the segments (`seg_idx`, `seg_off`) over the
-    pool buffer [owned rows | received rows] that list every owned parent's children in code order."""
+    children summed in code order), planned once per structure.  A parent's eight possible children are one Morton
+    range: when that range lies inside this rank's level-k range, all of the parent's children are here, and the
+    parent is pooled here (segment `pool_seg_*`) even when another rank owns it -- only the pooled row travels.  Only
+    a parent whose children straddle a range boundary has raw children sent to its owner, which pools them together
+    with its own in code order (`seg_*` over [owned rows | received rows]).  Pooled and raw rows go in ONE all-to-all,
+    grouped by destination.  The sums and their order are those of a single-device pool, so results are identical."""
 
     def __init__(self, level: "LevelShard", next_level: "LevelShard", group=None):
         world, rank = _world(group)
-        self.group = group
-        parents = level.codes >> 3
+        self.group, self.world = group, world
+        codes = level.codes
+        dev = codes.device
+        self.n_own = n_own = int(codes.numel())
+        parents = codes >> 3
         powner = _owner_of(parents, next_level.splitters)
-        away = powner != rank
-        away_idx = torch.nonzero(away).flatten()
-        order = torch.argsort(powner[away], stable=True)
-        self.send_idx = away_idx[order].contiguous()
-        self.send_splits = torch.bincount(powner[away], minlength=world).tolist()
-        got_codes, self.recv_splits = _alltoallv(level.codes[self.send_idx], self.send_splits, group)
-        self.n_own = int(level.codes.numel())
-        self.n_recv = int(got_codes.numel())
-        keep_idx = torch.nonzero(~away).flatten()
-        cand_idx = torch.cat([keep_idx, self.n_own + torch.arange(self.n_recv, device=keep_idx.device)])
-        cand_codes = torch.cat([level.codes[keep_idx], got_codes])
-        srt = torch.argsort(cand_codes, stable=True)                 # children in code order
-        codes = cand_codes[srt]
+        lo, hi = int(level.splitters[rank]), int(level.splitters[rank + 1])
+        pu, inv, cnt = torch.unique_consecutive(parents, return_inverse=True, return_counts=True)
+        first = torch.cumsum(cnt, 0) - cnt
+        gown = powner[first] if n_own else powner[:0]
+        complete = ((pu << 3) >= lo) & ((pu << 3) + 7 < hi)
+        # parents pooled here for another rank, grouped by destination (code order within)
+        pg = torch.nonzero((gown != rank) & complete).flatten()
+        pg = pg[torch.argsort(gown[pg], stable=True)]
+        self.n_pool_send = int(pg.numel())
+        self.pool_seg_off = torch.zeros(self.n_pool_send + 1, dtype=torch.int32, device=dev)
+        self.pool_seg_off[1:] = torch.cumsum(cnt[pg], 0).to(torch.int32)
+        # a group's children are consecutive owned rows: first[g] + 0 .. cnt[g] - 1
+        starts = torch.repeat_interleave(self.pool_seg_off[:-1].long(), cnt[pg])
+        base = torch.repeat_interleave(first[pg], cnt[pg])
+        self.pool_seg_idx = (base + torch.arange(int(starts.numel()), device=dev) - starts).to(torch.int32)
+        pool_send_counts = torch.bincount(gown[pg], minlength=world)
+        # raw children of straddling parents owned elsewhere, grouped by destination (code order within)
+        raw_child = ((gown != rank) & ~complete)[inv] if n_own else torch.zeros(0, dtype=torch.bool, device=dev)
+        rc = torch.nonzero(raw_child).flatten()
+        rc = rc[torch.argsort(powner[rc], stable=True)]
+        self.raw_send_idx = rc
+        raw_send_counts = torch.bincount(powner[rc], minlength=world)
+        # metadata: which parents arrive pooled, which children arrive raw
+        got_p, pool_recv = _alltoallv(pu[pg], pool_send_counts.tolist(), group)
+        got_c, raw_recv = _alltoallv(codes[rc], raw_send_counts.tolist(), group)
+        # one all-to-all of rows: to each destination its pooled rows, then its raw children
+        ps, rs_ = pool_send_counts.tolist(), raw_send_counts.tolist()
+        perm, po, ro = [], 0, 0
+        for d in range(world):
+            perm.append(torch.arange(po, po + ps[d], device=dev))
+            perm.append(self.n_pool_send + torch.arange(ro, ro + rs_[d], device=dev))
+            po += ps[d]
+            ro += rs_[d]
+        self.send_perm = torch.cat(perm) if perm else torch.zeros(0, dtype=torch.int64, device=dev)
+        self.send_splits = [a + b for a, b in zip(ps, rs_)]
+        self.recv_splits = [a + b for a, b in zip(pool_recv, raw_recv)]
+        self.n_recv = sum(self.recv_splits)
+        # positions (in the received rows) of the pooled rows and of the raw children
+        pool_pos, raw_pos, off = [], [], 0
+        for a, b in zip(pool_recv, raw_recv):
+            pool_pos.append(torch.arange(off, off + a, device=dev))
+            raw_pos.append(torch.arange(off + a, off + a + b, device=dev))
+            off += a + b
+        pool_pos = torch.cat(pool_pos) if pool_pos else torch.zeros(0, dtype=torch.int64, device=dev)
+        raw_pos = torch.cat(raw_pos) if raw_pos else torch.zeros(0, dtype=torch.int64, device=dev)
+        self.recv_pool_pos = pool_pos
+        # segments of the parents pooled here for this rank: own children (complete or not) + raw children received
+        keep_idx = torch.nonzero(powner == rank).flatten()
+        cand_idx = torch.cat([keep_idx, n_own + raw_pos])
+        cand_codes = torch.cat([codes[keep_idx], got_c])
+        srt = torch.argsort(cand_codes, stable=True)                     # children in code order
         self.seg_idx = cand_idx[srt].to(torch.int32).contiguous()
-        pc, cnt = torch.unique_consecutive(codes >> 3, return_counts=True)
-        if not torch.equal(pc, next_level.codes):
+        seg_p, seg_cnt = torch.unique_consecutive(cand_codes[srt] >> 3, return_counts=True)
+        self.n_seg = int(seg_p.numel())
+        self.seg_off = torch.zeros(self.n_seg + 1, dtype=torch.int32, device=dev)
+        self.seg_off[1:] = torch.cumsum(seg_cnt, 0).to(torch.int32)
+        self.n_parents = int(next_level.codes.numel())
+        # where each pooled row lands among the owned parents
+        self.seg_out = torch.searchsorted(next_level.codes, seg_p)
+        self.recv_out = torch.searchsorted(next_level.codes, got_p)
+        allp = torch.sort(torch.cat([seg_p, got_p])).values
+        if not torch.equal(allp, next_level.codes):
             raise RuntimeError("pooled parents differ from the next level's owned voxels")
-        self.n_parents = int(pc.numel())
-        self.seg_off = torch.zeros(self.n_parents + 1, dtype=torch.int32, device=codes.device)
-        self.seg_off[1:] = torch.cumsum(cnt, 0).to(torch.int32)
+        self.identity = self.n_seg == self.n_parents and not got_p.numel()
 
     def buffer(self, C: int, device) -> torch.Tensor:
         """[n_own + n_recv, C] fp32: the owned rows, then the rows other ranks send."""
@@ -609,17 +667,31 @@ class PoolPlan:
 
     def apply(self, buf: torch.Tensor) -> torch.Tensor:
         """Pool `buf` (owned rows written by the caller) into the owned parents' means [n_parents, C] fp32."""
-        from . import ops
         import torch.distributed as dist
-        world, _ = _world(self.group)
-        if world > 1 and (sum(self.send_splits) or self.n_recv):
-            send = buf[:self.n_own].index_select(0, self.send_idx)
+        if self.world > 1:                  # every rank enters the all-to-all, also with nothing to move
+            own = buf[:self.n_own]
+            pooled = _pool(own, self.pool_seg_idx, self.pool_seg_off, self.n_pool_send)
+            send = torch.cat([pooled, own.index_select(0, self.raw_send_idx)]).index_select(0, self.send_perm)
             dist.all_to_all_single(buf[self.n_own:], send, self.recv_splits, self.send_splits, group=self.group)
-        if buf.is_cuda:
-            return ops.pool_mean(buf, self.seg_idx, self.seg_off, self.n_parents)
-        rows = buf[self.seg_idx.long()]
-        return torch.stack([_mean_in_order(rows[int(a):int(b)]) for a, b in zip(self.seg_off[:-1], self.seg_off[1:])]) \
-            if self.n_parents else buf[:0]
+        rows = _pool(buf, self.seg_idx, self.seg_off, self.n_seg)
+        if self.identity:
+            return rows
+        out = torch.empty((self.n_parents, buf.shape[1]), dtype=buf.dtype, device=buf.device)
+        out.index_copy_(0, self.seg_out, rows)
+        if self.recv_pool_pos.numel():
+            out.index_copy_(0, self.recv_out, buf[self.n_own:].index_select(0, self.recv_pool_pos))
+        return out
+
+
+def _pool(buf: torch.Tensor, seg_idx: torch.Tensor, seg_off: torch.Tensor, n: int) -> torch.Tensor:
+    """Mean of every segment's rows of `buf`, summed in segment order (the pooling kernel on the GPU)."""
+    from . import ops
+    if n == 0:
+        return buf[:0]
+    if buf.is_cuda:
+        return ops.pool_mean(buf, seg_idx, seg_off, n)
+    rows = buf[seg_idx.long()]
+    return torch.stack([_mean_in_order(rows[int(a):int(b)]) for a, b in zip(seg_off[:-1], seg_off[1:])])
 
 
 def _mean_in_order(rows: torch.Tensor) -> torch.Tensor:
@@ -630,18 +702,44 @@ def _mean_in_order(rows: torch.Tensor) -> torch.Tensor:
     return acc / torch.tensor(float(rows.shape[0]), dtype=torch.float32)
 
 
-def build_levels(local_codes: torch.Tensor, levels: int, nmap_fn, group=None) -> list:
+# Relative cost of one voxel at each level of the sharded encoder (two convs, the pool into it and its link; measured
+# per voxel on one B200 with Model A's widths), used to balance the aligned ranges.
+LEVEL_COST = (0.68, 1.05, 2.09, 5.8, 7.1)
+
+
+def _level0_weights(codes: torch.Tensor, levels: int, cost=LEVEL_COST) -> torch.Tensor:
+    """Per level-0 voxel (sorted unique codes): its own cost plus, at every coarser level, its ancestor's cost shared
+    among the ancestor's level-0 descendants on this rank."""
+    w = torch.full(codes.shape, float(cost[0]), dtype=torch.float64, device=codes.device)
+    for k in range(1, levels):
+        _, inv, cnt = torch.unique_consecutive(codes >> (3 * k), return_inverse=True, return_counts=True)
+        w += float(cost[min(k, len(cost) - 1)]) / cnt[inv].to(torch.float64)
+    return w
+
+
+def build_levels(local_codes: torch.Tensor, levels: int, nmap_fn, group=None, aligned: bool = False) -> list:
     """Every level of a fused scene sharded by Morton ranges, from this rank's own back-projected codes.  Level 0:
-    codes to the owners of sample-balanced ranges, then once more to ranges balanced on the now unique owned voxels;
-    each coarser level: the parents (code >> 3) of the level below, balanced on their own counts and sent to their
-    owners.  Every level's ranges are balanced by that level's voxel count.  Returns [LevelShard] per level."""
+    codes to the owners of sample-balanced ranges, then once more to final ranges; each coarser level: the parents
+    (code >> 3) of the level below, sent to their owners.
+    By default every level's ranges are balanced by that level's own voxel count; a parent whose children sit on
+    another rank is pooled there and only its pooled row moves (PoolPlan).  aligned: the coarser levels' ranges are
+    the level-0 boundaries' parent codes (boundary >> 3 per level), so a parent's children all sit on its rank except
+    at the one parent straddling a boundary and the pool moves almost nothing, with the level-0 ranges cut to balance
+    the whole encoder's work (LEVEL_COST per voxel and level) -- each level then carries its own imbalance, which
+    measured slightly slower at 2 GPUs (11.19 vs 11.01 ms per step).  Returns [LevelShard] per level."""
     owned = distribute_codes(local_codes, morton_splitters(local_codes, group), group)
-    splitters = morton_splitters(owned, group)
+    weights = _level0_weights(owned, levels) if aligned else None
+    splitters = morton_splitters(owned, group, weights=weights)
     owned = distribute_codes(owned, splitters, group)
     lv = [LevelShard(owned, splitters, nmap_fn, group)]
-    for _ in range(1, levels):
+    s0 = splitters
+    for k in range(1, levels):
         cand = torch.unique(lv[-1].codes >> 3)
-        splitters = morton_splitters(cand, group)
+        if aligned:
+            splitters = s0.clone()
+            splitters[1:-1] = s0[1:-1] >> (3 * k)
+        else:
+            splitters = morton_splitters(cand, group)
         lv.append(LevelShard(distribute_codes(cand, splitters, group), splitters, nmap_fn, group))
     return lv
 

@@ -51,8 +51,8 @@ def link_cpu(pooled, layer):
     return torch.from_numpy(np.clip(np.rint(oref.silu(y) / np.float32(s_out)), -127, 127).astype(np.int8))
 
 
-def _run(local_codes, group, overlap=False):
-    levels = fused.build_levels(local_codes, len(WIDTHS), nmap_cpu, group)
+def _run(local_codes, group, overlap=False, aligned=False):
+    levels = fused.build_levels(local_codes, len(WIDTHS), nmap_cpu, group, aligned=aligned)
     convs, links = fused.encoder_layers(WIDTHS, 2, seed=9, device="cpu")
     rng = np.random.default_rng(17)
     n0 = levels[0].offset
@@ -61,6 +61,10 @@ def _run(local_codes, group, overlap=False):
     q0 = g_all[n0:n0 + levels[0].plan.n_own]
     outs = fused.encoder_forward(levels, q0, convs, links, conv_cpu, link_cpu, group, overlap=overlap)
     return levels, outs
+
+
+def fused_pools(levels):
+    return [fused.PoolPlan(levels[k], levels[k + 1], None) for k in range(len(levels) - 1)]
 
 
 def _free_port():
@@ -78,9 +82,15 @@ def _worker(rank, world, port, q):
         levels, outs = _run(_codes(range(b, e)), None)
         _, plain = _run(_codes(range(b, e)), None, overlap=True)      # exchanges beside the interior rows' conv
         assert all(torch.equal(a, p) for a, p in zip(outs, plain))
+        # every level balanced on its own count (the default run above): parents of whole child groups pooled where
+        # the children are; the aligned ranges (coarser levels cut at the parents of level 0's boundaries) as well
+        lv_b = levels
+        _, outs_b = _run(_codes(range(b, e)), None, aligned=True)
+        n_pooled = sum(pp.n_pool_send for pp in fused_pools(lv_b))
         # numpy arrays travel by value: shared-memory tensors would need this process alive while the parent reads
         q.put((rank, [l.codes.numpy() for l in levels], [l.offset for l in levels], [o.numpy() for o in outs],
-               [l.plan.n_halo for l in levels], [l.plan.n_int for l in levels]))
+               [l.plan.n_halo for l in levels], [l.plan.n_int for l in levels], [o.numpy() for o in outs_b],
+               n_pooled))
     finally:
         dist.destroy_process_group()
 
@@ -97,8 +107,8 @@ def test_sharded_levels_and_encoder_equal_single_rank(world):
     for p in procs:
         p.start()
     res = sorted((q.get(timeout=300) for _ in range(world)), key=lambda r: r[0])
-    res = [(r[0], [torch.from_numpy(c) for c in r[1]], r[2], [torch.from_numpy(o) for o in r[3]], r[4], r[5])
-           for r in res]
+    res = [(r[0], [torch.from_numpy(c) for c in r[1]], r[2], [torch.from_numpy(o) for o in r[3]], r[4], r[5],
+            [torch.from_numpy(o) for o in r[6]], r[7]) for r in res]
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -110,6 +120,9 @@ def test_sharded_levels_and_encoder_equal_single_rank(world):
         assert [r[2][k] for r in res] == list(np.cumsum([0] + [r[1][k].numel() for r in res])[:-1])
         out = torch.cat([r[3][k] for r in res])
         assert torch.equal(out, ref_outs[k]), k
+        # per-level balanced ranges (pooled rows and boundary children move between ranks): the same outputs
+        assert torch.equal(torch.cat([r[6][k] for r in res]), ref_outs[k]), k
+    assert sum(r[7] for r in res) > 0                          # some parents were pooled on another rank than theirs
 
 
 def test_single_rank_levels_are_the_global_structure():
