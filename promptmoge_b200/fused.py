@@ -353,7 +353,8 @@ class ShardPlan:
         work.wait()
         if self.n_own - self.n_int:
             parts.append(conv(buf, self.nmap_bnd, self.mask_bnd, layer))
-        buf[:self.n_own].index_copy_(0, self.perm, torch.cat(parts) if len(parts) > 1 else parts[0])
+        if parts:                          # a rank may own no voxel of a level (it still took part in the exchange)
+            buf[:self.n_own].index_copy_(0, self.perm, torch.cat(parts) if len(parts) > 1 else parts[0])
 
     def halo_bytes(self, C: int) -> int:
         """int8 bytes this rank receives per conv layer."""
@@ -399,6 +400,8 @@ def gpu_conv(q_local, nmap, mask, layer):
     """The product conv of a layer: tcgen05 int8 submanifold conv with the fused SiLU + requantise epilogue."""
     from . import ops
     w, ws, b, sa, s_out = layer
+    if nmap.shape[1] == 0:                 # no output rows (a rank that owns none of a level's voxels)
+        return torch.empty((0, w.shape[1]), dtype=torch.int8, device=q_local.device)
     return ops.spconv_i8(q_local, nmap, mask, w, ws, b, sa, ops.EPI_SILU_Q8, s_out, rows=nmap.shape[1])
 
 
@@ -812,5 +815,7 @@ def gpu_link(pooled: torch.Tensor, layer):
     int8 layer with the SiLU + requantise epilogue."""
     from . import ops
     w, ws, b, sa, s_out = layer
+    if pooled.shape[0] == 0:
+        return torch.empty((0, w.shape[0]), dtype=torch.int8, device=pooled.device)
     qp = ops.quantize(pooled.contiguous(), sa)
     return ops.dense_i8(qp, w, ws, b, sa, ops.EPI_SILU_Q8, s_out)
